@@ -1,0 +1,352 @@
+"""Benchmark: routed-expert decode tok/s through the 40-layer synthetic stack.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE config 3 at batch 1): 40 layers x 384 SwiGLU experts, hidden 7168,
+intermediate 1536, IQ2_XXS / IQ2_XS / IQ1_M drawn per (layer, expert) from the seed
+(~129.5 GB of packed weights resident in HBM), top-6 routing per layer from N(0,1)
+logits (uniformly random experts), x_{l+1} = x_l + combine_l. One step = one token
+through all 40 layers.
+
+  value  : tokens/s with inputs resident in HBM, CUDA events on the bank stream.
+  e2e    : tokens/s through clb_stack_decode (host x and logits in, host x out).
+  roofline: the gate/up kernel, timed alone with CUDA events right after the timed
+           region on the same kind of inputs; algorithmic bytes = packed gate+up
+           payload of the picked experts + Q8_K(x) in + h out.
+  cpu_baseline: crosslane's own CPU-lane arithmetic (q8k_core.hpp, built into
+           oracle/_ref/libref.so) on a persistent 64-row-job team over all host
+           threads, one token-layer sample, extrapolated to the 40-layer stack.
+
+With --gpus N (torchrun), every rank decodes its own token stream on its own full
+bank (independent replicas); value is the sum over ranks of tokens / the slowest
+rank's time.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+DIM, FF, EXPERTS, LAYERS, PICKS = 7168, 1536, 384, 40, 6
+SEED, POLICY = 20261201, 2
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "routed-expert decode tok/s (40-layer stack)"
+WORKLOAD = "BASELINE config 3: 40-layer routed-expert stack, batch-1 decode"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(rng, n):
+    xs = rng.standard_normal((n, DIM)).astype(np.float32)
+    logits = rng.standard_normal((n, LAYERS, EXPERTS)).astype(np.float32)
+    return xs, logits
+
+
+def cpu_baseline(samples=1, threads=0):
+    """Reference CPU lane (oracle/_ref: crosslane q8k_core.hpp) on one token-layer."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib
+    ref = oracle_lib.reference()
+    if ref is None:
+        return None
+    orc = oracle_lib.Oracle()
+    rng = np.random.default_rng(99)
+    times = []
+    cores = None
+    for s in range(samples + 1):  # first sample warms the team and page cache
+        layer = s % LAYERS
+        ids, w = orc.route_sigmoid(rng.standard_normal(EXPERTS).astype(np.float32), PICKS)
+        x = rng.standard_normal(DIM).astype(np.float32)
+        mats = []
+        for e in ids:
+            t = orc.expert_type(POLICY, SEED, layer, int(e))
+            mats.append((t, orc.synth_matrix(t, SEED, layer, int(e), 0, FF, DIM),
+                         orc.synth_matrix(t, SEED, layer, int(e), 1, FF, DIM),
+                         orc.synth_matrix(t, SEED, layer, int(e), 2, DIM, FF)))
+        t0 = time.perf_counter()
+        rows = np.stack([ref.expert(t, g, u, d, x, DIM, FF, 0.0, threads)[1] for t, g, u, d in mats])
+        ref.combine(ids, w, rows)
+        dt = time.perf_counter() - t0
+        if s > 0:
+            times.append(dt)
+        cores = ref.L.ref_team_threads(threads)
+    per_layer = statistics.median(times)
+    return {"value": 1.0 / (per_layer * LAYERS), "unit": "tok/s", "cores": int(cores), "kind": "reference",
+            "sample": f"{samples} token-layer(s) of config 3 (6 experts each, weights generated in RAM, "
+                      f"0 store readers), median {per_layer * 1e3:.1f} ms per token-layer x {LAYERS} layers; "
+                      f"crosslane q8k_core.hpp arithmetic, persistent 64-row-job team"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    samples = max(1, args.steps)
+    res = cpu_baseline(samples=samples)
+    if res is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref.so (crosslane q8k_core.hpp) "
+                                                              "was not built on this machine"}))
+        return
+    line = {"metric": METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 / res["value"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8xIQ/fp32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": EXPERTS, "dim": DIM, "ff": FF,
+                       "picks": PICKS, "types": "IQ2_XXS/IQ2_XS/IQ1_M per (layer, expert)", "batch": 1},
+            "impl": "reference", "cpu_baseline": res,
+            "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS, help="smaller stacks for quick checks only")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+
+    import crosslane_b200 as cb
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    L = args.layers
+    bank = cb.ExpertBank(n_layers=L, n_experts=EXPERTS, dim=DIM, ff=FF, max_picks=PICKS, device=local)
+    t0 = time.time()
+    bank.fill_synthetic(SEED, POLICY)
+    fill_s = time.time() - t0
+    stream = torch.cuda.ExternalStream(bank.stream)
+
+    rng = np.random.default_rng(1000 + rank)
+    n_in = args.warmup + args.steps
+    xs, logits = make_inputs(rng, n_in)
+    logits = logits[:, :L]
+    d_xs = torch.from_numpy(xs).cuda()
+    d_logits_all = torch.from_numpy(np.ascontiguousarray(logits)).cuda()
+    d_x = torch.empty(DIM, dtype=torch.float32, device="cuda")
+    d_lg = torch.empty((L, EXPERTS), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def step(i):
+        with torch.cuda.stream(stream):
+            d_x.copy_(d_xs[i], non_blocking=True)
+            d_lg.copy_(d_logits_all[i], non_blocking=True)
+        bank.stack_decode_device(0, L, d_x, d_lg)
+
+    for i in range(args.warmup):
+        step(i)
+    bank.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    ms_per_step = ms / args.steps
+    value = world * args.steps / (ms / 1e3)
+
+    # ---- e2e through the host-buffer C ABI call (copies inside the timed region) ----
+    hx = np.ascontiguousarray(xs)
+    hl = np.ascontiguousarray(logits)
+    for i in range(args.warmup):
+        bank.stack_decode(0, L, hx[i], hl[i])
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        bank.stack_decode(0, L, hx[args.warmup + i], hl[args.warmup + i])
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": world * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * DIM + 4 * L * EXPERTS,
+           "d2h_bytes_per_step": 4 * DIM}
+
+    # ---- roofline pass: the gate/up kernel alone, events around each launch ----
+    peak, peak_kind = peaks()
+    d_ids = torch.empty(PICKS, dtype=torch.int32, device="cuda")
+    d_w = torch.empty(PICKS, dtype=torch.float32, device="cuda")
+    d_out = torch.empty(DIM, dtype=torch.float32, device="cuda")
+    gu_bytes, gu_ms, dn_bytes, dn_ms = 0, 0.0, 0, 0.0
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    launches_timed = 0
+    for tok in range(min(args.steps, 8)):
+        for layer in range(L):
+            ids, w = cb.route_host(0, logits[tok, layer], PICKS)
+            with torch.cuda.stream(stream):
+                d_ids.copy_(torch.from_numpy(ids), non_blocking=False)
+                d_w.copy_(torch.from_numpy(w), non_blocking=False)
+                d_x.copy_(d_xs[tok])
+            bank.layer_phases_device(layer, d_ids, d_w, d_x, d_out, 1, stream=bank.stream)
+            evs[0].record(stream)
+            bank.layer_phases_device(layer, d_ids, d_w, d_x, d_out, 2, stream=bank.stream)
+            evs[1].record(stream)
+            bank.layer_phases_device(layer, d_ids, d_w, d_x, d_out, 4, stream=bank.stream)
+            evs[2].record(stream)
+            bank.layer_phases_device(layer, d_ids, d_w, d_x, d_out, 8, stream=bank.stream)
+            evs[3].record(stream)
+            evs[3].synchronize()
+            gu_ms += evs[0].elapsed_time(evs[1])
+            dn_ms += evs[2].elapsed_time(evs[3])
+            launches_timed += 1
+            for e in ids:
+                t, payload = bank.expert_info(layer, int(e))
+                per = payload // 3  # gate, up and down carry the same number of weights
+                gu_bytes += 2 * per
+                dn_bytes += per
+            gu_bytes += DIM + 4 * (DIM // 256) + 4 * PICKS * FF
+            dn_bytes += PICKS * FF + 4 * PICKS * (FF // 256) + 4 * DIM
+    gu_avg_s = gu_ms / 1e3 / launches_timed
+    gu_achieved = gu_bytes / launches_timed / gu_avg_s / 1e9
+    dn_achieved = dn_bytes / launches_timed / (dn_ms / 1e3 / launches_timed) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "k_gateup_traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get("bytes_per_launch")
+    roofline = {"bound": "hbm", "achieved": round(gu_achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(gu_achieved / peak, 4), "traffic": traffic, "kernel": "clb::k_gateup",
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6650 GB/s",
+                "algorithmic_bytes_per_launch": int(gu_bytes / launches_timed),
+                "avg_launch_us": round(gu_avg_s * 1e6, 2),
+                "down_combine_achieved_gbs": round(dn_achieved, 1)}
+
+    # whole-step effective bandwidth (algorithmic bytes per token / time per token)
+    step_bytes = 0
+    for layer in range(L):
+        ids, _ = cb.route_host(0, logits[args.warmup, layer], PICKS)
+        step_bytes += sum(bank.expert_info(layer, int(e))[1] for e in ids) + 8 * DIM
+    step_gbs = step_bytes / (ms_per_step / 1e3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(samples=2)
+
+    clk = clocks.summary()
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8xIQ/fp32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "layers": L, "experts": EXPERTS, "dim": DIM, "ff": FF, "picks": PICKS,
+                   "types": "IQ2_XXS/IQ2_XS/IQ1_M per (layer, expert), seed-drawn", "batch": 1,
+                   "routing": "top-6 by sigmoid of N(0,1) logits, renormalised",
+                   "parallelism": f"replica x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2: each token streams ~2 GB of distinct expert weights",
+                   "bank_gb": round(bank.weight_bytes / 1e9, 2), "fill_s": round(fill_s, 1)},
+        "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in e2e.items()},
+        "roofline": roofline,
+        "step_hbm_gbs": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
+        "cpu_baseline": cpu,
+        "clocks": clk,
+        "gpu_launches": (1 + 4 * L) * args.steps,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    bank.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

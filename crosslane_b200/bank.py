@@ -1,0 +1,240 @@
+"""Python face of the CUDA expert lane.
+
+`ExpertBank` mirrors crosslane's expert-lane interface `WarmRedirect`
+(engine/strata/warm/runtime.hpp:10-16): warm_contains / warm_grouped / warm_compute /
+warm_compute_many, plus `warm_execute` (engine/strata/warm/runtime.cpp:121-189) with a
+host lane for non-resident experts. Every call goes through the C ABI in
+include/crosslane_b200.h; host arrays are numpy float32, device arrays torch tensors.
+"""
+import ctypes as C
+
+import numpy as np
+
+from . import _capi
+from ._capi import BankConfigV1, ErrorV1, HOST_EXPERT_FN, check, lib
+
+IQ2_XXS, IQ2_XS, IQ1_M = 16, 17, 29
+BLOCK_BYTES = {IQ2_XXS: 66, IQ2_XS: 74, IQ1_M: 56}
+ROLE_GATE, ROLE_UP, ROLE_DOWN = 0, 1, 2
+Q8K_BLOCK_BYTES = 292
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    return C.c_void_p(stream)
+
+
+class ExpertBank:
+    """A resident bank of routed experts on one GPU (the CUDA lane)."""
+
+    def __init__(self, *, n_layers: int, n_experts: int, dim: int, ff: int, max_picks: int = 6,
+                 limit: float = 0.0, device: int = 0, expert_begin: int = 0, expert_end: int = 0):
+        cfg = BankConfigV1(device=device, n_layers=n_layers, n_experts=n_experts, dim=dim, ff=ff,
+                           max_picks=max_picks, limit=limit, expert_begin=expert_begin, expert_end=expert_end)
+        err = ErrorV1()
+        h = C.c_void_p()
+        check(lib.clb_bank_create(C.byref(cfg), C.byref(h), C.byref(err)), err)
+        self._h = h
+        self.n_layers, self.n_experts, self.dim, self.ff = n_layers, n_experts, dim, ff
+        self.max_picks, self.limit, self.device = max_picks, limit, device
+        self.expert_begin = expert_begin
+        self.expert_end = expert_end or n_experts
+
+    # -- lifetime --
+    def close(self):
+        if getattr(self, "_h", None):
+            lib.clb_bank_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # -- loading --
+    def fill_synthetic(self, seed: int, type_policy: int) -> None:
+        err = ErrorV1()
+        check(lib.clb_bank_fill_synthetic(self._h, C.c_uint64(seed), type_policy, C.byref(err)), err)
+
+    def load_matrix(self, layer: int, expert: int, role: int, qtype: int, ggml: np.ndarray) -> None:
+        buf = np.ascontiguousarray(ggml, dtype=np.uint8)
+        err = ErrorV1()
+        check(lib.clb_bank_load_matrix(self._h, layer, expert, role, qtype, _ptr(buf), buf.nbytes, C.byref(err)), err)
+
+    @property
+    def weight_bytes(self) -> int:
+        return int(lib.clb_bank_weight_bytes(self._h))
+
+    @property
+    def stream(self) -> int:
+        return int(lib.clb_bank_stream(self._h) or 0)
+
+    def synchronize(self) -> None:
+        err = ErrorV1()
+        check(lib.clb_bank_synchronize(self._h, C.byref(err)), err)
+
+    # -- WarmRedirect --
+    def warm_grouped(self) -> bool:
+        return True
+
+    def warm_contains(self, layer: int, expert: int) -> bool:
+        return bool(lib.clb_bank_contains(self._h, layer, expert))
+
+    def warm_compute(self, layer: int, expert: int, x) -> np.ndarray:
+        x = _f32(x)
+        y = np.empty(self.dim, np.float32)
+        err = ErrorV1()
+        check(lib.clb_bank_compute(self._h, layer, expert, _ptr(x), _ptr(y), C.byref(err)), err)
+        return y
+
+    def warm_compute_many(self, layer: int, ids, x) -> np.ndarray:
+        ids = _i32(ids)
+        x = _f32(x)
+        y = np.empty((len(ids), self.dim), np.float32)
+        err = ErrorV1()
+        check(lib.clb_bank_compute_many(self._h, layer, _ptr(ids), len(ids), _ptr(x), _ptr(y), C.byref(err)), err)
+        return y
+
+    # -- layer / stack --
+    def layer_execute(self, layer: int, ids, w, x, shared=None) -> np.ndarray:
+        ids, w, x = _i32(ids), _f32(w), _f32(x)
+        sh = _f32(shared) if shared is not None else None
+        out = np.empty(self.dim, np.float32)
+        err = ErrorV1()
+        check(lib.clb_layer_execute(self._h, layer, _ptr(ids), _ptr(w), len(ids), _ptr(x),
+                                    _ptr(sh) if sh is not None else None, _ptr(out), C.byref(err)), err)
+        return out
+
+    def warm_execute(self, layer: int, ids, w, x, shared=None, host_lane=None) -> np.ndarray:
+        """host_lane(layer, expert, x: np.ndarray) -> np.ndarray[dim] for non-resident picks."""
+        ids, w, x = _i32(ids), _f32(w), _f32(x)
+        sh = _f32(shared) if shared is not None else None
+        out = np.empty(self.dim, np.float32)
+        dim = self.dim
+
+        def trampoline(_ctx, layer_, expert, xp, n, yp):
+            try:
+                xv = np.ctypeslib.as_array(xp, shape=(n,)).copy()
+                y = np.asarray(host_lane(layer_, expert, xv), dtype=np.float32)
+                if y.shape != (dim,):
+                    return 1
+                C.memmove(yp, y.ctypes.data, 4 * dim)
+                return 0
+            except Exception:
+                return 1
+
+        cb = HOST_EXPERT_FN(trampoline) if host_lane is not None else HOST_EXPERT_FN()
+        err = ErrorV1()
+        check(lib.clb_warm_execute(self._h, layer, _ptr(ids), _ptr(w), len(ids), _ptr(x),
+                                   _ptr(sh) if sh is not None else None, cb, None, _ptr(out), C.byref(err)), err)
+        return out
+
+    def stack_decode(self, first_layer: int, n_layers: int, x, logits) -> np.ndarray:
+        x = _f32(x)
+        logits = _f32(logits)
+        assert logits.shape == (n_layers, self.n_experts)
+        out = np.empty(self.dim, np.float32)
+        err = ErrorV1()
+        check(lib.clb_stack_decode(self._h, first_layer, n_layers, _ptr(x), _ptr(logits), _ptr(out), C.byref(err)),
+              err)
+        return out
+
+    def stack_decode_device(self, first_layer: int, n_layers: int, d_x, d_logits) -> None:
+        """d_x: torch float32 [dim] on this device, updated in place on the bank stream."""
+        err = ErrorV1()
+        check(lib.clb_stack_decode_device(self._h, first_layer, n_layers, C.c_void_p(d_x.data_ptr()),
+                                          C.c_void_p(d_logits.data_ptr()), C.byref(err)), err)
+
+    def layer_phases_device(self, layer: int, d_ids, d_w, d_x, d_out, phase_mask: int, stream=None) -> None:
+        err = ErrorV1()
+        check(lib.clb_layer_phases_device(
+            self._h, layer, C.c_void_p(d_ids.data_ptr()), C.c_void_p(d_w.data_ptr()), d_ids.numel(),
+            C.c_void_p(d_x.data_ptr()), C.c_void_p(d_out.data_ptr()), phase_mask,
+            C.c_void_p(stream) if stream else None, C.byref(err)), err)
+
+    def expert_info(self, layer: int, expert: int):
+        """(ggml type id, payload bytes of gate+up+down) of a resident expert."""
+        t = C.c_int32()
+        b = C.c_uint64()
+        check(lib.clb_bank_expert_info(self._h, layer, expert, C.byref(t), C.byref(b)), what="not resident")
+        return int(t.value), int(b.value)
+
+    def layer_forward_device(self, layer: int, d_ids, d_w, d_x, d_out, d_shared=None, d_resid=None,
+                             stream=None) -> None:
+        err = ErrorV1()
+        check(lib.clb_layer_forward_device(
+            self._h, layer, C.c_void_p(d_ids.data_ptr()), C.c_void_p(d_w.data_ptr()), d_ids.numel(),
+            C.c_void_p(d_x.data_ptr()), C.c_void_p(d_shared.data_ptr()) if d_shared is not None else None,
+            C.c_void_p(d_resid.data_ptr()) if d_resid is not None else None, C.c_void_p(d_out.data_ptr()),
+            C.c_void_p(stream) if stream else None, C.byref(err)), err)
+
+
+# -- stateless primitives ------------------------------------------------------------
+
+def packed_bytes(qtype: int, n: int, k: int) -> int:
+    return int(lib.clb_packed_bytes(qtype, n, k))
+
+
+def pack(qtype: int, n: int, k: int, ggml: np.ndarray) -> np.ndarray:
+    src = np.ascontiguousarray(ggml, dtype=np.uint8)
+    out = np.zeros(packed_bytes(qtype, n, k), np.uint8)
+    check(lib.clb_pack(qtype, n, k, _ptr(src), src.nbytes, _ptr(out), out.nbytes), what="clb_pack")
+    return out
+
+
+def unpack(qtype: int, n: int, k: int, packed: np.ndarray) -> np.ndarray:
+    src = np.ascontiguousarray(packed, dtype=np.uint8)
+    out = np.zeros(n * (k // 256) * BLOCK_BYTES[qtype], np.uint8)
+    check(lib.clb_unpack(qtype, n, k, _ptr(src), src.nbytes, _ptr(out), out.nbytes), what="clb_unpack")
+    return out
+
+
+def route_host(mode: int, logits, k: int, bias=None, scale: float = 1.0):
+    logits = _f32(logits)
+    b = _f32(bias) if bias is not None else None
+    ids = np.empty(k, np.int32)
+    w = np.empty(k, np.float32)
+    check(lib.clb_route_host(mode, _ptr(logits), _ptr(b) if b is not None else None, logits.size, k, scale,
+                             _ptr(ids), _ptr(w)), what="clb_route_host")
+    return ids, w
+
+
+def q8k_quantize(d_x, d_q, stream=None) -> None:
+    check(lib.clb_q8k_quantize(C.c_void_p(d_x.data_ptr()), C.c_void_p(d_q.data_ptr()), d_x.numel(),
+                               _stream(stream)), what="clb_q8k_quantize")
+
+
+def q8k_mv(qtype: int, d_w, d_q, d_y, n: int, k: int, stream=None) -> None:
+    check(lib.clb_q8k_mv(qtype, C.c_void_p(d_w.data_ptr()), C.c_void_p(d_q.data_ptr()), C.c_void_p(d_y.data_ptr()),
+                         n, k, _stream(stream)), what="clb_q8k_mv")
+
+
+def q8k_activate(d_g, d_u, d_h, limit: float = 0.0, stream=None) -> None:
+    check(lib.clb_q8k_activate(C.c_void_p(d_g.data_ptr()), C.c_void_p(d_u.data_ptr()), C.c_void_p(d_h.data_ptr()),
+                               d_g.numel(), limit, _stream(stream)), what="clb_q8k_activate")
+
+
+def route_device(d_logits, n_experts: int, k: int, tokens: int, d_ids, d_w, stream=None) -> None:
+    check(lib.clb_route_device(0, C.c_void_p(d_logits.data_ptr()), n_experts, k, tokens, C.c_void_p(d_ids.data_ptr()),
+                               C.c_void_p(d_w.data_ptr()), _stream(stream)), what="clb_route_device")

@@ -1,0 +1,865 @@
+// Host side of the CUDA expert lane: bank, workspace, launches and the C ABI
+// declared in include/crosslane_b200.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <map>
+#include <mutex>
+#include <set>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <utility>
+#include <vector>
+
+#include "../../include/crosslane_b200.h"
+#include "clb_kernels.h"
+#include "clb_pack.h"
+#include "scale_table.h"
+
+namespace {
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+void require(bool ok, int code, const char* fmt, ...) {
+    if (ok) return;
+    char buf[480];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    throw Error(code, buf);
+}
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw Error(CLB_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int fail(clb_error_v1* err, int code, const char* msg) {
+    if (err) {
+        err->code = code;
+        std::snprintf(err->message, sizeof err->message, "%s", msg);
+    }
+    return code;
+}
+
+template <class F>
+int guarded(clb_error_v1* err, F&& f) {
+    try {
+        f();
+        if (err) {
+            err->code = CLB_OK;
+            err->message[0] = 0;
+        }
+        return CLB_OK;
+    } catch (const Error& e) {
+        return fail(err, e.code, e.what());
+    } catch (const std::bad_alloc&) {
+        return fail(err, CLB_E_NOMEM, "host allocation failed");
+    } catch (const std::exception& e) {
+        return fail(err, CLB_E_INVALID, e.what());
+    }
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cuda_check(cudaSetDevice(dev), "cudaSetDevice");
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+std::once_flag g_scale_once;
+uint16_t g_scale_host[65536];
+
+// Per-device one-time state: nibble tables uploaded and kernel attributes set.
+std::mutex g_dev_mutex;
+std::set<int> g_dev_ready;
+void ensure_device_ready(int dev, cudaStream_t s) {
+    std::lock_guard<std::mutex> l(g_dev_mutex);
+    if (g_dev_ready.count(dev)) return;
+    cuda_check(clb::upload_tables(s), "upload codebook tables");
+    cuda_check(clb::set_smem_limits(), "kernel shared-memory limits");
+    g_dev_ready.insert(dev);
+}
+
+bool finite_all(const float* v, size_t n) {
+    for (size_t i = 0; i < n; ++i)
+        if (!std::isfinite(v[i])) return false;
+    return true;
+}
+
+}  // namespace
+
+struct clb_bank {
+    clb_bank_config_v1 cfg{};
+    cudaStream_t stream = nullptr;
+    bool poisoned = false;
+    std::mutex call_mutex;  // one caller at a time (crosslane's WarmWorker guarantee)
+
+    std::vector<void*> allocations;
+    uint64_t weight_bytes = 0;
+    std::vector<clb::ExpertDesc> desc;  // [layer][expert]
+    std::vector<uint8_t> resident;
+    clb::ExpertDesc* d_desc = nullptr;
+    uint16_t* d_scales = nullptr;
+
+    // fixed workspace
+    float *d_x = nullptr, *d_out = nullptr, *d_shared = nullptr, *d_h = nullptr, *d_yrows = nullptr, *d_w = nullptr;
+    int8_t *d_xqs = nullptr, *d_hqs = nullptr;
+    float *d_xd = nullptr, *d_hd = nullptr;
+    int* d_ids = nullptr;
+    int* d_err = nullptr;
+    float* d_logits = nullptr;
+    int* d_route_ids = nullptr;
+    float* d_route_w = nullptr;
+    float *h_x = nullptr, *h_out = nullptr, *h_logits = nullptr, *h_yrows = nullptr;
+    std::map<std::pair<uint32_t, int>, cudaGraphExec_t> graphs, device_graphs;
+    const float* graph_dx = nullptr;
+
+    size_t L() const { return (size_t)cfg.n_layers; }
+    size_t E() const { return (size_t)cfg.n_experts; }
+    bool owns(int e) const { return e >= cfg.expert_begin && e < cfg.expert_end; }
+
+    template <class T>
+    T* dev_alloc(size_t count) {
+        void* p = nullptr;
+        cudaError_t e = cudaMalloc(&p, std::max<size_t>(count * sizeof(T), 256));
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            throw Error(CLB_E_NOMEM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+        }
+        allocations.push_back(p);
+        return static_cast<T*>(p);
+    }
+    template <class T>
+    T* host_alloc(size_t count) {
+        void* p = nullptr;
+        cuda_check(cudaMallocHost(&p, std::max<size_t>(count * sizeof(T), 256)), "cudaMallocHost");
+        host_allocations.push_back(p);
+        return static_cast<T*>(p);
+    }
+    std::vector<void*> host_allocations;
+
+    void check_usable() { require(!poisoned, CLB_E_STATE, "bank poisoned by an earlier device failure"); }
+
+    // Runs f; on a device failure the bank is poisoned (abi_backend_plugin.cpp:31-39 convention).
+    template <class F>
+    void device_step(F&& f) {
+        try {
+            f();
+        } catch (const Error& e) {
+            if (e.code == CLB_E_CUDA) poisoned = true;
+            throw;
+        }
+    }
+
+    void check_err_flag() {
+        int flag = 0;
+        cuda_check(cudaMemcpyAsync(&flag, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream), "error flag D2H");
+        cuda_check(cudaStreamSynchronize(stream), "stream sync");
+        if (flag) {
+            cuda_check(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "error flag reset");
+            throw Error(CLB_E_INVALID, "a picked expert is not resident or has a mismatched shape");
+        }
+    }
+
+    void validate_ids(uint32_t layer, const int32_t* ids, int n, bool need_resident) {
+        require(layer < (uint32_t)cfg.n_layers, CLB_E_INVALID, "layer %u out of range", layer);
+        require(n >= 1 && n <= cfg.max_picks, CLB_E_INVALID, "pick count %d outside [1, %d]", n, cfg.max_picks);
+        std::set<int> seen;
+        for (int i = 0; i < n; ++i) {
+            require(ids[i] >= 0 && ids[i] < cfg.n_experts, CLB_E_INVALID, "expert id %d out of range", ids[i]);
+            require(seen.insert(ids[i]).second, CLB_E_INVALID, "duplicate expert id %d", ids[i]);
+            if (need_resident)
+                require(resident[(size_t)layer * E() + (size_t)ids[i]], CLB_E_INVALID,
+                        "expert (%u, %d) is not resident in this bank", layer, ids[i]);
+        }
+    }
+
+    // norm: the stack's pre-norm x = RMSNorm(h) is fused into the quantisation of x.
+    void enqueue_layer(uint32_t layer, const int* ids, const float* w, int n, const float* x, const float* shared,
+                       const float* resid, float* out, float* yrows, cudaStream_t s, bool norm = false) {
+        const int dim = cfg.dim, ff = cfg.ff;
+        const clb::ExpertDesc* ex = d_desc + (size_t)layer * E();
+        if (norm)
+            cuda_check(clb::launch_norm_quant(x, dim, d_xqs, d_xd, nullptr, s), "norm + quantize x");
+        else
+            cuda_check(clb::launch_quant(x, dim / 256, d_xqs, d_xd, s), "quantize x");
+        cuda_check(clb::launch_gateup(ex, ids, n, d_xqs, d_xd, dim, ff, cfg.limit, d_h, d_err, s), "gate/up");
+        cuda_check(clb::launch_quant(d_h, n * ff / 256, d_hqs, d_hd, s), "quantize h");
+        cuda_check(clb::launch_down_combine(ex, ids, w, n, d_hqs, d_hd, dim, ff, shared, resid, out, yrows, d_err, s),
+                   "down/combine");
+    }
+
+    void enqueue_phases(uint32_t layer, const int* ids, const float* w, int n, const float* x, float* out, int mask,
+                        cudaStream_t s) {
+        const int dim = cfg.dim, ff = cfg.ff;
+        const clb::ExpertDesc* ex = d_desc + (size_t)layer * E();
+        if (mask & 1) cuda_check(clb::launch_quant(x, dim / 256, d_xqs, d_xd, s), "quantize x");
+        if (mask & 2)
+            cuda_check(clb::launch_gateup(ex, ids, n, d_xqs, d_xd, dim, ff, cfg.limit, d_h, d_err, s), "gate/up");
+        if (mask & 4) cuda_check(clb::launch_quant(d_h, n * ff / 256, d_hqs, d_hd, s), "quantize h");
+        if (mask & 8)
+            cuda_check(clb::launch_down_combine(ex, ids, w, n, d_hqs, d_hd, dim, ff, nullptr, nullptr, out, nullptr,
+                                                d_err, s),
+                       "down/combine");
+    }
+
+    void enqueue_stack(uint32_t first, int nl, float* dx, const float* dlogits, cudaStream_t s) {
+        const int k = cfg.max_picks;
+        cuda_check(clb::launch_route_sigmoid(dlogits, cfg.n_experts, k, nl, d_route_ids, d_route_w, s), "route");
+        for (int i = 0; i < nl; ++i)
+            enqueue_layer(first + (uint32_t)i, d_route_ids + (size_t)i * k, d_route_w + (size_t)i * k, k, dx, nullptr,
+                          dx, dx, nullptr, s, true);
+    }
+
+    void set_matrix(uint32_t layer, int e, int role, int type, uint8_t* base) {
+        const int n = role == 2 ? cfg.dim : cfg.ff, k = role == 2 ? cfg.ff : cfg.dim;
+        const PackedLayout l = clb_packed_layout(type, n, k);
+        PackedMat m{};
+        m.body = base + l.body;
+        m.sc = base + l.sc;
+        m.d = reinterpret_cast<const uint16_t*>(base + l.d);
+        m.type = type;
+        m.n = n;
+        m.k = k;
+        auto& d = desc[(size_t)layer * E() + (size_t)e];
+        (role == 0 ? d.gate : role == 1 ? d.up : d.down) = m;
+    }
+
+    void refresh_resident(uint32_t layer, int e) {
+        const auto& d = desc[(size_t)layer * E() + (size_t)e];
+        resident[(size_t)layer * E() + (size_t)e] = d.gate.body && d.up.body && d.down.body;
+    }
+
+    void upload_desc() {
+        cuda_check(cudaMemcpyAsync(d_desc, desc.data(), desc.size() * sizeof(clb::ExpertDesc), cudaMemcpyHostToDevice,
+                                   stream),
+                   "descriptor upload");
+        cuda_check(cudaStreamSynchronize(stream), "descriptor sync");
+    }
+
+    ~clb_bank() {
+        for (auto& g : graphs) cudaGraphExecDestroy(g.second);
+        for (auto& g : device_graphs) cudaGraphExecDestroy(g.second);
+        for (void* p : allocations) cudaFree(p);
+        for (void* p : host_allocations) cudaFreeHost(p);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+extern "C" {
+
+int32_t clb_abi_version(void) { return CLB_ABI_VERSION; }
+
+// ---- Q8_K primitives ----
+size_t clb_q8k_activation_bytes(int32_t k) {
+    return (k > 0 && k % 256 == 0) ? (size_t)(k / 256) * clb::kQ8KBlockBytes : 0;
+}
+
+int32_t clb_q8k_quantize(const float* x, void* q, int32_t k, void* stream) {
+    if (!x || !q || !clb_q8k_activation_bytes(k)) return CLB_E_INVALID;
+    return clb::launch_quant_blocks(x, k / 256, q, static_cast<cudaStream_t>(stream)) == cudaSuccess ? CLB_OK
+                                                                                                      : CLB_E_CUDA;
+}
+
+int32_t clb_q8k_mv(int32_t type, const void* w, const void* q, float* y, int32_t n, int32_t k, void* stream) {
+    if (!clb_type_supported(type) || !w || !q || !y || n <= 0 || !clb_q8k_activation_bytes(k) || k > 65536)
+        return CLB_E_INVALID;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return CLB_E_CUDA;
+    try {
+        ensure_device_ready(dev, static_cast<cudaStream_t>(stream));
+    } catch (...) {
+        return CLB_E_CUDA;
+    }
+    const PackedLayout l = clb_packed_layout(type, n, k);
+    const uint8_t* base = static_cast<const uint8_t*>(w);
+    PackedMat m{};
+    m.body = base + l.body;
+    m.sc = base + l.sc;
+    m.d = reinterpret_cast<const uint16_t*>(base + l.d);
+    m.type = type;
+    m.n = n;
+    m.k = k;
+    return clb::launch_mv(m, q, y, static_cast<cudaStream_t>(stream)) == cudaSuccess ? CLB_OK : CLB_E_CUDA;
+}
+
+int32_t clb_q8k_activate(const float* g, const float* u, float* h, int32_t n, float limit, void* stream) {
+    if (!g || !u || !h || n <= 0 || !std::isfinite(limit)) return CLB_E_INVALID;
+    return clb::launch_activate(g, u, h, n, limit, static_cast<cudaStream_t>(stream)) == cudaSuccess ? CLB_OK
+                                                                                                      : CLB_E_CUDA;
+}
+
+// ---- layout ----
+size_t clb_packed_bytes(int32_t type, int32_t n, int32_t k) {
+    if (!clb_type_supported(type) || n <= 0 || k <= 0 || k % 256) return 0;
+    return clb_packed_layout(type, n, k).total;
+}
+
+int32_t clb_pack(int32_t type, int32_t n, int32_t k, const void* ggml, size_t ggml_bytes, void* packed,
+                 size_t packed_bytes) {
+    const size_t need = clb_packed_bytes(type, n, k);
+    if (!need || !ggml || !packed) return CLB_E_INVALID;
+    const int nb = k / 256, bb = clb_block_bytes(type);
+    if (ggml_bytes != (size_t)n * nb * bb || packed_bytes < need) return CLB_E_INVALID;
+    const PackedLayout l = clb_packed_layout(type, n, k);
+    const uint8_t* src = static_cast<const uint8_t*>(ggml);
+    for (size_t i = 0; i < (size_t)n * nb; ++i)
+        if ((clb_block_half(type, src + i * bb) & 0x7c00u) == 0x7c00u) return CLB_E_NONFINITE;
+    std::memset(packed, 0, need);
+    for (int r = 0; r < n; ++r)
+        for (int b = 0; b < nb; ++b)
+            clb_pack_block(type, n, nb, r, b, src + ((size_t)r * nb + b) * bb, static_cast<uint8_t*>(packed), l);
+    return CLB_OK;
+}
+
+int32_t clb_unpack(int32_t type, int32_t n, int32_t k, const void* packed, size_t packed_bytes, void* ggml,
+                   size_t ggml_bytes) {
+    const size_t need = clb_packed_bytes(type, n, k);
+    if (!need || !ggml || !packed) return CLB_E_INVALID;
+    const int nb = k / 256, bb = clb_block_bytes(type);
+    if (ggml_bytes != (size_t)n * nb * bb || packed_bytes < need) return CLB_E_INVALID;
+    const PackedLayout l = clb_packed_layout(type, n, k);
+    for (int r = 0; r < n; ++r)
+        for (int b = 0; b < nb; ++b)
+            clb_unpack_block(type, n, nb, r, b, static_cast<const uint8_t*>(packed), l,
+                             static_cast<uint8_t*>(ggml) + ((size_t)r * nb + b) * bb);
+    return CLB_OK;
+}
+
+// ---- bank ----
+int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_error_v1* err) {
+    if (!cfg_in || !out) return fail(err, CLB_E_INVALID, "null config/out");
+    *out = nullptr;
+    clb_bank* bank = nullptr;
+    int rc = guarded(err, [&] {
+        clb_bank_config_v1 cfg = *cfg_in;
+        if (cfg.expert_begin == 0 && cfg.expert_end == 0) cfg.expert_end = cfg.n_experts;
+        require(cfg.n_layers > 0 && cfg.n_experts > 0 && cfg.n_experts <= clb::kMaxExperts, CLB_E_INVALID,
+                "layers/experts out of range");
+        require(cfg.dim > 0 && cfg.dim % 256 == 0 && cfg.ff > 0 && cfg.ff % 256 == 0 && cfg.dim <= 32768 &&
+                    cfg.ff <= 16384,
+                CLB_E_UNSUPPORTED, "dim and ff must be positive multiples of 256 (dim <= 32768, ff <= 16384)");
+        require(cfg.max_picks >= 1 && cfg.max_picks <= clb::kMaxPicks && cfg.max_picks <= cfg.n_experts,
+                CLB_E_INVALID, "max_picks must be in [1, 16]");
+        require(std::isfinite(cfg.limit) && cfg.limit >= 0, CLB_E_INVALID, "SwiGLU limit must be finite and >= 0");
+        require(cfg.expert_begin >= 0 && cfg.expert_begin < cfg.expert_end && cfg.expert_end <= cfg.n_experts,
+                CLB_E_INVALID, "owned expert range invalid");
+        require((size_t)cfg.max_picks * cfg.ff <= 65536 * 2, CLB_E_UNSUPPORTED, "max_picks * ff too large");
+        int ndev = 0;
+        cuda_check(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+        require(cfg.device >= 0 && cfg.device < ndev, CLB_E_INVALID, "device %d not present", cfg.device);
+        DeviceGuard g(cfg.device);
+        bank = new clb_bank();
+        bank->cfg = cfg;
+        cuda_check(cudaStreamCreateWithFlags(&bank->stream, cudaStreamNonBlocking), "stream");
+        ensure_device_ready(cfg.device, bank->stream);
+        bank->desc.assign(bank->L() * bank->E(), clb::ExpertDesc{});
+        bank->resident.assign(bank->L() * bank->E(), 0);
+        bank->d_desc = bank->dev_alloc<clb::ExpertDesc>(bank->L() * bank->E());
+        const size_t dim = (size_t)cfg.dim, ff = (size_t)cfg.ff, k = (size_t)cfg.max_picks;
+        bank->d_x = bank->dev_alloc<float>(dim);
+        bank->d_out = bank->dev_alloc<float>(dim);
+        bank->d_shared = bank->dev_alloc<float>(dim);
+        bank->d_xqs = bank->dev_alloc<int8_t>(dim);
+        bank->d_xd = bank->dev_alloc<float>(dim / 256);
+        bank->d_h = bank->dev_alloc<float>(k * ff);
+        bank->d_hqs = bank->dev_alloc<int8_t>(k * ff);
+        bank->d_hd = bank->dev_alloc<float>(k * ff / 256);
+        bank->d_yrows = bank->dev_alloc<float>(k * dim);
+        bank->d_ids = bank->dev_alloc<int>(k);
+        bank->d_w = bank->dev_alloc<float>(k);
+        bank->d_err = bank->dev_alloc<int>(1);
+        bank->d_logits = bank->dev_alloc<float>(bank->L() * bank->E());
+        bank->d_route_ids = bank->dev_alloc<int>(bank->L() * k);
+        bank->d_route_w = bank->dev_alloc<float>(bank->L() * k);
+        bank->h_x = bank->host_alloc<float>(dim);
+        bank->h_out = bank->host_alloc<float>(dim);
+        bank->h_yrows = bank->host_alloc<float>(k * dim);
+        bank->h_logits = bank->host_alloc<float>(bank->L() * bank->E());
+        cuda_check(cudaMemsetAsync(bank->d_err, 0, sizeof(int), bank->stream), "memset");
+        bank->upload_desc();
+    });
+    if (rc != CLB_OK) {
+        delete bank;
+        return rc;
+    }
+    *out = bank;
+    return CLB_OK;
+}
+
+void clb_bank_destroy(clb_bank* bank) {
+    if (!bank) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(bank->cfg.device);
+    if (bank->stream) cudaStreamSynchronize(bank->stream);
+    delete bank;
+    if (prev >= 0) cudaSetDevice(prev);
+}
+
+uint64_t clb_bank_weight_bytes(const clb_bank* bank) { return bank ? bank->weight_bytes : 0; }
+
+int32_t clb_bank_contains(const clb_bank* bank, uint32_t layer, int32_t expert) {
+    if (!bank || layer >= (uint32_t)bank->cfg.n_layers || expert < 0 || expert >= bank->cfg.n_experts) return 0;
+    return bank->resident[(size_t)layer * bank->E() + (size_t)expert] ? 1 : 0;
+}
+
+int32_t clb_bank_fill_synthetic(clb_bank* bank, uint64_t seed, int32_t policy, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        bank->check_usable();
+        require(policy >= 0 && policy <= 4, CLB_E_INVALID, "type policy %d unknown", policy);
+        DeviceGuard g(bank->cfg.device);
+        std::call_once(g_scale_once, [] { clb_build_scale_table(g_scale_host); });
+        bank->device_step([&] {
+            if (!bank->d_scales) {
+                bank->d_scales = bank->dev_alloc<uint16_t>(65536);
+                cuda_check(cudaMemcpyAsync(bank->d_scales, g_scale_host, sizeof g_scale_host, cudaMemcpyHostToDevice,
+                                           bank->stream),
+                           "scale table upload");
+            }
+            const auto& c = bank->cfg;
+            for (uint32_t layer = 0; layer < (uint32_t)c.n_layers; ++layer) {
+                // one slab per layer, each matrix 256-byte aligned inside it
+                size_t slab = 0;
+                std::vector<size_t> offs;
+                for (int e = c.expert_begin; e < c.expert_end; ++e) {
+                    const int t = clb_expert_type(policy, seed, layer, (uint32_t)e);
+                    for (int role = 0; role < 3; ++role) {
+                        offs.push_back(slab);
+                        slab += clb_packed_layout(t, role == 2 ? c.dim : c.ff, role == 2 ? c.ff : c.dim).total;
+                    }
+                }
+                uint8_t* base = bank->dev_alloc<uint8_t>(slab);
+                bank->weight_bytes += slab;
+                size_t i = 0;
+                for (int e = c.expert_begin; e < c.expert_end; ++e) {
+                    const int t = clb_expert_type(policy, seed, layer, (uint32_t)e);
+                    for (int role = 0; role < 3; ++role, ++i) {
+                        const int n = role == 2 ? c.dim : c.ff, k = role == 2 ? c.ff : c.dim;
+                        const PackedLayout l = clb_packed_layout(t, n, k);
+                        cuda_check(clb::launch_synth_fill(base + offs[i], l, t, n, k, seed, layer, (uint32_t)e,
+                                                          (uint32_t)role, bank->d_scales, bank->stream),
+                                   "synthetic fill");
+                        bank->set_matrix(layer, e, role, t, base + offs[i]);
+                    }
+                    bank->refresh_resident(layer, e);
+                }
+            }
+            cuda_check(cudaStreamSynchronize(bank->stream), "fill sync");
+            bank->upload_desc();
+        });
+    });
+}
+
+int32_t clb_bank_load_matrix(clb_bank* bank, uint32_t layer, int32_t expert, int32_t role, int32_t type,
+                             const void* ggml, size_t bytes, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        bank->check_usable();
+        const auto& c = bank->cfg;
+        require(layer < (uint32_t)c.n_layers && expert >= 0 && expert < c.n_experts && role >= 0 && role <= 2,
+                CLB_E_INVALID, "matrix address out of range");
+        require(bank->owns(expert), CLB_E_INVALID, "expert %d outside this bank's owned range", expert);
+        require(clb_type_supported(type), CLB_E_UNSUPPORTED, "quant type %d has no kernel", type);
+        const int n = role == 2 ? c.dim : c.ff, k = role == 2 ? c.ff : c.dim;
+        require(ggml && bytes == (size_t)n * (k / 256) * clb_block_bytes(type), CLB_E_INVALID,
+                "matrix byte extent %zu does not match [%d, %d] of type %d", bytes, n, k, type);
+        auto& d = bank->desc[(size_t)layer * bank->E() + (size_t)expert];
+        const PackedMat& cur = role == 0 ? d.gate : role == 1 ? d.up : d.down;
+        require(cur.body == nullptr, CLB_E_INVALID, "matrix already loaded");
+        DeviceGuard g(c.device);
+        bank->device_step([&] {
+            const PackedLayout l = clb_packed_layout(type, n, k);
+            uint8_t* packed = bank->dev_alloc<uint8_t>(l.total);
+            void* staging = nullptr;
+            cuda_check(cudaMalloc(&staging, bytes), "staging alloc");
+            int bad = 0;
+            cudaError_t e = cudaMemcpyAsync(staging, ggml, bytes, cudaMemcpyHostToDevice, bank->stream);
+            if (e == cudaSuccess) e = cudaMemsetAsync(bank->d_err, 0, sizeof(int), bank->stream);
+            if (e == cudaSuccess)
+                e = clb::launch_pack(static_cast<const uint8_t*>(staging), packed, l, type, n, k, bank->d_err,
+                                     bank->stream);
+            if (e == cudaSuccess) e = cudaMemcpyAsync(&bad, bank->d_err, sizeof(int), cudaMemcpyDeviceToHost, bank->stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(bank->stream);
+            cudaFree(staging);
+            cuda_check(e, "matrix upload/pack");
+            if (bad) {
+                cuda_check(cudaMemsetAsync(bank->d_err, 0, sizeof(int), bank->stream), "flag reset");
+                throw Error(CLB_E_NONFINITE, "non-finite fp16 super-scale in matrix");
+            }
+            bank->weight_bytes += l.total;
+            bank->set_matrix(layer, expert, role, type, packed);
+            bank->refresh_resident(layer, expert);
+            bank->upload_desc();
+        });
+    });
+}
+
+void* clb_bank_stream(clb_bank* bank) { return bank ? bank->stream : nullptr; }
+
+int32_t clb_bank_synchronize(clb_bank* bank, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    return guarded(err, [&] {
+        DeviceGuard g(bank->cfg.device);
+        bank->device_step([&] { cuda_check(cudaStreamSynchronize(bank->stream), "sync"); });
+    });
+}
+
+static void compute_rows(clb_bank* bank, uint32_t layer, const int32_t* ids, int32_t n, const float* x, float* y) {
+    const auto& c = bank->cfg;
+    require(x && y, CLB_E_INVALID, "null buffer");
+    bank->validate_ids(layer, ids, n, true);
+    require(finite_all(x, (size_t)c.dim), CLB_E_NONFINITE, "non-finite activation");
+    DeviceGuard g(c.device);
+    bank->device_step([&] {
+        std::memcpy(bank->h_x, x, sizeof(float) * c.dim);
+        cuda_check(cudaMemcpyAsync(bank->d_x, bank->h_x, sizeof(float) * c.dim, cudaMemcpyHostToDevice, bank->stream),
+                   "x H2D");
+        cuda_check(cudaMemcpyAsync(bank->d_ids, ids, sizeof(int) * n, cudaMemcpyHostToDevice, bank->stream), "ids H2D");
+        cuda_check(cudaMemsetAsync(bank->d_w, 0, sizeof(float) * n, bank->stream), "w memset");
+        bank->enqueue_layer(layer, bank->d_ids, bank->d_w, n, bank->d_x, nullptr, nullptr, bank->d_out, bank->d_yrows,
+                            bank->stream);
+        cuda_check(cudaMemcpyAsync(bank->h_yrows, bank->d_yrows, sizeof(float) * (size_t)n * c.dim,
+                                   cudaMemcpyDeviceToHost, bank->stream),
+                   "rows D2H");
+        bank->check_err_flag();
+    });
+    std::memcpy(y, bank->h_yrows, sizeof(float) * (size_t)n * c.dim);
+    require(finite_all(y, (size_t)n * c.dim), CLB_E_NONFINITE, "non-finite expert output");
+}
+
+int32_t clb_bank_compute(clb_bank* bank, uint32_t layer, int32_t expert, const float* x, float* y,
+                         clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        bank->check_usable();
+        compute_rows(bank, layer, &expert, 1, x, y);
+    });
+}
+
+int32_t clb_bank_compute_many(clb_bank* bank, uint32_t layer, const int32_t* ids, int32_t n, const float* x,
+                              float* y, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        bank->check_usable();
+        require(ids, CLB_E_INVALID, "null ids");
+        compute_rows(bank, layer, ids, n, x, y);
+    });
+}
+
+int32_t clb_layer_execute(clb_bank* bank, uint32_t layer, const int32_t* ids, const float* w, int32_t n,
+                          const float* x, const float* shared, float* out, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        bank->check_usable();
+        const auto& c = bank->cfg;
+        require(ids && w && x && out, CLB_E_INVALID, "null buffer");
+        bank->validate_ids(layer, ids, n, true);
+        require(finite_all(w, (size_t)n), CLB_E_NONFINITE, "non-finite route weight");
+        require(finite_all(x, (size_t)c.dim), CLB_E_NONFINITE, "non-finite activation");
+        require(!shared || finite_all(shared, (size_t)c.dim), CLB_E_NONFINITE, "non-finite shared output");
+        DeviceGuard g(c.device);
+        bank->device_step([&] {
+            std::memcpy(bank->h_x, x, sizeof(float) * c.dim);
+            cuda_check(cudaMemcpyAsync(bank->d_x, bank->h_x, sizeof(float) * c.dim, cudaMemcpyHostToDevice,
+                                       bank->stream),
+                       "x H2D");
+            if (shared)
+                cuda_check(cudaMemcpyAsync(bank->d_shared, shared, sizeof(float) * c.dim, cudaMemcpyHostToDevice,
+                                           bank->stream),
+                           "shared H2D");
+            cuda_check(cudaMemcpyAsync(bank->d_ids, ids, sizeof(int) * n, cudaMemcpyHostToDevice, bank->stream),
+                       "ids H2D");
+            cuda_check(cudaMemcpyAsync(bank->d_w, w, sizeof(float) * n, cudaMemcpyHostToDevice, bank->stream), "w H2D");
+            bank->enqueue_layer(layer, bank->d_ids, bank->d_w, n, bank->d_x, shared ? bank->d_shared : nullptr,
+                                nullptr, bank->d_out, nullptr, bank->stream);
+            cuda_check(cudaMemcpyAsync(bank->h_out, bank->d_out, sizeof(float) * c.dim, cudaMemcpyDeviceToHost,
+                                       bank->stream),
+                       "out D2H");
+            bank->check_err_flag();
+        });
+        std::memcpy(out, bank->h_out, sizeof(float) * c.dim);
+        require(finite_all(out, (size_t)c.dim), CLB_E_NONFINITE, "non-finite layer output");
+    });
+}
+
+int32_t clb_layer_forward_device(clb_bank* bank, uint32_t layer, const int32_t* d_ids, const float* d_w, int32_t n,
+                                 const float* d_x, const float* d_shared, const float* d_resid, float* d_out,
+                                 void* stream, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    return guarded(err, [&] {
+        bank->check_usable();
+        require(layer < (uint32_t)bank->cfg.n_layers && n >= 1 && n <= bank->cfg.max_picks && d_ids && d_w && d_x &&
+                    d_out,
+                CLB_E_INVALID, "invalid device layer arguments");
+        DeviceGuard g(bank->cfg.device);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : bank->stream;
+        bank->device_step([&] {
+            bank->enqueue_layer(layer, d_ids, d_w, n, d_x, d_shared, d_resid, d_out, nullptr, s);
+        });
+    });
+}
+
+int32_t clb_layer_phases_device(clb_bank* bank, uint32_t layer, const int32_t* d_ids, const float* d_w, int32_t n,
+                                const float* d_x, float* d_out, int32_t phase_mask, void* stream, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    return guarded(err, [&] {
+        bank->check_usable();
+        require(layer < (uint32_t)bank->cfg.n_layers && n >= 1 && n <= bank->cfg.max_picks && d_ids && d_w && d_x &&
+                    d_out && phase_mask > 0 && phase_mask < 16,
+                CLB_E_INVALID, "invalid phase arguments");
+        DeviceGuard g(bank->cfg.device);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : bank->stream;
+        bank->device_step([&] { bank->enqueue_phases(layer, d_ids, d_w, n, d_x, d_out, phase_mask, s); });
+    });
+}
+
+int32_t clb_bank_expert_info(const clb_bank* bank, uint32_t layer, int32_t expert, int32_t* type,
+                             uint64_t* payload_bytes) {
+    if (!bank || !clb_bank_contains(bank, layer, expert)) return CLB_E_INVALID;
+    const auto& d = bank->desc[(size_t)layer * bank->E() + (size_t)expert];
+    const int t = d.gate.type;
+    const uint64_t bb = (uint64_t)clb_block_bytes(t);
+    const uint64_t gu = (uint64_t)d.gate.n * (uint64_t)(d.gate.k / 256) * bb;
+    const uint64_t dn = (uint64_t)d.down.n * (uint64_t)(d.down.k / 256) * (uint64_t)clb_block_bytes(d.down.type);
+    if (type) *type = t;
+    if (payload_bytes) *payload_bytes = 2 * gu + dn;
+    return CLB_OK;
+}
+
+int32_t clb_route_device(int32_t mode, const float* d_logits, int32_t n_experts, int32_t k, int32_t tokens,
+                         int32_t* d_ids, float* d_w, void* stream) {
+    if (mode != 0 || !d_logits || !d_ids || !d_w || n_experts <= 0 || n_experts > clb::kMaxExperts || k <= 0 ||
+        k > clb::kMaxPicks || k > n_experts || tokens <= 0)
+        return CLB_E_INVALID;
+    return clb::launch_route_sigmoid(d_logits, n_experts, k, tokens, d_ids, d_w, static_cast<cudaStream_t>(stream)) ==
+                   cudaSuccess
+               ? CLB_OK
+               : CLB_E_CUDA;
+}
+
+int32_t clb_route_host(int32_t mode, const float* logits, const float* bias, int32_t n, int32_t k, float scale,
+                       int32_t* ids, float* w) {
+    if (!logits || !ids || !w || n <= 0 || k <= 0 || k > n || k > 64) return CLB_E_INVALID;
+    if (!finite_all(logits, (size_t)n)) return CLB_E_NONFINITE;
+    if (mode == 0) {
+        std::vector<char> used((size_t)n, 0);
+        float s[64], sum = 0.0f;
+        for (int i = 0; i < k; ++i) {
+            int best = -1;
+            for (int e = 0; e < n; ++e)
+                if (!used[(size_t)e] && (best < 0 || logits[e] > logits[best])) best = e;
+            used[(size_t)best] = 1;
+            ids[i] = best;
+            s[i] = 1.0f / (1.0f + std::exp(-logits[best]));
+            sum += s[i];
+        }
+        for (int i = 0; i < k; ++i) w[i] = s[i] / sum;
+        return CLB_OK;
+    }
+    if (mode != 1 || !bias) return CLB_E_INVALID;
+    if (!finite_all(bias, (size_t)n) || !std::isfinite(scale) || scale < 0) return CLB_E_INVALID;
+    std::vector<float> sc((size_t)n), bs((size_t)n);
+    for (int e = 0; e < n; ++e) {
+        const float l = logits[e];
+        const float sp = l > 20.0f ? l : std::log1p(std::exp(l));
+        sc[(size_t)e] = std::sqrt(sp);
+        bs[(size_t)e] = sc[(size_t)e] + bias[e];
+        if (!std::isfinite(bs[(size_t)e])) return CLB_E_NONFINITE;
+    }
+    float sum = 0.0f;
+    for (int i = 0; i < k; ++i) {
+        int best = 0;
+        for (int e = 1; e < n; ++e)
+            if (bs[(size_t)e] > bs[(size_t)best]) best = e;
+        ids[i] = best;
+        sum += sc[(size_t)best];
+        bs[(size_t)best] = -std::numeric_limits<float>::max();
+    }
+    for (int i = 0; i < k; ++i) w[i] = sc[(size_t)ids[i]] / (sum + 1e-20f) * scale;
+    return CLB_OK;
+}
+
+int32_t clb_stack_decode(clb_bank* bank, uint32_t first, int32_t nl, const float* x, const float* logits, float* out,
+                         clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        bank->check_usable();
+        const auto& c = bank->cfg;
+        require(x && logits && out, CLB_E_INVALID, "null buffer");
+        require(nl >= 1 && first + (uint32_t)nl <= (uint32_t)c.n_layers, CLB_E_INVALID, "layer range out of bounds");
+        require(c.expert_begin == 0 && c.expert_end == c.n_experts, CLB_E_INVALID,
+                "stack decode needs every expert resident (use the sharded driver for partial banks)");
+        for (int l = 0; l < nl; ++l)
+            for (int e = 0; e < c.n_experts; ++e)
+                require(bank->resident[(size_t)(first + l) * bank->E() + (size_t)e], CLB_E_INVALID,
+                        "expert (%u, %d) not resident", first + l, e);
+        DeviceGuard g(c.device);
+        bank->device_step([&] {
+            std::memcpy(bank->h_x, x, sizeof(float) * c.dim);
+            std::memcpy(bank->h_logits, logits, sizeof(float) * (size_t)nl * c.n_experts);
+            auto key = std::make_pair(first, nl);
+            auto it = bank->graphs.find(key);
+            if (it == bank->graphs.end()) {
+                cudaGraph_t graph = nullptr;
+                cuda_check(cudaStreamBeginCapture(bank->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+                try {
+                    cuda_check(cudaMemcpyAsync(bank->d_x, bank->h_x, sizeof(float) * c.dim, cudaMemcpyHostToDevice,
+                                               bank->stream),
+                               "x H2D");
+                    cuda_check(cudaMemcpyAsync(bank->d_logits, bank->h_logits, sizeof(float) * (size_t)nl * c.n_experts,
+                                               cudaMemcpyHostToDevice, bank->stream),
+                               "logits H2D");
+                    bank->enqueue_stack(first, nl, bank->d_x, bank->d_logits, bank->stream);
+                    cuda_check(cudaMemcpyAsync(bank->h_out, bank->d_x, sizeof(float) * c.dim, cudaMemcpyDeviceToHost,
+                                               bank->stream),
+                               "out D2H");
+                } catch (...) {
+                    cudaStreamEndCapture(bank->stream, &graph);
+                    if (graph) cudaGraphDestroy(graph);
+                    throw;
+                }
+                cuda_check(cudaStreamEndCapture(bank->stream, &graph), "end capture");
+                cudaGraphExec_t exec = nullptr;
+                cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+                cudaGraphDestroy(graph);
+                cuda_check(e, "graph instantiate");
+                it = bank->graphs.emplace(key, exec).first;
+            }
+            cuda_check(cudaGraphLaunch(it->second, bank->stream), "graph launch");
+            bank->check_err_flag();
+        });
+        std::memcpy(out, bank->h_out, sizeof(float) * c.dim);
+        require(finite_all(out, (size_t)c.dim), CLB_E_NONFINITE, "non-finite stack output");
+    });
+}
+
+int32_t clb_stack_decode_device(clb_bank* bank, uint32_t first, int32_t nl, float* d_x, const float* d_logits,
+                                clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    return guarded(err, [&] {
+        bank->check_usable();
+        const auto& c = bank->cfg;
+        require(d_x && d_logits && nl >= 1 && first + (uint32_t)nl <= (uint32_t)c.n_layers, CLB_E_INVALID,
+                "invalid stack arguments");
+        DeviceGuard g(c.device);
+        bank->device_step([&] {
+            // Graphs are keyed by layer range and bound to (d_x, d_logits) of their capture.
+            auto key = std::make_pair(first, nl);
+            auto it = bank->device_graphs.find(key);
+            if (it != bank->device_graphs.end() && bank->graph_dx != d_x) {
+                cudaGraphExecDestroy(it->second);
+                bank->device_graphs.erase(it);
+                it = bank->device_graphs.end();
+            }
+            if (it == bank->device_graphs.end()) {
+                cudaGraph_t graph = nullptr;
+                cuda_check(cudaStreamBeginCapture(bank->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+                try {
+                    bank->enqueue_stack(first, nl, d_x, d_logits, bank->stream);
+                } catch (...) {
+                    cudaStreamEndCapture(bank->stream, &graph);
+                    if (graph) cudaGraphDestroy(graph);
+                    throw;
+                }
+                cuda_check(cudaStreamEndCapture(bank->stream, &graph), "end capture");
+                cudaGraphExec_t exec = nullptr;
+                cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+                cudaGraphDestroy(graph);
+                cuda_check(e, "graph instantiate");
+                it = bank->device_graphs.emplace(key, exec).first;
+                bank->graph_dx = d_x;
+            }
+            cuda_check(cudaGraphLaunch(it->second, bank->stream), "graph launch");
+        });
+    });
+}
+
+int32_t clb_warm_execute(clb_bank* bank, uint32_t layer, const int32_t* ids, const float* w, int32_t n,
+                         const float* x, const float* shared, clb_host_expert_fn host_lane, void* host_ctx, float* out,
+                         clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    return guarded(err, [&] {
+        const auto& c = bank->cfg;
+        require(ids && w && x && out && n >= 1 && n <= 64, CLB_E_INVALID, "invalid warm_execute arguments");
+        require(layer < (uint32_t)c.n_layers, CLB_E_INVALID, "layer out of range");
+        std::set<int> seen;
+        for (int i = 0; i < n; ++i) {
+            require(ids[i] >= 0 && ids[i] < c.n_experts && seen.insert(ids[i]).second && std::isfinite(w[i]),
+                    CLB_E_INVALID, "invalid/duplicate route");
+        }
+        const size_t dim = (size_t)c.dim;
+        std::vector<int> gpu_pick, host_pick;
+        for (int i = 0; i < n; ++i) (clb_bank_contains(bank, layer, ids[i]) ? gpu_pick : host_pick).push_back(i);
+        require(host_pick.empty() || host_lane, CLB_E_INVALID, "picks outside the bank but no host lane");
+        require((int)gpu_pick.size() <= c.max_picks, CLB_E_INVALID, "more resident picks than the bank's max_picks");
+        std::vector<float> rows((size_t)n * dim);
+        // CUDA lane on a worker thread, host lane on the caller; both always joined.
+        clb_error_v1 gpu_err{};
+        int gpu_rc = CLB_OK;
+        std::thread gpu([&] {
+            if (gpu_pick.empty()) return;
+            std::vector<int32_t> sel;
+            for (int i : gpu_pick) sel.push_back(ids[i]);
+            std::vector<float> y(sel.size() * dim);
+            gpu_rc = clb_bank_compute_many(bank, layer, sel.data(), (int32_t)sel.size(), x, y.data(), &gpu_err);
+            if (gpu_rc == CLB_OK)
+                for (size_t j = 0; j < sel.size(); ++j)
+                    std::memcpy(&rows[(size_t)gpu_pick[j] * dim], &y[j * dim], sizeof(float) * dim);
+        });
+        int host_rc = CLB_OK;
+        std::string host_msg;
+        for (int i : host_pick) {
+            const int32_t rc = host_lane(host_ctx, layer, ids[i], x, c.dim, &rows[(size_t)i * dim]);
+            if (rc != 0) {
+                host_rc = CLB_E_LANE;
+                host_msg = "host lane failed for expert " + std::to_string(ids[i]);
+                break;
+            }
+            if (!finite_all(&rows[(size_t)i * dim], dim)) {
+                host_rc = CLB_E_NONFINITE;
+                host_msg = "host lane returned a non-finite row";
+                break;
+            }
+        }
+        gpu.join();
+        if (gpu_rc != CLB_OK) throw Error(gpu_rc, std::string("CUDA lane: ") + gpu_err.message);
+        if (host_rc != CLB_OK) throw Error(host_rc, host_msg);
+        // Combine: ascending expert id, out = fmaf(w, y, out), then + shared (runtime.cpp:184-187).
+        std::vector<int> order((size_t)n);
+        for (int i = 0; i < n; ++i) order[(size_t)i] = i;
+        std::sort(order.begin(), order.end(), [&](int a, int b) { return ids[a] < ids[b]; });
+        std::vector<float> acc(dim, 0.0f);
+        for (int i : order)
+            for (size_t k = 0; k < dim; ++k) acc[k] = std::fma(w[i], rows[(size_t)i * dim + k], acc[k]);
+        if (shared)
+            for (size_t k = 0; k < dim; ++k) acc[k] += shared[k];
+        std::memcpy(out, acc.data(), sizeof(float) * dim);
+    });
+}
+
+}  // extern "C"

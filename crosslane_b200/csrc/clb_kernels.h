@@ -1,0 +1,47 @@
+// Host-side declarations of the sm_100a kernels (clb_kernels.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "clb_types.h"
+
+namespace clb {
+
+constexpr int kTabXXS = 0;
+constexpr int kTabXS = 256;
+constexpr int kTabIQ1 = 768;
+constexpr int kTabSign = 2816;
+constexpr int kTableWords = 2944;     // 256 + 512 + 2048 + 128 nibble selectors
+constexpr int kQ8KBlockBytes = 292;   // crosslane q8k::Block (q8k_core.hpp:13-14)
+constexpr int kMaxExperts = 1024;     // per layer, for device routing
+constexpr int kMaxPicks = 16;         // hipex::max_jobs (hip_experts.hpp:8)
+
+// Device descriptor of one resident expert: gate (w1), up (w3), down (w2).
+struct ExpertDesc {
+    PackedMat gate, up, down;
+};
+
+void host_tables(uint32_t* out /* kTableWords */);
+cudaError_t upload_tables(cudaStream_t stream);
+cudaError_t set_smem_limits();
+size_t mv_smem(int k);
+size_t gateup_smem(int dim);
+size_t down_smem(int npick, int ff);
+
+cudaError_t launch_quant(const float* x, int nblocks, int8_t* qs, float* d, cudaStream_t s);
+cudaError_t launch_quant_blocks(const float* x, int nblocks, void* out, cudaStream_t s);
+cudaError_t launch_norm_quant(const float* h, int dim, int8_t* qs, float* d, float* xnorm, cudaStream_t s);
+cudaError_t launch_mv(const PackedMat& m, const void* q, float* y, cudaStream_t s);
+cudaError_t launch_activate(const float* g, const float* u, float* h, int n, float limit, cudaStream_t s);
+cudaError_t launch_gateup(const ExpertDesc* experts, const int* ids, int npick, const int8_t* xqs, const float* xd,
+                          int dim, int ff, float limit, float* h, int* err, cudaStream_t s);
+cudaError_t launch_down_combine(const ExpertDesc* experts, const int* ids, const float* w, int npick,
+                                const int8_t* hqs, const float* hd, int dim, int ff, const float* shared,
+                                const float* resid, float* out, float* y_rows, int* err, cudaStream_t s);
+cudaError_t launch_route_sigmoid(const float* logits, int n, int k, int tokens, int* ids, float* w, cudaStream_t s);
+cudaError_t launch_synth_fill(uint8_t* packed, const PackedLayout& l, int type, int n, int k, uint64_t seed,
+                              uint32_t layer, uint32_t expert, uint32_t role, const uint16_t* scales, cudaStream_t s);
+cudaError_t launch_pack(const uint8_t* aos, uint8_t* packed, const PackedLayout& l, int type, int n, int k, int* bad,
+                        cudaStream_t s);
+
+}  // namespace clb

@@ -1,0 +1,214 @@
+/* crosslane_b200 -- B200-native (sm_100a) routed-expert decode lane for crosslane.
+ *
+ * Drop-in C ABI of the CUDA expert lane. Plain pointers and sizes only; every
+ * function returns 0 on success or a CLB_E_* code. Functions taking a
+ * `clb_error_v1*` also write a message there (may be NULL); this mirrors crosslane's
+ * `strata_stage_error_v1 {int32 code; char message[512]}` convention
+ * (engine/strata/sycl/stage/abi.h:19-22).
+ *
+ * Device-pointer primitives take a caller-owned CUDA stream (`void*` = cudaStream_t,
+ * NULL = legacy default stream) and never allocate, like crosslane's Q8_K HIP API
+ * (engine/strata/sycl/stage/wiring/hip_q8k.hpp:6-10).
+ *
+ * Quant types use ggml ids: 16 = IQ2_XXS, 17 = IQ2_XS, 29 = IQ1_M.
+ * Matrices are [n rows, k columns], k % 256 == 0. Expert roles: 0 = gate (w1),
+ * 1 = up (w3), 2 = down (w2), as in layers.L.ffn.experts.E.{w1,w3,w2}.weight
+ * (engine/strata/sycl/stage/wiring/cpu_lane.hpp:36).
+ */
+#ifndef CROSSLANE_B200_H
+#define CROSSLANE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CLB_ABI_VERSION 1
+
+enum {
+    CLB_OK = 0,
+    CLB_E_INVALID = 1,     /* bad argument, shape, type or duplicate id */
+    CLB_E_CUDA = 2,        /* a CUDA call failed */
+    CLB_E_NOMEM = 3,       /* device or host allocation failed */
+    CLB_E_STATE = 4,       /* object unusable (earlier failure poisons it) */
+    CLB_E_NONFINITE = 5,   /* non-finite input or output */
+    CLB_E_UNSUPPORTED = 6, /* quant type or geometry without a kernel */
+    CLB_E_LANE = 7,        /* another lane of warm_execute failed */
+    CLB_E_NCCL = 8         /* a collective failed */
+};
+
+typedef struct clb_error_v1 {
+    int32_t code;
+    char message[512];
+} clb_error_v1;
+
+/* ABI version; lets a dlopen()ing host refuse a mismatched library. */
+int32_t clb_abi_version(void);
+
+/* ---- Q8_K activation primitives (device pointers, caller stream, no allocation) ---- */
+
+/* Bytes of the Q8_K activation of a k-vector: k/256 crosslane q8k::Block structs
+ * (292 B: fp32 d, int8 qs[256], int16 bsums[16]); 0 if k % 256 != 0.
+ * Replaces q8k::activation_bytes (engine/strata/sycl/stage/wiring/hip_q8k.hpp:8). */
+size_t clb_q8k_activation_bytes(int32_t k);
+
+/* q[k/256 blocks] = Q8_K(x[k]). Replaces q8k::quantize (hip_q8k.hpp:9). */
+int32_t clb_q8k_quantize(const float* x, void* q, int32_t k, void* stream);
+
+/* y[n] = W . q for a matrix in the packed bank layout (clb_pack).
+ * Bit-identical to crosslane's q8k::dot per row (q8k_core.hpp:76-91).
+ * Replaces q8k::mv (hip_q8k.hpp:10). */
+int32_t clb_q8k_mv(int32_t type, const void* w_packed, const void* q, float* y, int32_t n, int32_t k, void* stream);
+
+/* h[i] = swiglu(g[i], u[i]) with clamp `limit` (0 = none).
+ * Replaces q8k::activate (hip_q8k.hpp:11). */
+int32_t clb_q8k_activate(const float* g, const float* u, float* h, int32_t n, float limit, void* stream);
+
+/* ---- packed bank layout (host memory) ---- */
+
+/* Size of one matrix in the packed bank layout (>= the ggml bytes, planes 256 B
+ * aligned); 0 for an unsupported type or geometry.
+ * Replaces mmvq::extent (engine/strata/warm/mmvq_layout.hpp:12-15). */
+size_t clb_packed_bytes(int32_t type, int32_t n, int32_t k);
+
+/* ggml AoS bytes -> packed layout; rejects a non-finite fp16 super-scale.
+ * Replaces mmvq::reorder (mmvq_layout.hpp:19-32). */
+int32_t clb_pack(int32_t type, int32_t n, int32_t k, const void* ggml, size_t ggml_bytes, void* packed,
+                 size_t packed_bytes);
+
+/* packed layout -> ggml AoS bytes (exact inverse of clb_pack).
+ * Replaces mmvq::restore (mmvq_layout.hpp:33-42). */
+int32_t clb_unpack(int32_t type, int32_t n, int32_t k, const void* packed, size_t packed_bytes, void* ggml,
+                   size_t ggml_bytes);
+
+/* ---- expert bank: the resident CUDA lane ---- */
+
+typedef struct clb_bank clb_bank;
+
+typedef struct clb_bank_config_v1 {
+    int32_t device;        /* CUDA ordinal */
+    int32_t n_layers;      /* layers the bank spans (ids 0..n_layers-1) */
+    int32_t n_experts;     /* routed experts per layer */
+    int32_t dim;           /* hidden size (gate/up k, down n) */
+    int32_t ff;            /* expert intermediate size */
+    int32_t max_picks;     /* routed experts per token and layer, <= 16 */
+    float limit;           /* SwiGLU clamp, 0 = none (crosslane's model uses 10) */
+    int32_t expert_begin;  /* this bank owns experts [expert_begin, expert_end) of */
+    int32_t expert_end;    /*   every layer (expert-ID sharding); 0,0 = all */
+    int32_t reserved[7];
+} clb_bank_config_v1;
+
+/* Creates a bank and its fixed workspace on `device` (no allocation afterwards).
+ * Replaces the construction half of HipResidentBank::load
+ * (engine/strata/sycl/stage/wiring/hip_resident_bank.hpp:38-96). */
+int32_t clb_bank_create(const clb_bank_config_v1* cfg, clb_bank** out, clb_error_v1* err);
+void clb_bank_destroy(clb_bank* bank);
+
+/* Allocates and fills every owned matrix with the counter-based synthetic weights
+ * (seed, layer, expert, role, block) -> bytes. type_policy: 0 all IQ2_XXS,
+ * 1 experts 0-127 IQ2_XXS / 128-255 IQ2_XS / 256+ IQ1_M, 2 per (layer, expert) from
+ * the seed, 3 all IQ2_XS, 4 all IQ1_M. */
+int32_t clb_bank_fill_synthetic(clb_bank* bank, uint64_t seed, int32_t type_policy, clb_error_v1* err);
+
+/* Uploads one matrix given as ggml AoS bytes (host memory) and packs it on device.
+ * Replaces the per-matrix upload of HipResidentBank::load (hip_resident_bank.hpp:97-136). */
+int32_t clb_bank_load_matrix(clb_bank* bank, uint32_t layer, int32_t expert, int32_t role, int32_t type,
+                             const void* ggml, size_t bytes, clb_error_v1* err);
+
+/* Device bytes held by expert matrices (sum of packed sizes). */
+uint64_t clb_bank_weight_bytes(const clb_bank* bank);
+
+/* 1 if (layer, expert) is resident in this bank, else 0. Const, allocation free.
+ * Replaces WarmRedirect::warm_contains (engine/strata/warm/runtime.hpp:14). */
+int32_t clb_bank_contains(const clb_bank* bank, uint32_t layer, int32_t expert);
+
+/* y[dim] = expert(x) for one resident expert; host buffers, synchronous.
+ * Replaces WarmRedirect::warm_compute (runtime.hpp:15). */
+int32_t clb_bank_compute(clb_bank* bank, uint32_t layer, int32_t expert, const float* x, float* y,
+                         clb_error_v1* err);
+
+/* y[n][dim] = expert_i(x), one row per id in the given order; host buffers, one
+ * batched launch per phase for all picks. Replaces WarmRedirect::warm_compute_many
+ * (runtime.hpp:13) / HipResidentBank::enqueue_layer (hip_resident_bank.hpp:170-236). */
+int32_t clb_bank_compute_many(clb_bank* bank, uint32_t layer, const int32_t* ids, int32_t n, const float* x,
+                              float* y, clb_error_v1* err);
+
+/* out[dim] = sum over picks in ascending expert id of fma(w_i, expert_i(x)), then
+ * + shared (shared may be NULL = zeros); all picks resident; host buffers.
+ * The device-side twin of warm_execute's combine (engine/strata/warm/runtime.cpp:121-189). */
+int32_t clb_layer_execute(clb_bank* bank, uint32_t layer, const int32_t* ids, const float* w, int32_t n,
+                          const float* x, const float* shared, float* out, clb_error_v1* err);
+
+/* Device-pointer layer step on the bank's stream (or `stream` if non-NULL):
+ * d_out = [d_resid +] (combine over d_ids/d_w of expert(d_x) [+ d_shared]).
+ * d_ids/d_w live in device memory (e.g. written by clb_route_device). */
+int32_t clb_layer_forward_device(clb_bank* bank, uint32_t layer, const int32_t* d_ids, const float* d_w,
+                                 int32_t n, const float* d_x, const float* d_shared, const float* d_resid,
+                                 float* d_out, void* stream, clb_error_v1* err);
+
+/* Profiling form of clb_layer_forward_device: runs only the kernels selected by
+ * phase_mask (1 quantise x, 2 gate/up + SwiGLU, 4 quantise h, 8 down + combine).
+ * Phases read what earlier phases left in the bank's workspace, so a phase may run
+ * alone only after a full step has run with the same arguments. */
+int32_t clb_layer_phases_device(clb_bank* bank, uint32_t layer, const int32_t* d_ids, const float* d_w, int32_t n,
+                                const float* d_x, float* d_out, int32_t phase_mask, void* stream, clb_error_v1* err);
+
+/* Quant type and ggml payload bytes (sum of its three matrices) of a resident expert;
+ * returns CLB_E_INVALID if (layer, expert) is not resident. */
+int32_t clb_bank_expert_info(const clb_bank* bank, uint32_t layer, int32_t expert, int32_t* type,
+                             uint64_t* payload_bytes);
+
+/* Routing on device. mode 0: top-k by sigmoid(logit) (ties to the lower id),
+ * weights renormalised to sum 1. `tokens` rows of n_experts logits.
+ * Host twin of mode 1 (crosslane route_cpu, engine/strata/sycl/route/route.cpp:15-37)
+ * is clb_route_host. */
+int32_t clb_route_device(int32_t mode, const float* d_logits, int32_t n_experts, int32_t k, int32_t tokens,
+                         int32_t* d_ids, float* d_w, void* stream);
+
+/* Host routing for one token. mode 0 as above; mode 1 = route_cpu:
+ * sqrt(softplus(l)) + bias, top-k, w = sc / (sum + 1e-20) * scale. */
+int32_t clb_route_host(int32_t mode, const float* logits, const float* bias, int32_t n_experts, int32_t k,
+                       float scale, int32_t* ids, float* w);
+
+/* Decode of `n_layers` consecutive layers for one token, end to end from host
+ * memory, with the pre-norm residual structure of a DeepSeek layer:
+ *   x_l = RMSNorm(h_l) = h_l * (float)(1 / sqrt(mean(h_l^2) + 1e-6))  (unit weight),
+ *   h_{l+1} = h_l + combine_l(route(logits_l), experts(x_l)).
+ * The fp64 sum of squares has a fixed order (1024 strided lanes, then a binary
+ * tree) so it is reproducible bit for bit on the CPU.
+ * h: [dim] in, logits: [n_layers][n_experts], out: [dim]. Routing mode 0 on device.
+ * The per-token graph is captured once and replayed. */
+int32_t clb_stack_decode(clb_bank* bank, uint32_t first_layer, int32_t n_layers, const float* x,
+                         const float* logits, float* out, clb_error_v1* err);
+
+/* Device-resident variant of clb_stack_decode on the bank's stream (no host copies,
+ * no synchronisation): d_x [dim] is updated in place. */
+int32_t clb_stack_decode_device(clb_bank* bank, uint32_t first_layer, int32_t n_layers, float* d_x,
+                                const float* d_logits, clb_error_v1* err);
+
+/* The bank's CUDA stream (cudaStream_t) and a synchronisation helper. */
+void* clb_bank_stream(clb_bank* bank);
+int32_t clb_bank_synchronize(clb_bank* bank, clb_error_v1* err);
+
+/* ---- warm_execute: the three-lane join with this bank as the GPU lane ---- */
+
+/* Host lane callback: compute y[dim] of one non-resident expert (crosslane's
+ * CpuLane::expert, engine/strata/sycl/stage/wiring/cpu_lane.hpp:18). Return 0 on
+ * success; nonzero fails the layer after every lane has drained. */
+typedef int32_t (*clb_host_expert_fn)(void* ctx, uint32_t layer, int32_t expert, const float* x, int32_t dim,
+                                      float* y);
+
+/* Partitions the picks (resident -> this bank, else -> host lane), runs both lanes
+ * concurrently, always joins both, then combines in ascending expert id with fmaf
+ * and adds `shared`. Replaces warm_execute (engine/strata/warm/runtime.cpp:121-189). */
+int32_t clb_warm_execute(clb_bank* bank, uint32_t layer, const int32_t* ids, const float* w, int32_t n,
+                         const float* x, const float* shared, clb_host_expert_fn host_lane, void* host_ctx,
+                         float* out, clb_error_v1* err);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CROSSLANE_B200_H */

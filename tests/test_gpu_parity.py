@@ -1,0 +1,343 @@
+"""GPU parity of the CUDA expert lane against the CPU oracle (through the C ABI).
+
+Contract: Q8_K activation bytes, integer dots and every row dot are bit-identical to
+crosslane's CPU-lane arithmetic (q8k_core.hpp); SwiGLU differs at most by CUDA-vs-glibc
+expf rounding (<= 2 ulp asserted); combined fp32 layer outputs are within the
+relative L2 <= 1e-3 and max-abs-relative <= 5e-3.
+"""
+import numpy as np
+import pytest
+
+from oracle_lib import Q8K, bits, max_abs_rel, rel_l2, tie_probe
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 1e-3
+MAX_ABS_REL = 5e-3
+TYPES = [16, 17, 29]
+
+
+@pytest.fixture(scope="module")
+def cb(cuda):
+    import crosslane_b200
+    return crosslane_b200
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def gpu_quantize(torch, cb, x):
+    dx = dev(torch, np.asarray(x, np.float32))
+    dq = torch.zeros(x.size // 256 * Q8K, dtype=torch.uint8, device="cuda")
+    cb.q8k_quantize(dx, dq)
+    torch.cuda.synchronize()
+    return dq.cpu().numpy()
+
+
+def gpu_mv(torch, cb, qtype, w_ggml, q, n, k):
+    packed = cb.pack(qtype, n, k, w_ggml)
+    dw = dev(torch, packed)
+    dq = dev(torch, q)
+    dy = torch.zeros(n, dtype=torch.float32, device="cuda")
+    cb.q8k_mv(qtype, dw, dq, dy, n, k)
+    torch.cuda.synchronize()
+    return dy.cpu().numpy()
+
+
+def ulp_diff(a, b):
+    ai = bits(a).astype(np.int64)
+    bi = bits(b).astype(np.int64)
+    ai = np.where(ai & 0x80000000, 0x80000000 - ai, ai)
+    bi = np.where(bi & 0x80000000, 0x80000000 - bi, bi)
+    return np.abs(ai - bi)
+
+
+# ---------------------------------------------------------------- quantisation
+
+@pytest.mark.parametrize("case", ["normal", "zero", "tie", "wide", "signed_tie", "tiny"])
+def test_quantize_bitexact(cuda, cb, orc, case):
+    rng = np.random.default_rng(11)
+    k = 7168
+    if case == "normal":
+        x = rng.standard_normal(k).astype(np.float32)
+    elif case == "zero":
+        x = rng.standard_normal(k).astype(np.float32)
+        x[:512] = 0.0
+        x[700] = -0.0
+    elif case == "tie":
+        x = tie_probe(k)
+    elif case == "wide":
+        x = (rng.standard_normal(k) * np.exp(rng.uniform(-60, 60, k))).astype(np.float32)
+    elif case == "signed_tie":
+        x = rng.uniform(-1, 1, k).astype(np.float32)
+        for b in range(k // 256):  # equal magnitude, opposite sign: the first one sets d
+            x[256 * b + 3] = -2.0 if b % 2 else 2.0
+            x[256 * b + 200] = 2.0 if b % 2 else -2.0
+    else:
+        x = (rng.standard_normal(k) * 1e-40).astype(np.float32)  # subnormals
+    got = gpu_quantize(cuda, cb, x)
+    want = orc.quantize(x)
+    assert np.array_equal(got, want)
+
+
+# ---------------------------------------------------------------- row dots
+
+MV_SHAPES = [(1536, 7168), (7168, 1536), (33, 256), (5, 512), (31, 2304), (2304, 5120), (5120, 2304), (17, 768)]
+
+
+@pytest.mark.parametrize("qtype", TYPES)
+@pytest.mark.parametrize("n,k", MV_SHAPES)
+def test_mv_bitexact(cuda, cb, orc, qtype, n, k):
+    rng = np.random.default_rng(n * 131 + k + qtype)
+    w = orc.synth_matrix(qtype, 7 + n, 1, 3, 0, n, k)
+    x = rng.standard_normal(k).astype(np.float32)
+    q = orc.quantize(x)
+    got = gpu_mv(cuda, cb, qtype, w, q, n, k)
+    want = orc.mv(qtype, w, q, n, k)
+    assert np.array_equal(bits(got), bits(want)), f"{np.count_nonzero(bits(got) != bits(want))} rows differ"
+
+
+@pytest.mark.parametrize("qtype", TYPES)
+def test_mv_random_bytes_bitexact(cuda, cb, orc, qtype):
+    """Uniformly random block bytes (every grid index, sign, sub-scale, delta) with finite scales."""
+    rng = np.random.default_rng(qtype)
+    n, k = 96, 2048
+    bb = {16: 66, 17: 74, 29: 56}[qtype]
+    w = rng.integers(0, 256, n * (k // 256) * bb, dtype=np.uint8).reshape(-1, bb)
+    h = rng.integers(0, 0x7800, len(w)).astype(np.uint16)  # finite fp16 incl. subnormals, both signs
+    h |= (rng.integers(0, 2, len(w)) << 15).astype(np.uint16)
+    if qtype == 29:
+        for j in range(4):
+            word = (w[:, 48 + 2 * j].astype(np.uint16) | (w[:, 49 + 2 * j].astype(np.uint16) << 8)) & 0x0FFF
+            word |= ((h >> (4 * j)) & 15) << 12
+            w[:, 48 + 2 * j] = word & 255
+            w[:, 49 + 2 * j] = word >> 8
+    else:
+        w[:, 0] = h & 255
+        w[:, 1] = h >> 8
+    w = w.reshape(-1)
+    x = tie_probe(k) if qtype == 17 else rng.standard_normal(k).astype(np.float32) * 3
+    q = orc.quantize(x)
+    got = gpu_mv(cuda, cb, qtype, w, q, n, k)
+    want = orc.mv(qtype, w, q, n, k)
+    assert np.array_equal(bits(got), bits(want))
+
+
+def test_activate_ulps(cuda, cb, orc):
+    rng = np.random.default_rng(5)
+    n = 20000
+    g = (rng.standard_normal(n) * 6).astype(np.float32)
+    u = (rng.standard_normal(n) * 6).astype(np.float32)
+    for limit in (0.0, 10.0):
+        dg, du = dev(cuda, g), dev(cuda, u)
+        dh = cuda.zeros(n, dtype=cuda.float32, device="cuda")
+        cb.q8k_activate(dg, du, dh, limit)
+        cuda.cuda.synchronize()
+        got = dh.cpu().numpy()
+        want = orc.swiglu(g, u, limit)
+        assert ulp_diff(got, want).max() <= 2
+
+
+# ---------------------------------------------------------------- one expert, stage by stage
+
+@pytest.mark.parametrize("qtype", TYPES)
+@pytest.mark.parametrize("probe", ["data", "zero", "tie"])
+def test_expert_stage_chain(cuda, cb, orc, qtype, probe):
+    """crosslane engine/strata/warm/expert_check.cpp:78-101, on the B200 lane: every stage
+    is compared with the oracle given the same stage input."""
+    dim, ff = 7168, 1536
+    rng = np.random.default_rng(qtype)
+    x = {"data": rng.standard_normal(dim).astype(np.float32), "zero": np.zeros(dim, np.float32),
+         "tie": tie_probe(dim)}[probe]
+    gate = orc.synth_matrix(qtype, 99, 2, 5, 0, ff, dim)
+    up = orc.synth_matrix(qtype, 99, 2, 5, 1, ff, dim)
+    down = orc.synth_matrix(qtype, 99, 2, 5, 2, dim, ff)
+    qx = gpu_quantize(cuda, cb, x)
+    assert np.array_equal(qx, orc.quantize(x))
+    g = gpu_mv(cuda, cb, qtype, gate, qx, ff, dim)
+    u = gpu_mv(cuda, cb, qtype, up, qx, ff, dim)
+    assert np.array_equal(bits(g), bits(orc.mv(qtype, gate, qx, ff, dim)))
+    assert np.array_equal(bits(u), bits(orc.mv(qtype, up, qx, ff, dim)))
+    dh = cuda.zeros(ff, dtype=cuda.float32, device="cuda")
+    cb.q8k_activate(dev(cuda, g), dev(cuda, u), dh, 0.0)
+    cuda.cuda.synchronize()
+    h = dh.cpu().numpy()
+    assert ulp_diff(h, orc.swiglu(g, u)).max() <= 2
+    qh = gpu_quantize(cuda, cb, h)
+    assert np.array_equal(qh, orc.quantize(h))
+    y = gpu_mv(cuda, cb, qtype, down, qh, dim, ff)
+    assert np.array_equal(bits(y), bits(orc.mv(qtype, down, qh, dim, ff)))
+
+
+# ---------------------------------------------------------------- bank / layer
+
+def _route(orc, rng, n_experts, k):
+    logits = rng.standard_normal(n_experts).astype(np.float32)
+    return orc.route_sigmoid(logits, k)
+
+
+@pytest.fixture(scope="module")
+def bank_c1(cb):
+    """one layer, 384 IQ2_XXS experts, 7168 x 1536."""
+    b = cb.ExpertBank(n_layers=1, n_experts=384, dim=7168, ff=1536, max_picks=6)
+    b.fill_synthetic(1234, 0)
+    yield b
+    b.close()
+
+
+@pytest.fixture(scope="module")
+def bank_c2(cb):
+    """one layer, experts 0-127 IQ2_XXS, 128-255 IQ2_XS, 256-383 IQ1_M."""
+    b = cb.ExpertBank(n_layers=1, n_experts=384, dim=7168, ff=1536, max_picks=6)
+    b.fill_synthetic(4321, 1)
+    yield b
+    b.close()
+
+
+def test_config1_layer(bank_c1, orc):
+    rng = np.random.default_rng(1)
+    for trial in range(2):
+        ids, w = _route(orc, rng, 384, 6)
+        x = rng.standard_normal(7168).astype(np.float32)
+        got = bank_c1.layer_execute(0, ids, w, x)
+        want = orc.layer_synth(0, 1234, 0, ids, w, x, 7168, 1536)
+        assert rel_l2(got, want) <= REL_L2 and max_abs_rel(got, want) <= MAX_ABS_REL
+        print(f"config1 trial {trial}: rel_l2={rel_l2(got, want):.3e} exact={np.mean(bits(got) == bits(want)):.4f}")
+
+
+def test_config2_layer_mixed(bank_c2, orc):
+    rng = np.random.default_rng(2)
+    ids = np.array([5, 300, 140, 17, 383, 200], np.int32)  # all three quant types
+    w = rng.uniform(0.05, 0.3, 6).astype(np.float32)
+    w /= w.sum()
+    x = rng.standard_normal(7168).astype(np.float32)
+    shared = rng.standard_normal(7168).astype(np.float32) * 0.1
+    got = bank_c2.layer_execute(0, ids, w, x, shared)
+    want = orc.layer_synth(1, 4321, 0, ids, w, x, 7168, 1536, shared=shared)
+    assert rel_l2(got, want) <= REL_L2 and max_abs_rel(got, want) <= MAX_ABS_REL
+
+
+def test_compute_many_rows(bank_c2, orc):
+    rng = np.random.default_rng(3)
+    ids = [299, 1, 130]
+    x = rng.standard_normal(7168).astype(np.float32)
+    rows = bank_c2.warm_compute_many(0, ids, x)
+    for i, e in enumerate(ids):
+        t = orc.expert_type(1, 4321, 0, e)
+        gate = orc.synth_matrix(t, 4321, 0, e, 0, 1536, 7168)
+        up = orc.synth_matrix(t, 4321, 0, e, 1, 1536, 7168)
+        down = orc.synth_matrix(t, 4321, 0, e, 2, 7168, 1536)
+        _, want = orc.expert(t, gate, up, down, x, 7168, 1536)
+        assert rel_l2(rows[i], want) <= REL_L2 and max_abs_rel(rows[i], want) <= MAX_ABS_REL
+    single = bank_c2.warm_compute(0, 130, x)
+    assert np.array_equal(bits(single), bits(rows[2]))
+
+
+def test_reference_geometry_clamp(cb, orc):
+    """crosslane's own model geometry: dim 5120, ff 2304, SwiGLU clamp 10."""
+    b = cb.ExpertBank(n_layers=1, n_experts=12, dim=5120, ff=2304, max_picks=6, limit=10.0)
+    try:
+        b.fill_synthetic(77, 2)
+        rng = np.random.default_rng(4)
+        ids = np.array([11, 0, 7, 3, 9, 4], np.int32)
+        w = np.full(6, 1 / 6, np.float32)
+        x = (rng.standard_normal(5120) * 4).astype(np.float32)
+        got = b.layer_execute(0, ids, w, x)
+        want = orc.layer_synth(2, 77, 0, ids, w, x, 5120, 2304, limit=10.0)
+        assert rel_l2(got, want) <= REL_L2 and max_abs_rel(got, want) <= MAX_ABS_REL
+    finally:
+        b.close()
+
+
+def test_stack_decode_three_layers(cb, orc):
+    """Config 3 shape on 3 layers: mixed types per (layer, expert), h += layer(RMSNorm(h))."""
+    L, E = 3, 384
+    b = cb.ExpertBank(n_layers=L, n_experts=E, dim=7168, ff=1536, max_picks=6)
+    try:
+        b.fill_synthetic(2024, 2)
+        rng = np.random.default_rng(5)
+        x0 = rng.standard_normal(7168).astype(np.float32)
+        logits = rng.standard_normal((L, E)).astype(np.float32)
+        got = b.stack_decode(0, L, x0, logits)
+        got2 = b.stack_decode(0, L, x0, logits)  # replayed graph: run-to-run identical
+        assert np.array_equal(bits(got), bits(got2))
+        want = orc.stack(2, 2024, x0, logits, 7168, 1536)
+        assert np.all(np.isfinite(got))
+        assert rel_l2(got, want) <= REL_L2 and max_abs_rel(got, want) <= MAX_ABS_REL
+    finally:
+        b.close()
+
+
+def test_route_device_matches_host(cuda, cb, orc):
+    rng = np.random.default_rng(6)
+    T, E, k = 512, 384, 6
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    logits[7, 10] = logits[7, 20] = 9.0  # exact tie: lower id first
+    d_ids = cuda.zeros(T * k, dtype=cuda.int32, device="cuda")
+    d_w = cuda.zeros(T * k, dtype=cuda.float32, device="cuda")
+    cb.route_device(dev(cuda, logits), E, k, T, d_ids, d_w)
+    cuda.cuda.synchronize()
+    ids = d_ids.cpu().numpy().reshape(T, k)
+    w = d_w.cpu().numpy().reshape(T, k)
+    for t in range(T):
+        oi, ow = orc.route_sigmoid(logits[t], k)
+        hi, hw = cb.route_host(0, logits[t], k)
+        assert np.array_equal(ids[t], oi) and np.array_equal(hi, oi)
+        assert ulp_diff(w[t], ow).max() <= 4 and ulp_diff(hw, ow).max() <= 4
+    assert list(ids[7][:2]) == [10, 20]
+
+
+def test_warm_execute_two_lanes(cb, orc):
+    """Resident picks on the CUDA lane, the rest on a host lane; joined and combined in
+    ascending expert id (runtime.cpp:121-189)."""
+    E, dim, ff, seed, pol = 16, 2048, 512, 31, 2
+    b = cb.ExpertBank(n_layers=1, n_experts=E, dim=dim, ff=ff, max_picks=6, expert_begin=0, expert_end=8)
+    try:
+        b.fill_synthetic(seed, pol)
+        assert b.warm_contains(0, 3) and not b.warm_contains(0, 12)
+
+        def host_lane(layer, e, x):
+            t = orc.expert_type(pol, seed, layer, e)
+            g = orc.synth_matrix(t, seed, layer, e, 0, ff, dim)
+            u = orc.synth_matrix(t, seed, layer, e, 1, ff, dim)
+            d = orc.synth_matrix(t, seed, layer, e, 2, dim, ff)
+            return orc.expert(t, g, u, d, x, dim, ff)[1]
+
+        rng = np.random.default_rng(7)
+        ids = np.array([12, 3, 9, 0, 15, 6], np.int32)
+        w = rng.uniform(0.1, 0.2, 6).astype(np.float32)
+        x = rng.standard_normal(dim).astype(np.float32)
+        shared = rng.standard_normal(dim).astype(np.float32)
+        got = b.warm_execute(0, ids, w, x, shared, host_lane)
+        want = orc.layer_synth(pol, seed, 0, ids, w, x, dim, ff, shared=shared)
+        assert rel_l2(got, want) <= REL_L2 and max_abs_rel(got, want) <= MAX_ABS_REL
+
+        def failing_lane(layer, e, x):
+            raise RuntimeError("injected host-lane failure")
+
+        with pytest.raises(cb.ClbError) as ei:
+            b.warm_execute(0, ids, w, x, shared, failing_lane)
+        assert ei.value.code == 7  # CLB_E_LANE, raised after both lanes drained
+        again = b.warm_execute(0, ids, w, x, shared, host_lane)  # bank still healthy
+        assert np.array_equal(bits(again), bits(got))
+    finally:
+        b.close()
+
+
+def test_errors_do_not_poison(cb, bank_c1):
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal(7168).astype(np.float32)
+    with pytest.raises(cb.ClbError) as e1:
+        bank_c1.layer_execute(0, [1, 1, 2, 3, 4, 5], np.full(6, 1 / 6, np.float32), x)
+    assert e1.value.code == 1
+    with pytest.raises(cb.ClbError) as e2:
+        bank_c1.layer_execute(0, [1, 2, 3, 4, 5, 384], np.full(6, 1 / 6, np.float32), x)
+    assert e2.value.code == 1
+    bad = x.copy()
+    bad[17] = np.nan
+    with pytest.raises(cb.ClbError) as e3:
+        bank_c1.warm_compute(0, 3, bad)
+    assert e3.value.code == 5
+    y = bank_c1.warm_compute(0, 3, x)
+    assert np.all(np.isfinite(y))
