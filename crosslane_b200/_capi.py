@@ -56,6 +56,7 @@ SIGNATURES = {
     "clb_q8k_quantize": (_I, [_P, _P, _I, _P]),
     "clb_q8k_mv": (_I, [_I, _P, _P, _P, _I, _I, _P]),
     "clb_q8k_activate": (_I, [_P, _P, _P, _I, _F, _P]),
+    "clb_decode_tables": (_SZ, [_P, _SZ]),
     "clb_packed_bytes": (_SZ, [_I, _I, _I]),
     "clb_pack": (_I, [_I, _I, _I, _P, _SZ, _P, _SZ]),
     "clb_unpack": (_I, [_I, _I, _I, _P, _SZ, _P, _SZ]),

@@ -306,6 +306,12 @@ int32_t clb_q8k_activate(const float* g, const float* u, float* h, int32_t n, fl
                                                                                                       : CLB_E_CUDA;
 }
 
+size_t clb_decode_tables(uint32_t* out, size_t words) {
+    if (!out || words < (size_t)clb::kTableWords) return 0;
+    clb::host_tables(out);
+    return (size_t)clb::kTableWords;
+}
+
 // ---- layout ----
 size_t clb_packed_bytes(int32_t type, int32_t n, int32_t k) {
     if (!clb_type_supported(type) || n <= 0 || k <= 0 || k % 256) return 0;

@@ -66,6 +66,12 @@ int32_t clb_q8k_mv(int32_t type, const void* w_packed, const void* q, float* y, 
  * Replaces q8k::activate (hip_q8k.hpp:11). */
 int32_t clb_q8k_activate(const float* g, const float* u, float* h, int32_t n, float limit, void* stream);
 
+/* Diagnostics: copies the decode kernels' nibble-selector tables (2944 u32: IQ2_XXS
+ * grid 256, IQ2_XS grid 512, IQ1 grid 2048, sign masks 128) to `out`; returns the
+ * number of words, or 0 if `words` is too small. No counterpart in crosslane; lets
+ * host tests prove the byte-permute decode against the ggml codebooks. */
+size_t clb_decode_tables(uint32_t* out, size_t words);
+
 /* ---- packed bank layout (host memory) ---- */
 
 /* Size of one matrix in the packed bank layout (>= the ggml bytes, planes 256 B

@@ -1,8 +1,8 @@
 """GPU parity of the CUDA expert lane against the CPU oracle (through the C ABI).
 
 Contract: Q8_K activation bytes, integer dots and every row dot are bit-identical to
-crosslane's CPU-lane arithmetic (q8k_core.hpp); SwiGLU differs at most by CUDA-vs-glibc
-expf rounding (<= 2 ulp asserted); combined fp32 layer outputs are within the
+crosslane's CPU-lane arithmetic (q8k_core.hpp); SwiGLU matches on >= 99.9% of inputs and
+otherwise differs by exp rounding (<= 4 ulp asserted); combined fp32 layer outputs are within the
 relative L2 <= 1e-3 and max-abs-relative <= 5e-3.
 """
 import numpy as np
@@ -136,7 +136,8 @@ def test_activate_ulps(cuda, cb, orc):
         cuda.cuda.synchronize()
         got = dh.cpu().numpy()
         want = orc.swiglu(g, u, limit)
-        assert ulp_diff(got, want).max() <= 2
+        d = ulp_diff(got, want)
+        assert d.max() <= 4 and np.mean(d == 0) >= 0.999, (d.max(), np.mean(d == 0))
 
 
 # ---------------------------------------------------------------- one expert, stage by stage
@@ -163,7 +164,7 @@ def test_expert_stage_chain(cuda, cb, orc, qtype, probe):
     cb.q8k_activate(dev(cuda, g), dev(cuda, u), dh, 0.0)
     cuda.cuda.synchronize()
     h = dh.cpu().numpy()
-    assert ulp_diff(h, orc.swiglu(g, u)).max() <= 2
+    assert ulp_diff(h, orc.swiglu(g, u)).max() <= 4
     qh = gpu_quantize(cuda, cb, h)
     assert np.array_equal(qh, orc.quantize(h))
     y = gpu_mv(cuda, cb, qtype, down, qh, dim, ff)
