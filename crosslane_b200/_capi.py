@@ -79,6 +79,7 @@ SIGNATURES = {
     "clb_bank_stream": (_P, [_P]),
     "clb_bank_synchronize": (_I, [_P, _PE]),
     "clb_warm_execute": (_I, [_P, _U32, _P, _P, _I, _P, _P, HOST_EXPERT_FN, _P, _P, _PE]),
+    "clb_expert_forward_noalloc": (_I, [_I, _P, _P, _P, _P, _P, _I, _I, _F, _P, _PE]),
 }
 
 

@@ -52,6 +52,11 @@ cudaError_t upload_tables(cudaStream_t stream) {
     return cudaStreamSynchronize(stream);
 }
 
+// Device address of the selector tables, for kernels compiled in other translation units.
+cudaError_t tables_device_ptr(const uint32_t** out) {
+    return cudaGetSymbolAddress(reinterpret_cast<void**>(const_cast<uint32_t**>(out)), g_tables);
+}
+
 __device__ __forceinline__ Tables load_tables(uint32_t* smem) {
     for (int i = threadIdx.x; i < kTableWords; i += blockDim.x) smem[i] = g_tables[i];
     Tables tb;

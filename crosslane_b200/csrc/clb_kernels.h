@@ -23,6 +23,7 @@ struct ExpertDesc {
 
 void host_tables(uint32_t* out /* kTableWords */);
 cudaError_t upload_tables(cudaStream_t stream);
+cudaError_t tables_device_ptr(const uint32_t** out);
 cudaError_t set_smem_limits();
 size_t mv_smem(int k);
 size_t gateup_smem(int dim);

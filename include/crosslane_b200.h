@@ -198,6 +198,25 @@ int32_t clb_stack_decode_device(clb_bank* bank, uint32_t first_layer, int32_t n_
 void* clb_bank_stream(clb_bank* bank);
 int32_t clb_bank_synchronize(clb_bank* bank, clb_error_v1* err);
 
+/* ---- one expert without any allocation ---- */
+
+/* y[dim] = down(swiglu(gate(x), up(x))) for one expert whose three matrices are given
+ * in the packed layout (device pointers w_gate/w_up [ff, dim], w_down [dim, ff]); x and y
+ * are device buffers; runs on `stream` and returns without synchronising.
+ * No counterpart in crosslane. For callers that cannot call cudaMalloc (a decode step
+ * being captured into a CUDA graph, a serving loop that must not risk an allocation's
+ * implicit device synchronisation, a plugin whose device memory belongs to another
+ * allocator): the quantised input, hidden vector and its quantisation live in one fixed
+ * 57,728-byte array inside the library, held by every GPU that loads it until exit.
+ * Limits: dim <= 16384, ff <= 8192 (else CLB_E_UNSUPPORTED with a message). It calls no
+ * cudaMalloc/cudaFree. The first call on a device resolves that array's address and
+ * uploads the decode tables (a synchronising step): make it before any stream capture.
+ * All calls share the array, so calls that overlap on the GPU (other streams, other
+ * threads) race; serialise them on one stream. Results equal clb_bank_compute's. */
+int32_t clb_expert_forward_noalloc(int32_t type, const void* w_gate, const void* w_up, const void* w_down,
+                                   const float* x, float* y, int32_t dim, int32_t ff, float limit, void* stream,
+                                   clb_error_v1* err);
+
 /* ---- warm_execute: the three-lane join with this bank as the GPU lane ---- */
 
 /* Host lane callback: compute y[dim] of one non-resident expert (crosslane's
