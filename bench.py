@@ -280,7 +280,6 @@ def main():
             evs[0].record(stream)
             bank.layer_phases_device(layer, d_ids, d_w, d_x, d_out, 2, stream=bank.stream)
             evs[1].record(stream)
-            bank.layer_phases_device(layer, d_ids, d_w, d_x, d_out, 4, stream=bank.stream)
             evs[2].record(stream)
             bank.layer_phases_device(layer, d_ids, d_w, d_x, d_out, 8, stream=bank.stream)
             evs[3].record(stream)
@@ -293,18 +292,18 @@ def main():
                 per = payload // 3  # gate, up and down carry the same number of weights
                 gu_bytes += 2 * per
                 dn_bytes += per
-            gu_bytes += DIM + 4 * (DIM // 256) + 4 * PICKS * FF
-            dn_bytes += PICKS * FF + 4 * PICKS * (FF // 256) + 4 * DIM
+            gu_bytes += DIM + 4 * (DIM // 256) + PICKS * FF + 4 * PICKS * (FF // 256)  # Q8_K(x) in, Q8_K(h) out
+            dn_bytes += PICKS * FF + 4 * PICKS * (FF // 256) + 8 * DIM  # Q8_K(h) in, residual in, out
     gu_avg_s = gu_ms / 1e3 / launches_timed
     gu_achieved = gu_bytes / launches_timed / gu_avg_s / 1e9
     dn_achieved = dn_bytes / launches_timed / (dn_ms / 1e3 / launches_timed) / 1e9
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "k_gateup_traffic.json")
+    tp = os.path.join(ROOT, "profiles", "k_gateup2_traffic.json")
     if os.path.exists(tp):
         with open(tp) as f:
             traffic = json.load(f).get("bytes_per_launch")
     roofline = {"bound": "hbm", "achieved": round(gu_achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(gu_achieved / peak, 4), "traffic": traffic, "kernel": "clb::k_gateup",
+                "frac": round(gu_achieved / peak, 4), "traffic": traffic, "kernel": "clb::k_gateup2",
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6650 GB/s",
                 "algorithmic_bytes_per_launch": int(gu_bytes / launches_timed),
@@ -338,7 +337,7 @@ def main():
         "step_hbm_gbs": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
         "cpu_baseline": cpu,
         "clocks": clk,
-        "gpu_launches": (1 + 4 * L) * args.steps,
+        "gpu_launches": (1 + 3 * L) * args.steps,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

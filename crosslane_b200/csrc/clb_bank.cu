@@ -94,6 +94,7 @@ void ensure_device_ready(int dev, cudaStream_t s) {
     if (g_dev_ready.count(dev)) return;
     cuda_check(clb::upload_tables(s), "upload codebook tables");
     cuda_check(clb::set_smem_limits(), "kernel shared-memory limits");
+    cuda_check(clb::set_v2_smem_limits(), "kernel shared-memory limits");
     g_dev_ready.insert(dev);
 }
 
@@ -124,6 +125,9 @@ struct clb_bank {
     float *d_xd = nullptr, *d_hd = nullptr;
     int* d_ids = nullptr;
     int* d_err = nullptr;
+    float* d_gu = nullptr;          // gate/up rows [pick][2][ff]
+    int* d_cnt_h = nullptr;         // last-arriver counters per (pick, 256-row block of h)
+    int* d_cnt_y = nullptr;         // last-arriver counters per 32-row output group
     float* d_logits = nullptr;
     int* d_route_ids = nullptr;
     float* d_route_w = nullptr;
@@ -200,10 +204,11 @@ struct clb_bank {
             cuda_check(clb::launch_norm_quant(x, dim, d_xqs, d_xd, nullptr, s), "norm + quantize x");
         else
             cuda_check(clb::launch_quant(x, dim / 256, d_xqs, d_xd, s), "quantize x");
-        cuda_check(clb::launch_gateup(ex, ids, n, d_xqs, d_xd, dim, ff, cfg.limit, d_h, d_err, s), "gate/up");
-        cuda_check(clb::launch_quant(d_h, n * ff / 256, d_hqs, d_hd, s), "quantize h");
-        cuda_check(clb::launch_down_combine(ex, ids, w, n, d_hqs, d_hd, dim, ff, shared, resid, out, yrows, d_err, s),
-                   "down/combine");
+        cuda_check(clb::launch_gateup2(ex, ids, n, d_xqs, d_xd, dim, ff, cfg.limit, d_gu, d_hqs, d_hd, d_cnt_h, d_err, s),
+                   "gate/up + SwiGLU + quantize h");
+        cuda_check(clb::launch_down2(ex, ids, w, n, d_hqs, d_hd, dim, ff, shared, resid, out, yrows ? yrows : d_yrows,
+                                     d_cnt_y, d_err, s),
+                   "down + combine");
     }
 
     void enqueue_phases(uint32_t layer, const int* ids, const float* w, int n, const float* x, float* out, int mask,
@@ -212,12 +217,13 @@ struct clb_bank {
         const clb::ExpertDesc* ex = d_desc + (size_t)layer * E();
         if (mask & 1) cuda_check(clb::launch_quant(x, dim / 256, d_xqs, d_xd, s), "quantize x");
         if (mask & 2)
-            cuda_check(clb::launch_gateup(ex, ids, n, d_xqs, d_xd, dim, ff, cfg.limit, d_h, d_err, s), "gate/up");
-        if (mask & 4) cuda_check(clb::launch_quant(d_h, n * ff / 256, d_hqs, d_hd, s), "quantize h");
+            cuda_check(clb::launch_gateup2(ex, ids, n, d_xqs, d_xd, dim, ff, cfg.limit, d_gu, d_hqs, d_hd, d_cnt_h, d_err,
+                                           s),
+                       "gate/up + SwiGLU + quantize h");
         if (mask & 8)
-            cuda_check(clb::launch_down_combine(ex, ids, w, n, d_hqs, d_hd, dim, ff, nullptr, nullptr, out, nullptr,
-                                                d_err, s),
-                       "down/combine");
+            cuda_check(clb::launch_down2(ex, ids, w, n, d_hqs, d_hd, dim, ff, nullptr, nullptr, out, d_yrows, d_cnt_y,
+                                         d_err, s),
+                       "down + combine");
     }
 
     void enqueue_stack(uint32_t first, int nl, float* dx, const float* dlogits, cudaStream_t s) {
@@ -297,7 +303,7 @@ int32_t clb_q8k_mv(int32_t type, const void* w, const void* q, float* y, int32_t
     m.type = type;
     m.n = n;
     m.k = k;
-    return clb::launch_mv(m, q, y, static_cast<cudaStream_t>(stream)) == cudaSuccess ? CLB_OK : CLB_E_CUDA;
+    return clb::launch_mv2(m, q, y, static_cast<cudaStream_t>(stream)) == cudaSuccess ? CLB_OK : CLB_E_CUDA;
 }
 
 int32_t clb_q8k_activate(const float* g, const float* u, float* h, int32_t n, float limit, void* stream) {
@@ -367,7 +373,8 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         require(std::isfinite(cfg.limit) && cfg.limit >= 0, CLB_E_INVALID, "SwiGLU limit must be finite and >= 0");
         require(cfg.expert_begin >= 0 && cfg.expert_begin < cfg.expert_end && cfg.expert_end <= cfg.n_experts,
                 CLB_E_INVALID, "owned expert range invalid");
-        require((size_t)cfg.max_picks * cfg.ff <= 65536 * 2, CLB_E_UNSUPPORTED, "max_picks * ff too large");
+        require((size_t)cfg.max_picks * (cfg.ff / 256) <= 256, CLB_E_UNSUPPORTED,
+                "max_picks * ff / 256 must be <= 256 (the down kernel stages every pick's Q8_K(h) in shared memory)");
         int ndev = 0;
         cuda_check(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
         require(cfg.device >= 0 && cfg.device < ndev, CLB_E_INVALID, "device %d not present", cfg.device);
@@ -389,6 +396,11 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         bank->d_hqs = bank->dev_alloc<int8_t>(k * ff);
         bank->d_hd = bank->dev_alloc<float>(k * ff / 256);
         bank->d_yrows = bank->dev_alloc<float>(k * dim);
+        bank->d_gu = bank->dev_alloc<float>(k * 2 * ff);
+        bank->d_cnt_h = bank->dev_alloc<int>(k * ff / 256);
+        bank->d_cnt_y = bank->dev_alloc<int>((dim + 31) / 32);
+        cuda_check(cudaMemsetAsync(bank->d_cnt_h, 0, sizeof(int) * k * ff / 256, bank->stream), "memset");
+        cuda_check(cudaMemsetAsync(bank->d_cnt_y, 0, sizeof(int) * ((dim + 31) / 32), bank->stream), "memset");
         bank->d_ids = bank->dev_alloc<int>(k);
         bank->d_w = bank->dev_alloc<float>(k);
         bank->d_err = bank->dev_alloc<int>(1);

@@ -112,13 +112,14 @@ template <int T>
 __device__ __forceinline__ void decode_group(const RowBlock& rb, int c, int t, const Tables& tb, uint32_t& lo,
                                              uint32_t& hi, int& scale, int& delta) {
     if (T == CLB_IQ2_XXS) {
-        const uint32_t gw = word_of(rb.body, 2 * c), aux = word_of(rb.body, 2 * c + 1);
+        // packed chunk: [4 grid bytes][4 sign bytes, bit 7 of byte j = sub-scale bit j]
+        const uint32_t gw = word_of(rb.body, 2 * c), sw = word_of(rb.body, 2 * c + 1);
         const uint32_t gi = (gw >> (8 * t)) & 0xffu;
-        const uint32_t si = (aux >> (7 * t)) & 0x7fu;
+        const uint32_t si = (sw >> (8 * t)) & 0x7fu;
         const uint32_t sel = tb.xxs[gi] | tb.sign[si];
         lo = prmt(kIq2Pos, kIq2Neg, sel);
         hi = prmt(kIq2Pos, kIq2Neg, sel >> 16);
-        scale = (int)((aux >> 28) << 1) | 1;
+        scale = (int)((((sw & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27);
         delta = 0;
     } else if (T == CLB_IQ2_XS) {
         const uint32_t w = word_of(rb.body, 2 * c + (t >> 1));

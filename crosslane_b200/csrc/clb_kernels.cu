@@ -2,6 +2,8 @@
 // arithmetic contract and clb_types.h for the packed weight layout.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "clb_device.cuh"
 #include "clb_kernels.h"
 #include "clb_pack.h"
@@ -398,6 +400,356 @@ cudaError_t launch_pack(const uint8_t* aos, uint8_t* packed, const PackedLayout&
     const size_t total = (size_t)n * (k >> 8);
     const int grid = (int)((total + 255) / 256 < 148 * 32 ? (total + 255) / 256 : 148 * 32);
     k_pack<<<grid, 256, 0, s>>>(aos, packed, l, type, n, k, bad);
+    return cudaGetLastError();
+}
+
+}  // namespace clb
+
+// ==============================================================================
+// v2: row-per-thread decode (clb_rowdot.cuh), persistent CTAs, fused epilogues.
+// ==============================================================================
+#include "clb_rowdot.cuh"
+
+namespace clb {
+
+constexpr int kV2Threads = 512;          // 16 warps per CTA, one CTA per SM
+constexpr int kV2Warps = kV2Threads / 32;
+constexpr int kActStride = 272;          // padded Q8_K block stride in shared memory
+constexpr int kXchWords = 18;            // per (row, block-slot) exchange record
+
+// Q8_K of 256 values held 8 per lane (lane i holds values 8i..8i+7), as warp_quant_block.
+__device__ __forceinline__ void warp_quant_regs(float v[8], int8_t* qs, float* d) {
+    const int lane = threadIdx.x & 31;
+    float am = 0.0f;
+    int ai = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float a = fabsf(v[i]);
+        if (a > am) { am = a; ai = lane * 8 + i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, am, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, ai, o);
+        if (oa > am || (oa == am && oi < ai)) { am = oa; ai = oi; }
+    }
+    if (am == 0.0f) {
+        *reinterpret_cast<uint2*>(qs + lane * 8) = make_uint2(0u, 0u);
+        if (lane == 0) *d = 0.0f;
+        return;
+    }
+    float mine = v[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i)
+        if ((ai & 7) == i) mine = v[i];
+    const float mx = __shfl_sync(0xffffffffu, mine, (ai >> 3) & 31);
+    const float is = __fdiv_rn(-127.0f, mx);
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float z = __fadd_rn(__fmul_rn(is, v[i]), 12582912.0f);
+        int r = (int)(__float_as_uint(z) & 0x007fffffu) - 0x00400000;
+        r = r < 127 ? r : 127;
+        packed[i >> 2] |= ((uint32_t)(uint8_t)(int8_t)r) << (8 * (i & 3));
+    }
+    *reinterpret_cast<uint2*>(qs + lane * 8) = make_uint2(packed[0], packed[1]);
+    if (lane == 0) *d = __fdiv_rn(1.0f, is);
+}
+
+// Gate/up item for one warp: 8 rows of one matrix; 4 threads per row split the blocks
+// (thread k takes blocks k, k+4, ...). Per round the 4 threads exchange their blocks'
+// lane integers through shared memory so that thread k folds lanes 2k, 2k+1 of all 4
+// blocks in block order, exactly the reference chain. Returns the row value in k == 0.
+template <int T>
+__device__ __forceinline__ float quad_row_dot(const PackedMat& m, int row, const int8_t* act_qs, const float* act_d,
+                                              uint32_t tab, uint32_t* xch) {
+    const int lane = threadIdx.x & 31, k = lane & 3, rr = lane >> 2;
+    const uint32_t lb = (uint32_t)lane * 4u;
+    const int nb = m.k >> 8;
+    const int rounds = (nb + 3) >> 2;
+    float acc0 = 0.0f, acc1 = 0.0f, dacc0 = 0.0f, dacc1 = 0.0f;
+    RowRaw cur, nxt;
+    if (k < nb) load_raw<T>(m, row, k, cur);
+    for (int i = 0; i < rounds; ++i) {
+        const int b = 4 * i + k;
+        const bool have = b < nb;
+        if (b + 4 < nb) load_raw<T>(m, row, b + 4, nxt);
+        int I[8], D[8];
+        float dd = 0.0f;
+        if (have) {
+            block_lanes<T>(cur, act_qs + (size_t)b * kActStride, tab, lb, I, D);
+            dd = __fmul_rn(raw_scale<T>(cur), act_d[b]);
+        } else {
+#pragma unroll
+            for (int L = 0; L < 8; ++L) I[L] = D[L] = 0;
+        }
+        uint32_t* mine = xch + (rr * 4 + k) * kXchWords;
+#pragma unroll
+        for (int L = 0; L < 8; ++L) mine[L] = (uint32_t)I[L];
+        mine[8] = __float_as_uint(dd);
+        if (T == CLB_IQ1_M) {
+#pragma unroll
+            for (int L = 0; L < 8; ++L) mine[9 + L] = (uint32_t)D[L];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            if (4 * i + s < nb) {
+                const uint32_t* src = xch + (rr * 4 + s) * kXchWords;
+                const float ds = __uint_as_float(src[8]);
+                acc0 = __fmaf_rn(ds, (float)(int)src[2 * k], acc0);
+                acc1 = __fmaf_rn(ds, (float)(int)src[2 * k + 1], acc1);
+                if (T == CLB_IQ1_M) {
+                    dacc0 = __fmaf_rn(ds, (float)(int)src[9 + 2 * k], dacc0);
+                    dacc1 = __fmaf_rn(ds, (float)(int)src[9 + 2 * k + 1], dacc1);
+                }
+            }
+        }
+        __syncwarp();
+        if (b + 4 < nb) cur = nxt;
+    }
+    const float main = quad_hsum(acc0, acc1);
+    if (T == CLB_IQ1_M) return __fadd_rn(main, __fmul_rn(0.125f, quad_hsum(dacc0, dacc1)));
+    return __fmul_rn(0.125f, main);
+}
+
+// One thread = one row over all blocks; the 8 lane chains stay in registers.
+template <int T>
+__device__ __forceinline__ float thread_row_dot(const PackedMat& m, int row, const int8_t* act_qs, const float* act_d,
+                                                uint32_t tab) {
+    const uint32_t lb = (uint32_t)(threadIdx.x & 31) * 4u;
+    const int nb = m.k >> 8;
+    float acc[8], dacc[8];
+#pragma unroll
+    for (int L = 0; L < 8; ++L) acc[L] = dacc[L] = 0.0f;
+    RowRaw cur, nxt;
+    load_raw<T>(m, row, 0, cur);
+    for (int b = 0; b < nb; ++b) {
+        if (b + 1 < nb) load_raw<T>(m, row, b + 1, nxt);
+        int I[8], D[8];
+        block_lanes<T>(cur, act_qs + (size_t)b * kActStride, tab, lb, I, D);
+        const float dd = __fmul_rn(raw_scale<T>(cur), act_d[b]);
+#pragma unroll
+        for (int L = 0; L < 8; ++L) {
+            acc[L] = __fmaf_rn(dd, (float)I[L], acc[L]);
+            if (T == CLB_IQ1_M) dacc[L] = __fmaf_rn(dd, (float)D[L], dacc[L]);
+        }
+        if (b + 1 < nb) cur = nxt;
+    }
+    const float main = hsum8_rn(acc);
+    if (T == CLB_IQ1_M) return __fadd_rn(main, __fmul_rn(0.125f, hsum8_rn(dacc)));
+    return __fmul_rn(0.125f, main);
+}
+
+__device__ __forceinline__ float quad_row_dot_any(const PackedMat& m, int row, const int8_t* aq, const float* ad,
+                                                  uint32_t tab, uint32_t* xch) {
+    if (m.type == CLB_IQ2_XXS) return quad_row_dot<CLB_IQ2_XXS>(m, row, aq, ad, tab, xch);
+    if (m.type == CLB_IQ2_XS) return quad_row_dot<CLB_IQ2_XS>(m, row, aq, ad, tab, xch);
+    return quad_row_dot<CLB_IQ1_M>(m, row, aq, ad, tab, xch);
+}
+__device__ __forceinline__ float thread_row_dot_any(const PackedMat& m, int row, const int8_t* aq, const float* ad,
+                                                    uint32_t tab) {
+    if (m.type == CLB_IQ2_XXS) return thread_row_dot<CLB_IQ2_XXS>(m, row, aq, ad, tab);
+    if (m.type == CLB_IQ2_XS) return thread_row_dot<CLB_IQ2_XS>(m, row, aq, ad, tab);
+    return thread_row_dot<CLB_IQ1_M>(m, row, aq, ad, tab);
+}
+
+// Shared-memory copy of Q8_K activations (qs int8 + d floats, from global) with the
+// padded block stride.
+__device__ __forceinline__ void stage_act(const int8_t* __restrict__ qs, const float* __restrict__ d, int nblocks,
+                                          int8_t* aq, float* ad) {
+    for (int i = threadIdx.x; i < nblocks * 16; i += blockDim.x) {
+        const int b = i >> 4, p = i & 15;
+        *reinterpret_cast<uint4*>(aq + (size_t)b * kActStride + 16 * p) =
+            reinterpret_cast<const uint4*>(qs + (size_t)b * 256)[p];
+    }
+    for (int b = threadIdx.x; b < nblocks; b += blockDim.x) ad[b] = d[b];
+}
+
+// ------------------------------------------------------------------------------
+// Gate + up for all picks (one warp item = 8 rows of one matrix of one pick), then,
+// in the last warp to finish each 256-row block of a pick, SwiGLU and Q8_K(h).
+__global__ void __launch_bounds__(kV2Threads, 1)
+    k_gateup2(const ExpertDesc* __restrict__ experts, const int* __restrict__ ids, int npick,
+              const int8_t* __restrict__ xqs, const float* __restrict__ xd, int dim, int ff, float limit,
+              float* __restrict__ gu, int8_t* __restrict__ hqs, float* __restrict__ hd, int* __restrict__ counters,
+              int* __restrict__ err) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int nbx = dim >> 8;
+    int8_t* aq = reinterpret_cast<int8_t*>(smem + kRowTableBytes);
+    float* ad = reinterpret_cast<float*>(smem + kRowTableBytes + (size_t)nbx * kActStride);
+    uint32_t* xch_all = reinterpret_cast<uint32_t*>(smem + kRowTableBytes + (size_t)nbx * kActStride + 4 * nbx);
+    fill_row_tables(g_tables, smem);
+    stage_act(xqs, xd, nbx, aq, ad);
+    __syncthreads();
+    const uint32_t tab = smem_u32(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint32_t* xch = xch_all + warp * 32 * kXchWords;
+    const int groups = ff >> 3;                       // 8-row groups per matrix
+    const int items = npick * 2 * groups;
+    const int hblocks = ff >> 8;
+    for (int it = blockIdx.x * kV2Warps + warp; it < items; it += gridDim.x * kV2Warps) {
+        const int pick = it / (2 * groups), rem = it % (2 * groups);
+        const int group = rem >> 1, mat = rem & 1;       // gate/up of the same rows are adjacent
+        const ExpertDesc& ex = experts[ids[pick]];
+        const PackedMat& m = mat ? ex.up : ex.gate;
+        const int row = group * 8 + (lane >> 2);
+        float y = 0.0f;
+        if (m.body != nullptr && m.k == dim && m.n == ff) y = quad_row_dot_any(m, row, aq, ad, tab, xch);
+        else if (lane == 0) atomicExch(err, 1);
+        if ((lane & 3) == 0) gu[((size_t)pick * 2 + mat) * ff + row] = y;
+        // last arriver of this (pick, 256-row block) applies SwiGLU and quantises h
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        const int ci = pick * hblocks + (group >> 5);
+        if (lane == 0) last = atomicAdd(&counters[ci], 1) == 63;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __threadfence();
+            const int hb = group >> 5;
+            const float* g = gu + ((size_t)pick * 2) * ff + hb * 256;
+            const float* u = gu + ((size_t)pick * 2 + 1) * ff + hb * 256;
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = swiglu(__ldcg(g + lane * 8 + i), __ldcg(u + lane * 8 + i), limit);
+            warp_quant_regs(v, hqs + (size_t)pick * ff + hb * 256, hd + pick * hblocks + hb);
+            if (lane == 0) counters[ci] = 0;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------
+// Down projection (one warp item = 32 rows of one pick, one thread per row), then, in
+// the last warp to finish each 32-row group, the ascending-id fma combine
+// (runtime.cpp:184-187), + shared, + residual.
+__global__ void __launch_bounds__(kV2Threads, 1)
+    k_down2(const ExpertDesc* __restrict__ experts, const int* __restrict__ ids, const float* __restrict__ wts, int npick,
+            const int8_t* __restrict__ hqs, const float* __restrict__ hd, int dim, int ff,
+            const float* __restrict__ shared, const float* __restrict__ resid, float* __restrict__ out,
+            float* __restrict__ yrows, int* __restrict__ counters, int* __restrict__ err) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int nbh = ff >> 8;
+    int8_t* aq = reinterpret_cast<int8_t*>(smem + kRowTableBytes);
+    float* ad = reinterpret_cast<float*>(smem + kRowTableBytes + (size_t)npick * nbh * kActStride);
+    fill_row_tables(g_tables, smem);
+    stage_act(hqs, hd, npick * nbh, aq, ad);
+    __syncthreads();
+    const uint32_t tab = smem_u32(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int groups = (dim + 31) >> 5;
+    const int items = npick * groups;
+    for (int it = blockIdx.x * kV2Warps + warp; it < items; it += gridDim.x * kV2Warps) {
+        const int group = it / npick, pick = it % npick;
+        const PackedMat& m = experts[ids[pick]].down;
+        const int row = group * 32 + lane;
+        const int rowc = row < dim ? row : dim - 1;
+        float y = 0.0f;
+        if (m.body != nullptr && m.k == ff && m.n == dim)
+            y = thread_row_dot_any(m, rowc, aq + (size_t)pick * nbh * kActStride, ad + pick * nbh, tab);
+        else if (lane == 0) atomicExch(err, 1);
+        if (row < dim) yrows[(size_t)pick * dim + row] = y;
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&counters[group], 1) == npick - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last && row < dim) {
+            __threadfence();
+            float acc = 0.0f;
+            int prev = -1;
+            for (int o = 0; o < npick; ++o) {
+                int best = -1;
+                for (int p = 0; p < npick; ++p)
+                    if (ids[p] > prev && (best < 0 || ids[p] < ids[best])) best = p;
+                if (best < 0) break;
+                prev = ids[best];
+                acc = __fmaf_rn(wts[best], __ldcg(yrows + (size_t)best * dim + row), acc);
+            }
+            if (shared) acc = __fadd_rn(acc, shared[row]);
+            if (resid) acc = __fadd_rn(resid[row], acc);
+            out[row] = acc;
+        }
+        if (last && lane == 0) counters[group] = 0;
+    }
+}
+
+// ------------------------------------------------------------------------------
+// y[n] = W . q for one packed matrix (crosslane q8k::Block input), one thread per row.
+__global__ void __launch_bounds__(kV2Threads, 1) k_mv2(PackedMat m, const uint8_t* __restrict__ q, float* __restrict__ y) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int nb = m.k >> 8;
+    int8_t* aq = reinterpret_cast<int8_t*>(smem + kRowTableBytes);
+    float* ad = reinterpret_cast<float*>(smem + kRowTableBytes + (size_t)nb * kActStride);
+    fill_row_tables(g_tables, smem);
+    for (int i = threadIdx.x; i < nb * 64; i += blockDim.x) {
+        const int b = i >> 6, w = i & 63;
+        reinterpret_cast<uint32_t*>(aq + (size_t)b * kActStride)[w] =
+            *reinterpret_cast<const uint32_t*>(q + (size_t)b * kQ8KBlockBytes + 4 + 4 * w);
+    }
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) ad[b] = *reinterpret_cast<const float*>(q + (size_t)b * kQ8KBlockBytes);
+    __syncthreads();
+    const uint32_t tab = smem_u32(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int groups = (m.n + 31) >> 5;
+    for (int g = blockIdx.x * kV2Warps + warp; g < groups; g += gridDim.x * kV2Warps) {
+        const int row = g * 32 + lane;
+        const float v = thread_row_dot_any(m, row < m.n ? row : m.n - 1, aq, ad, tab);
+        if (row < m.n) y[row] = v;
+    }
+}
+
+size_t gateup2_smem(int dim) {
+    return kRowTableBytes + (size_t)(dim >> 8) * kActStride + 4 * (size_t)(dim >> 8) +
+           (size_t)kV2Warps * 32 * kXchWords * 4 + 16;
+}
+size_t down2_smem(int npick, int ff) {
+    return kRowTableBytes + (size_t)npick * (ff >> 8) * (kActStride + 4) + 16;
+}
+size_t mv2_smem(int k) { return kRowTableBytes + (size_t)(k >> 8) * (kActStride + 4) + 16; }
+
+static int g_num_sms = 0;
+static int num_sms() {
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    return g_num_sms;
+}
+
+cudaError_t set_v2_smem_limits() {
+    cudaError_t e;
+    const int lim = 227 * 1024;
+    if ((e = cudaFuncSetAttribute(k_gateup2, cudaFuncAttributeMaxDynamicSharedMemorySize, lim))) return e;
+    if ((e = cudaFuncSetAttribute(k_down2, cudaFuncAttributeMaxDynamicSharedMemorySize, lim))) return e;
+    if ((e = cudaFuncSetAttribute(k_mv2, cudaFuncAttributeMaxDynamicSharedMemorySize, lim))) return e;
+    return cudaSuccess;
+}
+
+cudaError_t launch_gateup2(const ExpertDesc* experts, const int* ids, int npick, const int8_t* xqs, const float* xd,
+                           int dim, int ff, float limit, float* gu, int8_t* hqs, float* hd, int* counters, int* err,
+                           cudaStream_t s) {
+    const int items = npick * 2 * (ff >> 3);
+    const int grid = std::min(num_sms(), (items + kV2Warps - 1) / kV2Warps);
+    k_gateup2<<<grid, kV2Threads, gateup2_smem(dim), s>>>(experts, ids, npick, xqs, xd, dim, ff, limit, gu, hqs, hd,
+                                                         counters, err);
+    return cudaGetLastError();
+}
+cudaError_t launch_down2(const ExpertDesc* experts, const int* ids, const float* w, int npick, const int8_t* hqs,
+                         const float* hd, int dim, int ff, const float* shared, const float* resid, float* out,
+                         float* yrows, int* counters, int* err, cudaStream_t s) {
+    const int items = npick * ((dim + 31) >> 5);
+    const int grid = std::min(num_sms(), (items + kV2Warps - 1) / kV2Warps);
+    k_down2<<<grid, kV2Threads, down2_smem(npick, ff), s>>>(experts, ids, w, npick, hqs, hd, dim, ff, shared, resid,
+                                                           out, yrows, counters, err);
+    return cudaGetLastError();
+}
+cudaError_t launch_mv2(const PackedMat& m, const void* q, float* y, cudaStream_t s) {
+    const int groups = (m.n + 31) >> 5;
+    const int grid = std::min(num_sms(), (groups + kV2Warps - 1) / kV2Warps);
+    k_mv2<<<grid, kV2Threads, mv2_smem(m.k), s>>>(m, static_cast<const uint8_t*>(q), y);
     return cudaGetLastError();
 }
 

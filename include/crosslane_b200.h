@@ -155,7 +155,8 @@ int32_t clb_layer_forward_device(clb_bank* bank, uint32_t layer, const int32_t* 
                                  float* d_out, void* stream, clb_error_v1* err);
 
 /* Profiling form of clb_layer_forward_device: runs only the kernels selected by
- * phase_mask (1 quantise x, 2 gate/up + SwiGLU, 4 quantise h, 8 down + combine).
+ * phase_mask (1 quantise x, 2 gate/up + SwiGLU + quantise h, 8 down + combine; bit 4 is
+ * accepted and does nothing: h is quantised inside the gate/up kernel).
  * Phases read what earlier phases left in the bank's workspace, so a phase may run
  * alone only after a full step has run with the same arguments. */
 int32_t clb_layer_phases_device(clb_bank* bank, uint32_t layer, const int32_t* d_ids, const float* d_w, int32_t n,

@@ -3,10 +3,11 @@
 1. The oracle's lane integers (q8k_core.hpp restatement) agree with an independent
    per-32 decoder (core.hpp restatement) for every IQ2_XXS index x sign pair, every
    IQ2_XS 9-bit index x sign word, every IQ1_M index x delta x scale pair.
-2. The GPU kernel's decode -- nibble-selector tables from the library, byte permute
-   (PTX prmt.b32 semantics), the mma.sync m16n8k32 fragment layout and the per-lane
-   activation masks -- reproduces the oracle's lane integers exactly. This is the
-   kernel's algorithm restated in numpy, run on every code.
+2. The GPU kernels' decode -- nibble-selector tables from the library, the packed
+   IQ2_XXS sign bytes, byte permute (PTX prmt.b32 semantics), and both ways of forming
+   lanes (the row-per-thread dp4a lanes of clb_rowdot.cuh and the mma.sync m16n8k32
+   fragments with per-lane activation masks of clb_device.cuh) -- reproduces the
+   oracle's lane integers exactly. The kernels' algorithm restated in numpy, on every code.
 """
 import ctypes as C
 
@@ -42,19 +43,29 @@ def s8(word):
     return np.asarray(word, np.uint32).view(np.uint8).reshape(-1, 4).astype(np.int8).astype(np.int32)
 
 
+def aux_to_signbytes(aux):
+    """clb_pack.h's IQ2_XXS chunk re-planing of the u32 aux."""
+    out = 0
+    for j in range(4):
+        out |= (((aux >> (7 * j)) & 127) | (((aux >> (28 + j)) & 1) << 7)) << (8 * j)
+    return out
+
+
 def gpu_group_decode(qtype, tb, blocks, c, t):
     """decode_group<T> of clb_device.cuh for chunk c, group t over an array of AoS blocks.
     Returns (lo int8x4 as int32[...,4], hi, scale, delta)."""
     n = len(blocks)
     if qtype == 16:
+        # packed chunk: [4 grid bytes][4 sign bytes; bit 7 of byte j = sub-scale bit j]
         gw = blocks[:, 2 + 8 * c: 6 + 8 * c].copy().view(np.uint32)[:, 0]
         aux = blocks[:, 6 + 8 * c: 10 + 8 * c].copy().view(np.uint32)[:, 0]
+        sw = np.array([aux_to_signbytes(int(a)) for a in aux], np.uint32)
         gi = (gw >> (8 * t)) & 0xFF
-        si = (aux >> (7 * t)) & 0x7F
+        si = (sw >> (8 * t)) & 0x7F
         sel = tb["xxs"][gi] | tb["sign"][si]
         lo = prmt(PRMT_IQ2_POS, PRMT_IQ2_NEG, sel)
         hi = prmt(PRMT_IQ2_POS, PRMT_IQ2_NEG, sel >> 16)
-        scale = ((aux >> 28) << 1) | 1
+        scale = ((((sw & 0x80808080) | 0x08000000).astype(np.uint64) * 0x00204081 >> 27) & 0x1F).astype(np.uint32)
         delta = np.zeros(n, np.int64)
     elif qtype == 17:
         w = blocks[:, 2 + 8 * c + 4 * (t >> 1): 6 + 8 * c + 4 * (t >> 1)].copy().view(np.uint32)[:, 0]
@@ -113,6 +124,24 @@ def gpu_lane_ints(qtype, tb, blocks, q):
             main[:, lane] += scale[:, t] * D[:, lane]
             lsum = int(q32[4 * lane: 4 * lane + 4].sum())
             dl[:, lane] += scale[:, t] * delta[:, t] * lsum
+    return main, dl
+
+
+def gpu_row_lane_ints(qtype, tb, blocks, q):
+    """block_lanes<T> of clb_rowdot.cuh: one thread decodes all 4 groups of every chunk,
+    lane 2j += scale * dp4a(lo_j, q lane 2j), lane 2j+1 += scale * dp4a(hi_j, q lane 2j+1);
+    IQ1_M delta lanes += (+-scale) * sum of the lane's 4 activations."""
+    n = len(blocks)
+    main = np.zeros((n, 8), np.int64)
+    dl = np.zeros((n, 8), np.int64)
+    for c in range(8):
+        q32 = q[32 * c: 32 * c + 32].astype(np.int64)
+        for j in range(4):
+            lo, hi, sc, de = gpu_group_decode(qtype, tb, blocks, c, j)
+            main[:, 2 * j] += sc * (lo * q32[8 * j: 8 * j + 4]).sum(axis=1)
+            main[:, 2 * j + 1] += sc * (hi * q32[8 * j + 4: 8 * j + 8]).sum(axis=1)
+            dl[:, 2 * j] += sc * de * int(q32[8 * j: 8 * j + 4].sum())
+            dl[:, 2 * j + 1] += sc * de * int(q32[8 * j + 4: 8 * j + 8].sum())
     return main, dl
 
 
@@ -203,6 +232,8 @@ def test_gpu_decode_model_exhaustive(orc, qtype):
         qb = orc.quantize(x)
         qs = qb[4:260].view(np.int8)
         main, delta = gpu_lane_ints(qtype, tb, blocks, qs)
+        rmain, rdelta = gpu_row_lane_ints(qtype, tb, blocks, qs)
+        assert np.array_equal(main, rmain) and (qtype != 29 or np.array_equal(delta, rdelta))
         sample = range(0, len(blocks), max(1, len(blocks) // 400))
         for r in sample:
             blk = np.ascontiguousarray(blocks[r])

@@ -53,17 +53,33 @@ def test_pack_geometry_checks():
         cb.pack(16, 4, 256, np.zeros(10, np.uint8))
 
 
-def test_pack_plane_order():
-    """Body piece q of block b of row r lands at ((b*4 + q)*n + r)*16 (clb_types.h)."""
+def aux_to_signbytes(aux):
+    out = 0
+    for j in range(4):
+        out |= (((aux >> (7 * j)) & 127) | (((aux >> (28 + j)) & 1) << 7)) << (8 * j)
+    return out
+
+
+@pytest.mark.parametrize("qtype", [16, 17])
+def test_pack_plane_order(qtype):
+    """Body piece q of block b of row r lands at ((b*4 + q)*n + r)*16 (clb_types.h); an
+    IQ2_XXS chunk's u32 aux becomes 4 sign bytes carrying the sub-scale bits on top."""
     n, k = 5, 512
-    raw = np.arange(n * 2 * 66, dtype=np.uint32).astype(np.uint8)
-    packed = cb.pack(16, n, k, raw)
-    blk = raw.reshape(n, 2, 66)
+    bb = cb.BLOCK_BYTES[qtype]
+    raw = (np.arange(n * 2 * bb, dtype=np.uint32) * 7 + 3).astype(np.uint8)
+    raw.reshape(-1, bb)[:, 1] &= 0x7B
+    packed = cb.pack(qtype, n, k, raw)
+    blk = raw.reshape(n, 2, bb)
     for r in range(n):
         for b in range(2):
             for q in range(4):
                 off = ((b * 4 + q) * n + r) * 16
-                assert np.array_equal(packed[off:off + 16], blk[r, b, 2 + 16 * q: 18 + 16 * q])
+                want = blk[r, b, 2 + 16 * q: 18 + 16 * q].copy()
+                if qtype == 16:
+                    for c in range(2):
+                        aux = int(want[8 * c + 4: 8 * c + 8].view(np.uint32)[0])
+                        want[8 * c + 4: 8 * c + 8] = np.frombuffer(np.uint32(aux_to_signbytes(aux)).tobytes(), np.uint8)
+                assert np.array_equal(packed[off:off + 16], want)
 
 
 # ---------------------------------------------------------------- synthetic inputs
