@@ -176,6 +176,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS, help="smaller stacks for quick checks only")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--policy", type=int, default=POLICY, help="quant type policy of the bank (2 = config 3 mix)")
+    ap.add_argument("--quick", action="store_true", help="skip the e2e pass and the CPU baseline (tuning sweeps)")
+    ap.add_argument("--exact-order", action="store_true",
+                    help="reference summation order (CLB_BANK_EXACT_ORDER): bit-identical to the CPU lane")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -197,9 +201,10 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
 
     L = args.layers
-    bank = cb.ExpertBank(n_layers=L, n_experts=EXPERTS, dim=DIM, ff=FF, max_picks=PICKS, device=local)
+    bank = cb.ExpertBank(n_layers=L, n_experts=EXPERTS, dim=DIM, ff=FF, max_picks=PICKS, device=local,
+                         exact_order=args.exact_order)
     t0 = time.time()
-    bank.fill_synthetic(SEED, POLICY)
+    bank.fill_synthetic(SEED, args.policy)
     fill_s = time.time() - t0
     stream = torch.cuda.ExternalStream(bank.stream)
 
@@ -246,14 +251,16 @@ def main():
     # ---- e2e through the host-buffer C ABI call (copies inside the timed region) ----
     hx = np.ascontiguousarray(xs)
     hl = np.ascontiguousarray(logits)
-    for i in range(args.warmup):
+    e2e_steps = 1 if args.quick else args.steps
+    for i in range(0 if args.quick else args.warmup):
         bank.stack_decode(0, L, hx[i], hl[i])
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
-    for i in range(args.steps):
+    for i in range(e2e_steps):
         bank.stack_decode(0, L, hx[args.warmup + i], hl[args.warmup + i])
     e2e_s = time.perf_counter() - t0
+    e2e_s = e2e_s * args.steps / e2e_steps
     if world > 1:
         t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -318,7 +325,7 @@ def main():
     step_gbs = step_bytes / (ms_per_step / 1e3) / 1e9
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
         cpu = cpu_baseline(samples=2)
 
     clk = clocks.summary()
@@ -330,6 +337,8 @@ def main():
                    "types": "IQ2_XXS/IQ2_XS/IQ1_M per (layer, expert), seed-drawn", "batch": 1,
                    "routing": "top-6 by sigmoid of N(0,1) logits, renormalised",
                    "parallelism": f"replica x{world}" if world > 1 else "single GPU",
+                   "summation": "exact reference order" if args.exact_order
+                   else "segmented rows, fixed-tree partials (run-to-run identical)",
                    "l2": "inputs larger than L2: each token streams ~2 GB of distinct expert weights",
                    "bank_gb": round(bank.weight_bytes / 1e9, 2), "fill_s": round(fill_s, 1)},
         "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in e2e.items()},

@@ -36,7 +36,8 @@ class ErrorV1(C.Structure):
 class BankConfigV1(C.Structure):
     _fields_ = [("device", C.c_int32), ("n_layers", C.c_int32), ("n_experts", C.c_int32), ("dim", C.c_int32),
                 ("ff", C.c_int32), ("max_picks", C.c_int32), ("limit", C.c_float), ("expert_begin", C.c_int32),
-                ("expert_end", C.c_int32), ("reserved", C.c_int32 * 7)]
+                ("expert_end", C.c_int32), ("flags", C.c_int32),
+                ("reserved", C.c_int32 * 6)]
 
 
 HOST_EXPERT_FN = C.CFUNCTYPE(C.c_int32, C.c_void_p, C.c_uint32, C.c_int32, C.POINTER(C.c_float), C.c_int32,

@@ -127,7 +127,7 @@ struct clb_bank {
     int* d_err = nullptr;
     float* d_gu = nullptr;          // gate/up rows [pick][2][ff]
     int* d_cnt_h = nullptr;         // last-arriver counters per (pick, 256-row block of h)
-    int* d_cnt_y = nullptr;         // last-arriver counters per 32-row output group
+    int* d_cnt_y = nullptr;         // last-arriver counters per output row group (16 or 32 rows)
     float* d_logits = nullptr;
     int* d_route_ids = nullptr;
     float* d_route_w = nullptr;
@@ -138,6 +138,7 @@ struct clb_bank {
     size_t L() const { return (size_t)cfg.n_layers; }
     size_t E() const { return (size_t)cfg.n_experts; }
     bool owns(int e) const { return e >= cfg.expert_begin && e < cfg.expert_end; }
+    bool fast() const { return (cfg.flags & CLB_BANK_EXACT_ORDER) == 0; }
 
     template <class T>
     T* dev_alloc(size_t count) {
@@ -204,10 +205,10 @@ struct clb_bank {
             cuda_check(clb::launch_norm_quant(x, dim, d_xqs, d_xd, nullptr, s), "norm + quantize x");
         else
             cuda_check(clb::launch_quant(x, dim / 256, d_xqs, d_xd, s), "quantize x");
-        cuda_check(clb::launch_gateup2(ex, ids, n, d_xqs, d_xd, dim, ff, cfg.limit, d_gu, d_hqs, d_hd, d_cnt_h, d_err, s),
+        cuda_check(clb::launch_gateup2(ex, ids, n, d_xqs, d_xd, dim, ff, cfg.limit, d_gu, d_hqs, d_hd, d_cnt_h, d_err, fast(), s),
                    "gate/up + SwiGLU + quantize h");
         cuda_check(clb::launch_down2(ex, ids, w, n, d_hqs, d_hd, dim, ff, shared, resid, out, yrows ? yrows : d_yrows,
-                                     d_cnt_y, d_err, s),
+                                     d_cnt_y, d_err, fast(), s),
                    "down + combine");
     }
 
@@ -218,11 +219,11 @@ struct clb_bank {
         if (mask & 1) cuda_check(clb::launch_quant(x, dim / 256, d_xqs, d_xd, s), "quantize x");
         if (mask & 2)
             cuda_check(clb::launch_gateup2(ex, ids, n, d_xqs, d_xd, dim, ff, cfg.limit, d_gu, d_hqs, d_hd, d_cnt_h, d_err,
-                                           s),
+                                           fast(), s),
                        "gate/up + SwiGLU + quantize h");
         if (mask & 8)
             cuda_check(clb::launch_down2(ex, ids, w, n, d_hqs, d_hd, dim, ff, nullptr, nullptr, out, d_yrows, d_cnt_y,
-                                         d_err, s),
+                                         d_err, fast(), s),
                        "down + combine");
     }
 
@@ -371,6 +372,7 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         require(cfg.max_picks >= 1 && cfg.max_picks <= clb::kMaxPicks && cfg.max_picks <= cfg.n_experts,
                 CLB_E_INVALID, "max_picks must be in [1, 16]");
         require(std::isfinite(cfg.limit) && cfg.limit >= 0, CLB_E_INVALID, "SwiGLU limit must be finite and >= 0");
+        require((cfg.flags & ~CLB_BANK_EXACT_ORDER) == 0, CLB_E_INVALID, "unknown bank flags 0x%x", cfg.flags);
         require(cfg.expert_begin >= 0 && cfg.expert_begin < cfg.expert_end && cfg.expert_end <= cfg.n_experts,
                 CLB_E_INVALID, "owned expert range invalid");
         require((size_t)cfg.max_picks * (cfg.ff / 256) <= 256, CLB_E_UNSUPPORTED,
@@ -398,9 +400,9 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         bank->d_yrows = bank->dev_alloc<float>(k * dim);
         bank->d_gu = bank->dev_alloc<float>(k * 2 * ff);
         bank->d_cnt_h = bank->dev_alloc<int>(k * ff / 256);
-        bank->d_cnt_y = bank->dev_alloc<int>((dim + 31) / 32);
+        bank->d_cnt_y = bank->dev_alloc<int>((dim + 15) / 16);
         cuda_check(cudaMemsetAsync(bank->d_cnt_h, 0, sizeof(int) * k * ff / 256, bank->stream), "memset");
-        cuda_check(cudaMemsetAsync(bank->d_cnt_y, 0, sizeof(int) * ((dim + 31) / 32), bank->stream), "memset");
+        cuda_check(cudaMemsetAsync(bank->d_cnt_y, 0, sizeof(int) * ((dim + 15) / 16), bank->stream), "memset");
         bank->d_ids = bank->dev_alloc<int>(k);
         bank->d_w = bank->dev_alloc<float>(k);
         bank->d_err = bank->dev_alloc<int>(1);

@@ -42,11 +42,7 @@ constexpr uint32_t kIq2Pos = 0x002B1908u;  // +8, +25, +43
 constexpr uint32_t kIq2Neg = 0x00D5E7F8u;  // -8, -25, -43
 constexpr uint32_t kIq1Val = 0x000100FFu;  // -1, 0, +1
 
-__device__ __forceinline__ uint32_t prmt(uint32_t lo, uint32_t hi, uint32_t sel) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(lo), "r"(hi), "r"(sel));
-    return r;
-}
+__device__ __forceinline__ uint32_t prmt(uint32_t lo, uint32_t hi, uint32_t sel) { return __byte_perm(lo, hi, sel); }
 
 // D(16x8 s32) = A(16x32 s8) * B(32x8 s8); C = 0.
 __device__ __forceinline__ void mma_s8(const uint32_t a[4], uint32_t b0, uint32_t b1, int d[4]) {

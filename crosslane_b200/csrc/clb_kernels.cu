@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "clb_device.cuh"
 #include "clb_kernels.h"
@@ -460,25 +461,36 @@ __device__ __forceinline__ void warp_quant_regs(float v[8], int8_t* qs, float* d
 // (thread k takes blocks k, k+4, ...). Per round the 4 threads exchange their blocks'
 // lane integers through shared memory so that thread k folds lanes 2k, 2k+1 of all 4
 // blocks in block order, exactly the reference chain. Returns the row value in k == 0.
+// Not inlined: each quant type gets its own register allocation (inlined together the
+// three paths exceed 128 registers); the call happens once per warp item.
+// L2 prefetch of one row block (no registers held).
 template <int T>
-__device__ __forceinline__ float quad_row_dot(const PackedMat& m, int row, const int8_t* act_qs, const float* act_d,
-                                              uint32_t tab, uint32_t* xch) {
+__device__ __forceinline__ void prefetch_raw(const PackedMat& m, int row, int b) {
+    const size_t n = (size_t)m.n;
+    const uint8_t* p = m.body + ((size_t)b * (T == CLB_IQ1_M ? 3 : 4) * n + (size_t)row) * 16;
+    prefetch_l2(p);
+    prefetch_l2(p + n * 16);
+    prefetch_l2(p + n * 32);
+    if (T != CLB_IQ1_M) prefetch_l2(p + n * 48);
+}
+
+template <int T, bool PF>
+__device__ __noinline__ float quad_row_dot(const PackedMat& m, int row, const int8_t* act_qs, const float* act_d,
+                                           uint32_t* xch) {
     const int lane = threadIdx.x & 31, k = lane & 3, rr = lane >> 2;
     const uint32_t lb = (uint32_t)lane * 4u;
     const int nb = m.k >> 8;
     const int rounds = (nb + 3) >> 2;
     float acc0 = 0.0f, acc1 = 0.0f, dacc0 = 0.0f, dacc1 = 0.0f;
-    RowRaw cur, nxt;
-    if (k < nb) load_raw<T>(m, row, k, cur);
-    for (int i = 0; i < rounds; ++i) {
+    // One round: decode block b = 4i + k from `r`, exchange lane integers within the
+    // row's 4 threads, fold blocks 4i..4i+3 in order into lanes 2k, 2k+1.
+    auto round = [&](int i, const RowRaw& r) {
         const int b = 4 * i + k;
-        const bool have = b < nb;
-        if (b + 4 < nb) load_raw<T>(m, row, b + 4, nxt);
         int I[8], D[8];
         float dd = 0.0f;
-        if (have) {
-            block_lanes<T>(cur, act_qs + (size_t)b * kActStride, tab, lb, I, D);
-            dd = __fmul_rn(raw_scale<T>(cur), act_d[b]);
+        if (b < nb) {
+            block_lanes<T>(r, act_qs + (size_t)b * kActStride, lb, I, D);
+            dd = __fmul_rn(raw_scale<T>(r), act_d[b]);
         } else {
 #pragma unroll
             for (int L = 0; L < 8; ++L) I[L] = D[L] = 0;
@@ -506,52 +518,120 @@ __device__ __forceinline__ float quad_row_dot(const PackedMat& m, int row, const
             }
         }
         __syncwarp();
-        if (b + 4 < nb) cur = nxt;
+    };
+    if (PF) {
+        // ping-pong: round i decodes buffer i%2 while the loads of round i+1 are in flight
+        RowRaw ra, rb;
+        if (k < nb) load_raw_early<T>(m, row, k, ra);
+        for (int i = 0; i < rounds; i += 2) {
+            if (4 * (i + 1) + k < nb) load_raw_early<T>(m, row, 4 * (i + 1) + k, rb);
+            round(i, ra);
+            if (i + 1 >= rounds) break;
+            if (4 * (i + 2) + k < nb) load_raw_early<T>(m, row, 4 * (i + 2) + k, ra);
+            round(i + 1, rb);
+        }
+    } else {
+        RowRaw cur;
+        for (int i = 0; i < rounds; ++i) {
+            const int b = 4 * i + k;
+            if (b + 4 < nb) prefetch_raw<T>(m, row, b + 4);
+            if (b < nb) load_raw<T>(m, row, b, cur);
+            round(i, cur);
+        }
     }
     const float main = quad_hsum(acc0, acc1);
     if (T == CLB_IQ1_M) return __fadd_rn(main, __fmul_rn(0.125f, quad_hsum(dacc0, dacc1)));
     return __fmul_rn(0.125f, main);
 }
 
-// One thread = one row over all blocks; the 8 lane chains stay in registers.
-template <int T>
-__device__ __forceinline__ float thread_row_dot(const PackedMat& m, int row, const int8_t* act_qs, const float* act_d,
-                                                uint32_t tab) {
+template <int T, bool PF>
+__device__ __noinline__ float thread_row_dot(const PackedMat& m, int row, const int8_t* act_qs, const float* act_d) {
     const uint32_t lb = (uint32_t)(threadIdx.x & 31) * 4u;
     const int nb = m.k >> 8;
     float acc[8], dacc[8];
 #pragma unroll
     for (int L = 0; L < 8; ++L) acc[L] = dacc[L] = 0.0f;
-    RowRaw cur, nxt;
-    load_raw<T>(m, row, 0, cur);
-    for (int b = 0; b < nb; ++b) {
-        if (b + 1 < nb) load_raw<T>(m, row, b + 1, nxt);
+    auto step = [&](int b, const RowRaw& r) {
         int I[8], D[8];
-        block_lanes<T>(cur, act_qs + (size_t)b * kActStride, tab, lb, I, D);
-        const float dd = __fmul_rn(raw_scale<T>(cur), act_d[b]);
+        block_lanes<T>(r, act_qs + (size_t)b * kActStride, lb, I, D);
+        const float dd = __fmul_rn(raw_scale<T>(r), act_d[b]);
 #pragma unroll
         for (int L = 0; L < 8; ++L) {
             acc[L] = __fmaf_rn(dd, (float)I[L], acc[L]);
             if (T == CLB_IQ1_M) dacc[L] = __fmaf_rn(dd, (float)D[L], dacc[L]);
         }
-        if (b + 1 < nb) cur = nxt;
+    };
+    if (PF) {
+        RowRaw ra, rb;
+        load_raw_early<T>(m, row, 0, ra);
+        for (int b = 0; b < nb; b += 2) {
+            if (b + 1 < nb) load_raw_early<T>(m, row, b + 1, rb);
+            step(b, ra);
+            if (b + 1 >= nb) break;
+            if (b + 2 < nb) load_raw_early<T>(m, row, b + 2, ra);
+            step(b + 1, rb);
+        }
+    } else {
+        RowRaw cur;
+        for (int b = 0; b < nb; ++b) {
+            if (b + 1 < nb) prefetch_raw<T>(m, row, b + 1);
+            load_raw<T>(m, row, b, cur);
+            step(b, cur);
+        }
     }
     const float main = hsum8_rn(acc);
     if (T == CLB_IQ1_M) return __fadd_rn(main, __fmul_rn(0.125f, hsum8_rn(dacc)));
     return __fmul_rn(0.125f, main);
 }
 
-__device__ __forceinline__ float quad_row_dot_any(const PackedMat& m, int row, const int8_t* aq, const float* ad,
-                                                  uint32_t tab, uint32_t* xch) {
-    if (m.type == CLB_IQ2_XXS) return quad_row_dot<CLB_IQ2_XXS>(m, row, aq, ad, tab, xch);
-    if (m.type == CLB_IQ2_XS) return quad_row_dot<CLB_IQ2_XS>(m, row, aq, ad, tab, xch);
-    return quad_row_dot<CLB_IQ1_M>(m, row, aq, ad, tab, xch);
+// Fast math: thread k of a row's group of S threads streams the contiguous block range
+// [k*nb/S, (k+1)*nb/S) and accumulates fp32 partials acc += d_b * M_b (and the IQ1_M
+// delta); the S partials are then added in a fixed tree, so results are run-to-run
+// identical and differ from the reference's per-lane order only by fp32 reassociation.
+template <int T, int S>
+__device__ __noinline__ float seg_row_dot(const PackedMat& m, int row, const int8_t* act_qs, const float* act_d) {
+    const int lane = threadIdx.x & 31, k = lane % S;
+    const uint32_t lb = (uint32_t)lane * 4u;
+    const int nb = m.k >> 8;
+    const int per = (nb + S - 1) / S, b0 = k * per, b1 = min(nb, b0 + per);
+    float acc = 0.0f, dacc = 0.0f;
+    for (int b = b0; b < b1; ++b) {
+        if (b + 1 < b1) prefetch_raw<T>(m, row, b + 1);
+        RowRaw r;
+        load_raw<T>(m, row, b, r);
+        int M, D;
+        block_sum<T>(r, act_qs + (size_t)b * kActStride, lb, M, D);
+        const float dd = __fmul_rn(raw_scale<T>(r), act_d[b]);
+        acc = __fmaf_rn(dd, (float)M, acc);
+        if (T == CLB_IQ1_M) dacc = __fmaf_rn(dd, (float)D, dacc);
+    }
+#pragma unroll
+    for (int o = 1; o < S; o <<= 1) {
+        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+        if (T == CLB_IQ1_M) dacc = __fadd_rn(dacc, __shfl_xor_sync(0xffffffffu, dacc, o));
+    }
+    if (T == CLB_IQ1_M) return __fadd_rn(acc, __fmul_rn(0.125f, dacc));
+    return __fmul_rn(0.125f, acc);
 }
-__device__ __forceinline__ float thread_row_dot_any(const PackedMat& m, int row, const int8_t* aq, const float* ad,
-                                                    uint32_t tab) {
-    if (m.type == CLB_IQ2_XXS) return thread_row_dot<CLB_IQ2_XXS>(m, row, aq, ad, tab);
-    if (m.type == CLB_IQ2_XS) return thread_row_dot<CLB_IQ2_XS>(m, row, aq, ad, tab);
-    return thread_row_dot<CLB_IQ1_M>(m, row, aq, ad, tab);
+template <int S>
+__device__ __forceinline__ float seg_row_dot_any(const PackedMat& m, int row, const int8_t* aq, const float* ad) {
+    if (m.type == CLB_IQ2_XXS) return seg_row_dot<CLB_IQ2_XXS, S>(m, row, aq, ad);
+    if (m.type == CLB_IQ2_XS) return seg_row_dot<CLB_IQ2_XS, S>(m, row, aq, ad);
+    return seg_row_dot<CLB_IQ1_M, S>(m, row, aq, ad);
+}
+
+template <bool PF>
+__device__ __forceinline__ float quad_row_dot_any(const PackedMat& m, int row, const int8_t* aq, const float* ad,
+                                                  uint32_t* xch) {
+    if (m.type == CLB_IQ2_XXS) return quad_row_dot<CLB_IQ2_XXS, PF>(m, row, aq, ad, xch);
+    if (m.type == CLB_IQ2_XS) return quad_row_dot<CLB_IQ2_XS, PF>(m, row, aq, ad, xch);
+    return quad_row_dot<CLB_IQ1_M, PF>(m, row, aq, ad, xch);
+}
+template <bool PF>
+__device__ __forceinline__ float thread_row_dot_any(const PackedMat& m, int row, const int8_t* aq, const float* ad) {
+    if (m.type == CLB_IQ2_XXS) return thread_row_dot<CLB_IQ2_XXS, PF>(m, row, aq, ad);
+    if (m.type == CLB_IQ2_XS) return thread_row_dot<CLB_IQ2_XS, PF>(m, row, aq, ad);
+    return thread_row_dot<CLB_IQ1_M, PF>(m, row, aq, ad);
 }
 
 // Shared-memory copy of Q8_K activations (qs int8 + d floats, from global) with the
@@ -569,33 +649,34 @@ __device__ __forceinline__ void stage_act(const int8_t* __restrict__ qs, const f
 // ------------------------------------------------------------------------------
 // Gate + up for all picks (one warp item = 8 rows of one matrix of one pick), then,
 // in the last warp to finish each 256-row block of a pick, SwiGLU and Q8_K(h).
-__global__ void __launch_bounds__(kV2Threads, 1)
+template <int MAXT, bool PF, bool FAST>
+__global__ void __launch_bounds__(MAXT, 1)
     k_gateup2(const ExpertDesc* __restrict__ experts, const int* __restrict__ ids, int npick,
               const int8_t* __restrict__ xqs, const float* __restrict__ xd, int dim, int ff, float limit,
               float* __restrict__ gu, int8_t* __restrict__ hqs, float* __restrict__ hd, int* __restrict__ counters,
               int* __restrict__ err) {
-    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* smem = clb_dyn_smem;
     const int nbx = dim >> 8;
     int8_t* aq = reinterpret_cast<int8_t*>(smem + kRowTableBytes);
     float* ad = reinterpret_cast<float*>(smem + kRowTableBytes + (size_t)nbx * kActStride);
     uint32_t* xch_all = reinterpret_cast<uint32_t*>(smem + kRowTableBytes + (size_t)nbx * kActStride + 4 * nbx);
-    fill_row_tables(g_tables, smem);
+    fill_row_tables(g_tables, xch_all);  // the exchange area doubles as the staging area
     stage_act(xqs, xd, nbx, aq, ad);
     __syncthreads();
-    const uint32_t tab = smem_u32(smem);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     uint32_t* xch = xch_all + warp * 32 * kXchWords;
     const int groups = ff >> 3;                       // 8-row groups per matrix
     const int items = npick * 2 * groups;
     const int hblocks = ff >> 8;
-    for (int it = blockIdx.x * kV2Warps + warp; it < items; it += gridDim.x * kV2Warps) {
+    for (int it = blockIdx.x * nwarps + warp; it < items; it += gridDim.x * nwarps) {
         const int pick = it / (2 * groups), rem = it % (2 * groups);
         const int group = rem >> 1, mat = rem & 1;       // gate/up of the same rows are adjacent
         const ExpertDesc& ex = experts[ids[pick]];
         const PackedMat& m = mat ? ex.up : ex.gate;
         const int row = group * 8 + (lane >> 2);
         float y = 0.0f;
-        if (m.body != nullptr && m.k == dim && m.n == ff) y = quad_row_dot_any(m, row, aq, ad, tab, xch);
+        if (m.body != nullptr && m.k == dim && m.n == ff)
+            y = FAST ? seg_row_dot_any<4>(m, row, aq, ad) : quad_row_dot_any<PF>(m, row, aq, ad, xch);
         else if (lane == 0) atomicExch(err, 1);
         if ((lane & 3) == 0) gu[((size_t)pick * 2 + mat) * ff + row] = y;
         // last arriver of this (pick, 256-row block) applies SwiGLU and quantises h
@@ -623,38 +704,41 @@ __global__ void __launch_bounds__(kV2Threads, 1)
 // Down projection (one warp item = 32 rows of one pick, one thread per row), then, in
 // the last warp to finish each 32-row group, the ascending-id fma combine
 // (runtime.cpp:184-187), + shared, + residual.
-__global__ void __launch_bounds__(kV2Threads, 1)
+template <int MAXT, bool PF, bool FAST>
+__global__ void __launch_bounds__(MAXT, 1)
     k_down2(const ExpertDesc* __restrict__ experts, const int* __restrict__ ids, const float* __restrict__ wts, int npick,
             const int8_t* __restrict__ hqs, const float* __restrict__ hd, int dim, int ff,
             const float* __restrict__ shared, const float* __restrict__ resid, float* __restrict__ out,
             float* __restrict__ yrows, int* __restrict__ counters, int* __restrict__ err) {
-    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* smem = clb_dyn_smem;
     const int nbh = ff >> 8;
     int8_t* aq = reinterpret_cast<int8_t*>(smem + kRowTableBytes);
     float* ad = reinterpret_cast<float*>(smem + kRowTableBytes + (size_t)npick * nbh * kActStride);
-    fill_row_tables(g_tables, smem);
+    fill_row_tables(g_tables, reinterpret_cast<uint32_t*>(ad + npick * nbh + 4));
     stage_act(hqs, hd, npick * nbh, aq, ad);
     __syncthreads();
-    const uint32_t tab = smem_u32(smem);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int groups = (dim + 31) >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    // exact: one thread per row, 32 rows per item; fast: 2 threads per row, 16 rows
+    constexpr int RPI = FAST ? 16 : 32;
+    const int groups = (dim + RPI - 1) / RPI;
     const int items = npick * groups;
-    for (int it = blockIdx.x * kV2Warps + warp; it < items; it += gridDim.x * kV2Warps) {
+    for (int it = blockIdx.x * nwarps + warp; it < items; it += gridDim.x * nwarps) {
         const int group = it / npick, pick = it % npick;
         const PackedMat& m = experts[ids[pick]].down;
-        const int row = group * 32 + lane;
+        const int row = group * RPI + (FAST ? lane >> 1 : lane);
         const int rowc = row < dim ? row : dim - 1;
         float y = 0.0f;
         if (m.body != nullptr && m.k == ff && m.n == dim)
-            y = thread_row_dot_any(m, rowc, aq + (size_t)pick * nbh * kActStride, ad + pick * nbh, tab);
+            y = FAST ? seg_row_dot_any<2>(m, rowc, aq + (size_t)pick * nbh * kActStride, ad + pick * nbh)
+                     : thread_row_dot_any<PF>(m, rowc, aq + (size_t)pick * nbh * kActStride, ad + pick * nbh);
         else if (lane == 0) atomicExch(err, 1);
-        if (row < dim) yrows[(size_t)pick * dim + row] = y;
+        if (row < dim && (!FAST || (lane & 1) == 0)) yrows[(size_t)pick * dim + row] = y;
         __threadfence();
         __syncwarp();
         int last = 0;
         if (lane == 0) last = atomicAdd(&counters[group], 1) == npick - 1;
         last = __shfl_sync(0xffffffffu, last, 0);
-        if (last && row < dim) {
+        if (last && row < dim && (!FAST || (lane & 1) == 0)) {
             __threadfence();
             float acc = 0.0f;
             int prev = -1;
@@ -677,11 +761,11 @@ __global__ void __launch_bounds__(kV2Threads, 1)
 // ------------------------------------------------------------------------------
 // y[n] = W . q for one packed matrix (crosslane q8k::Block input), one thread per row.
 __global__ void __launch_bounds__(kV2Threads, 1) k_mv2(PackedMat m, const uint8_t* __restrict__ q, float* __restrict__ y) {
-    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* smem = clb_dyn_smem;
     const int nb = m.k >> 8;
     int8_t* aq = reinterpret_cast<int8_t*>(smem + kRowTableBytes);
     float* ad = reinterpret_cast<float*>(smem + kRowTableBytes + (size_t)nb * kActStride);
-    fill_row_tables(g_tables, smem);
+    fill_row_tables(g_tables, reinterpret_cast<uint32_t*>(ad + nb + 4));
     for (int i = threadIdx.x; i < nb * 64; i += blockDim.x) {
         const int b = i >> 6, w = i & 63;
         reinterpret_cast<uint32_t*>(aq + (size_t)b * kActStride)[w] =
@@ -689,24 +773,26 @@ __global__ void __launch_bounds__(kV2Threads, 1) k_mv2(PackedMat m, const uint8_
     }
     for (int b = threadIdx.x; b < nb; b += blockDim.x) ad[b] = *reinterpret_cast<const float*>(q + (size_t)b * kQ8KBlockBytes);
     __syncthreads();
-    const uint32_t tab = smem_u32(smem);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     const int groups = (m.n + 31) >> 5;
-    for (int g = blockIdx.x * kV2Warps + warp; g < groups; g += gridDim.x * kV2Warps) {
+    for (int g = blockIdx.x * nwarps + warp; g < groups; g += gridDim.x * nwarps) {
         const int row = g * 32 + lane;
-        const float v = thread_row_dot_any(m, row < m.n ? row : m.n - 1, aq, ad, tab);
+        const float v = thread_row_dot_any<true>(m, row < m.n ? row : m.n - 1, aq, ad);
         if (row < m.n) y[row] = v;
     }
 }
 
-size_t gateup2_smem(int dim) {
-    return kRowTableBytes + (size_t)(dim >> 8) * kActStride + 4 * (size_t)(dim >> 8) +
-           (size_t)kV2Warps * 32 * kXchWords * 4 + 16;
+// The exchange area doubles as the 2944-word staging buffer of fill_row_tables, so it
+// is never smaller than that, whatever the warp count.
+size_t gateup2_smem(int dim, int warps) {
+    size_t xch_words = (size_t)warps * 32 * kXchWords;
+    if (xch_words < 2944) xch_words = 2944;
+    return kRowTableBytes + (size_t)(dim >> 8) * kActStride + 4 * (size_t)(dim >> 8) + xch_words * 4 + 16;
 }
 size_t down2_smem(int npick, int ff) {
-    return kRowTableBytes + (size_t)npick * (ff >> 8) * (kActStride + 4) + 16;
+    return kRowTableBytes + (size_t)npick * (ff >> 8) * (kActStride + 4) + 16 + 2944 * 4;
 }
-size_t mv2_smem(int k) { return kRowTableBytes + (size_t)(k >> 8) * (kActStride + 4) + 16; }
+size_t mv2_smem(int k) { return kRowTableBytes + (size_t)(k >> 8) * (kActStride + 4) + 16 + 2944 * 4; }
 
 static int g_num_sms = 0;
 static int num_sms() {
@@ -719,37 +805,96 @@ static int num_sms() {
     return g_num_sms;
 }
 
+// One CTA per SM with just enough warps (<= max_warps) that every SM gets a share of
+// the warp items; items per warp stay within one of each other.
+static void spread(int items, int max_warps, int& grid, int& threads) {
+    const int sms = num_sms();
+    int warps = (items + sms - 1) / sms;
+    warps = warps < 1 ? 1 : warps > max_warps ? max_warps : warps;
+    grid = (items + warps - 1) / warps;
+    if (grid > sms) grid = sms;
+    threads = 32 * warps;
+}
+
+// Occupancy / prefetch variant of the v2 decode kernels, chosen once per process from
+// CLB_V2_VARIANT (a tuning knob; every variant of a summation order computes identical
+// results): 0 = 512 threads, exact order with register prefetch of the next block;
+// 1 = 512 threads with L2 prefetch (default); 2 = 1024 threads with L2 prefetch.
+static int v2_variant() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("CLB_V2_VARIANT");
+        v = e ? atoi(e) : 1;
+        if (v < 0 || v > 2) v = 1;
+    }
+    return v;
+}
+static int v2_max_threads() { return v2_variant() == 2 ? 1024 : 512; }
+
+template <typename K>
+static cudaError_t allow_smem(K kernel) {
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
 cudaError_t set_v2_smem_limits() {
     cudaError_t e;
-    const int lim = 227 * 1024;
-    if ((e = cudaFuncSetAttribute(k_gateup2, cudaFuncAttributeMaxDynamicSharedMemorySize, lim))) return e;
-    if ((e = cudaFuncSetAttribute(k_down2, cudaFuncAttributeMaxDynamicSharedMemorySize, lim))) return e;
-    if ((e = cudaFuncSetAttribute(k_mv2, cudaFuncAttributeMaxDynamicSharedMemorySize, lim))) return e;
-    return cudaSuccess;
+    if ((e = allow_smem(k_gateup2<512, true, false>))) return e;
+    if ((e = allow_smem(k_gateup2<512, false, false>))) return e;
+    if ((e = allow_smem(k_gateup2<1024, false, false>))) return e;
+    if ((e = allow_smem(k_gateup2<512, false, true>))) return e;
+    if ((e = allow_smem(k_gateup2<1024, false, true>))) return e;
+    if ((e = allow_smem(k_down2<512, true, false>))) return e;
+    if ((e = allow_smem(k_down2<512, false, false>))) return e;
+    if ((e = allow_smem(k_down2<1024, false, false>))) return e;
+    if ((e = allow_smem(k_down2<512, false, true>))) return e;
+    if ((e = allow_smem(k_down2<1024, false, true>))) return e;
+    return allow_smem(k_mv2);
 }
 
 cudaError_t launch_gateup2(const ExpertDesc* experts, const int* ids, int npick, const int8_t* xqs, const float* xd,
                            int dim, int ff, float limit, float* gu, int8_t* hqs, float* hd, int* counters, int* err,
-                           cudaStream_t s) {
+                           bool fast, cudaStream_t s) {
     const int items = npick * 2 * (ff >> 3);
-    const int grid = std::min(num_sms(), (items + kV2Warps - 1) / kV2Warps);
-    k_gateup2<<<grid, kV2Threads, gateup2_smem(dim), s>>>(experts, ids, npick, xqs, xd, dim, ff, limit, gu, hqs, hd,
-                                                         counters, err);
+    int grid, threads;
+    spread(items, v2_max_threads() / 32, grid, threads);
+    const size_t sm = gateup2_smem(dim, threads / 32);
+#define CLB_GU_ARGS experts, ids, npick, xqs, xd, dim, ff, limit, gu, hqs, hd, counters, err
+    const int v = v2_variant();
+    if (fast) {
+        if (v == 2) k_gateup2<1024, false, true><<<grid, threads, sm, s>>>(CLB_GU_ARGS);
+        else k_gateup2<512, false, true><<<grid, threads, sm, s>>>(CLB_GU_ARGS);
+    } else {
+        if (v == 0) k_gateup2<512, true, false><<<grid, threads, sm, s>>>(CLB_GU_ARGS);
+        else if (v == 2) k_gateup2<1024, false, false><<<grid, threads, sm, s>>>(CLB_GU_ARGS);
+        else k_gateup2<512, false, false><<<grid, threads, sm, s>>>(CLB_GU_ARGS);
+    }
+#undef CLB_GU_ARGS
     return cudaGetLastError();
 }
 cudaError_t launch_down2(const ExpertDesc* experts, const int* ids, const float* w, int npick, const int8_t* hqs,
                          const float* hd, int dim, int ff, const float* shared, const float* resid, float* out,
-                         float* yrows, int* counters, int* err, cudaStream_t s) {
-    const int items = npick * ((dim + 31) >> 5);
-    const int grid = std::min(num_sms(), (items + kV2Warps - 1) / kV2Warps);
-    k_down2<<<grid, kV2Threads, down2_smem(npick, ff), s>>>(experts, ids, w, npick, hqs, hd, dim, ff, shared, resid,
-                                                           out, yrows, counters, err);
+                         float* yrows, int* counters, int* err, bool fast, cudaStream_t s) {
+    const int items = npick * (fast ? (dim + 15) >> 4 : (dim + 31) >> 5);
+    int grid, threads;
+    spread(items, v2_max_threads() / 32, grid, threads);
+    const size_t sm = down2_smem(npick, ff);
+#define CLB_DN_ARGS experts, ids, w, npick, hqs, hd, dim, ff, shared, resid, out, yrows, counters, err
+    const int v = v2_variant();
+    if (fast) {
+        if (v == 2) k_down2<1024, false, true><<<grid, threads, sm, s>>>(CLB_DN_ARGS);
+        else k_down2<512, false, true><<<grid, threads, sm, s>>>(CLB_DN_ARGS);
+    } else {
+        if (v == 0) k_down2<512, true, false><<<grid, threads, sm, s>>>(CLB_DN_ARGS);
+        else if (v == 2) k_down2<1024, false, false><<<grid, threads, sm, s>>>(CLB_DN_ARGS);
+        else k_down2<512, false, false><<<grid, threads, sm, s>>>(CLB_DN_ARGS);
+    }
+#undef CLB_DN_ARGS
     return cudaGetLastError();
 }
 cudaError_t launch_mv2(const PackedMat& m, const void* q, float* y, cudaStream_t s) {
     const int groups = (m.n + 31) >> 5;
-    const int grid = std::min(num_sms(), (groups + kV2Warps - 1) / kV2Warps);
-    k_mv2<<<grid, kV2Threads, mv2_smem(m.k), s>>>(m, static_cast<const uint8_t*>(q), y);
+    int grid, threads;
+    spread(groups, kV2Warps, grid, threads);
+    k_mv2<<<grid, threads, mv2_smem(m.k), s>>>(m, static_cast<const uint8_t*>(q), y);
     return cudaGetLastError();
 }
 

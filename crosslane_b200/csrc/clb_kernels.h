@@ -47,14 +47,14 @@ cudaError_t launch_pack(const uint8_t* aos, uint8_t* packed, const PackedLayout&
 
 // v2 (row-per-thread decode, persistent CTAs, fused SwiGLU+Q8_K(h) and combine)
 cudaError_t set_v2_smem_limits();
-size_t gateup2_smem(int dim);
+size_t gateup2_smem(int dim, int warps);
 size_t down2_smem(int npick, int ff);
 cudaError_t launch_gateup2(const ExpertDesc* experts, const int* ids, int npick, const int8_t* xqs, const float* xd,
                            int dim, int ff, float limit, float* gu, int8_t* hqs, float* hd, int* counters, int* err,
-                           cudaStream_t s);
+                           bool fast, cudaStream_t s);
 cudaError_t launch_down2(const ExpertDesc* experts, const int* ids, const float* w, int npick, const int8_t* hqs,
                          const float* hd, int dim, int ff, const float* shared, const float* resid, float* out,
-                         float* yrows, int* counters, int* err, cudaStream_t s);
+                         float* yrows, int* counters, int* err, bool fast, cudaStream_t s);
 cudaError_t launch_mv2(const PackedMat& m, const void* q, float* y, cudaStream_t s);
 
 }  // namespace clb

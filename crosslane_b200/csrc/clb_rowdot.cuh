@@ -36,15 +36,15 @@ constexpr uint32_t kPos2 = 0x002B1908u;  // +8, +25, +43
 constexpr uint32_t kNeg2 = 0x00D5E7F8u;  // -8, -25, -43
 constexpr uint32_t kVal1 = 0x000100FFu;  // -1, 0, +1
 
-__device__ __forceinline__ uint32_t prmt2(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-    return r;
-}
-__device__ __forceinline__ uint32_t lds32(uint32_t smem_addr) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr));
-    return v;
+// Byte permute (PTX prmt.b32, default mode) through the intrinsic, so constant operands
+// become immediates instead of registers the compiler re-materialises.
+__device__ __forceinline__ uint32_t prmt2(uint32_t a, uint32_t b, uint32_t sel) { return __byte_perm(a, b, sel); }
+// Table word at byte offset `off` of the kernel's dynamic shared memory. Indexing the
+// extern __shared__ array directly lets the compiler fold its base into the load's
+// immediate and schedule the load early.
+extern __shared__ __align__(16) uint8_t clb_dyn_smem[];
+__device__ __forceinline__ uint32_t tab32(uint32_t off) {
+    return *reinterpret_cast<const uint32_t*>(clb_dyn_smem + off);
 }
 __device__ __forceinline__ int dp4a_s(uint32_t a, uint32_t b) {
     return __dp4a((int)a, (int)b, 0);
@@ -54,23 +54,27 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 
 // Compact selectors (256 + 512 + 2048 + 128 words, clb_kernels.h layout) -> replicated
-// shared-memory tables. Called by every thread of the CTA; caller syncs afterwards.
-__device__ __forceinline__ void fill_row_tables(const uint32_t* __restrict__ compact, uint8_t* smem) {
-    // region A: 4096 x 16 B stores (slot i: 8 stores of grid, 8 stores of sign)
-    for (int s = threadIdx.x; s < 4096; s += blockDim.x) {
+// shared-memory tables, using `stage` (2944 words of shared memory past the tables) to
+// read the compact copy from global memory once with independent loads. Called by every
+// thread of the CTA; the caller syncs afterwards.
+__device__ __forceinline__ void fill_row_tables(const uint32_t* __restrict__ compact, uint32_t* stage) {
+    for (int i = threadIdx.x; i < 2944; i += blockDim.x) stage[i] = __ldg(compact + i);
+    __syncthreads();
+    uint4* a = reinterpret_cast<uint4*>(clb_dyn_smem + kRowTabXXS);
+    for (int s = threadIdx.x; s < 4096; s += blockDim.x) {  // slot i: 8 x grid, 8 x sign
         const int slot = s >> 4, part = s & 15;
-        const uint32_t v = part < 8 ? compact[slot] : compact[2816 + (slot & 127)];
-        reinterpret_cast<uint4*>(smem + kRowTabXXS)[s] = make_uint4(v, v, v, v);
+        const uint32_t v = part < 8 ? stage[slot] : stage[2816 + (slot & 127)];
+        a[s] = make_uint4(v, v, v, v);
     }
-    // region B: 512 entries x 16 copies = 2048 x 16 B
-    for (int s = threadIdx.x; s < 2048; s += blockDim.x) {
-        const uint32_t v = compact[256 + (s >> 2)];
-        reinterpret_cast<uint4*>(smem + kRowTabXS)[s] = make_uint4(v, v, v, v);
+    uint4* b = reinterpret_cast<uint4*>(clb_dyn_smem + kRowTabXS);
+    for (int s = threadIdx.x; s < 2048; s += blockDim.x) {  // 512 entries x 16 copies
+        const uint32_t v = stage[256 + (s >> 2)];
+        b[s] = make_uint4(v, v, v, v);
     }
-    // region C: 2048 entries x 4 copies = 2048 x 16 B
-    for (int s = threadIdx.x; s < 2048; s += blockDim.x) {
-        const uint32_t v = compact[768 + s];
-        reinterpret_cast<uint4*>(smem + kRowTabIQ1)[s] = make_uint4(v, v, v, v);
+    uint4* c = reinterpret_cast<uint4*>(clb_dyn_smem + kRowTabIQ1);
+    for (int s = threadIdx.x; s < 2048; s += blockDim.x) {  // 2048 entries x 4 copies
+        const uint32_t v = stage[768 + s];
+        c[s] = make_uint4(v, v, v, v);
     }
 }
 
@@ -80,6 +84,36 @@ struct RowRaw {
     uint2 sc;              // IQ2_XS scale bytes / IQ1_M scale words
     uint16_t d;            // IQ2 fp16 super-scale
 };
+
+// 128/64/16-bit global loads through the non-coherent path that the compiler may not
+// move: a prefetch issued with them really starts a round ahead of its use.
+__device__ __forceinline__ uint4 ldg_v4_early(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ldg_v2_early(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint16_t ldg_u16_early(const void* p) {
+    uint16_t v;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+
+template <int T>
+__device__ __forceinline__ void load_raw_early(const PackedMat& m, int row, int b, RowRaw& r) {
+    const size_t n = (size_t)m.n;
+    const uint8_t* p = m.body + ((size_t)b * (T == CLB_IQ1_M ? 3 : 4) * n + (size_t)row) * 16;
+    r.b0 = ldg_v4_early(p);
+    r.b1 = ldg_v4_early(p + n * 16);
+    r.b2 = ldg_v4_early(p + n * 32);
+    if (T != CLB_IQ1_M) r.b3 = ldg_v4_early(p + n * 48);
+    if (T != CLB_IQ2_XXS) r.sc = ldg_v2_early(m.sc + ((size_t)b * n + row) * 8);
+    if (T != CLB_IQ1_M) r.d = ldg_u16_early(m.d + (size_t)b * n + row);
+}
 
 template <int T>
 __device__ __forceinline__ void load_raw(const PackedMat& m, int row, int b, RowRaw& r) {
@@ -109,10 +143,9 @@ __device__ __forceinline__ float raw_scale(const RowRaw& r) {
 }
 
 // Lane integers of one block. q: the block's 256 activation int8 in shared memory (16 B
-// aligned). tab: shared address of the table region base. lb = lane*4.
+// aligned). Tables sit at offset 0 of the dynamic shared memory. lb = lane*4.
 template <int T>
-__device__ __forceinline__ void block_lanes(const RowRaw& r, const int8_t* q, uint32_t tab, uint32_t lb, int I[8],
-                                            int D[8]) {
+__device__ __forceinline__ void block_lanes(const RowRaw& r, const int8_t* q, uint32_t lb, int I[8], int D[8]) {
 #pragma unroll
     for (int L = 0; L < 8; ++L) I[L] = D[L] = 0;
 #pragma unroll
@@ -129,7 +162,7 @@ __device__ __forceinline__ void block_lanes(const RowRaw& r, const int8_t* q, ui
                 const uint32_t sel_j = 0x5504u | ((uint32_t)j << 4);
                 const uint32_t ga = prmt2(gw, lb, sel_j);  // grid byte * 256 + lane*4
                 const uint32_t sa = prmt2(sw, lb, sel_j);  // sign byte * 256 + lane*4
-                const uint32_t sel = lds32(tab + kRowTabXXS + ga) + lds32(tab + kRowTabXXS + 128 + sa);
+                const uint32_t sel = tab32(kRowTabXXS + ga) + tab32(kRowTabXXS + 128 + sa);
                 const uint32_t lo = prmt2(kPos2, kNeg2, sel), hi = prmt2(kPos2, kNeg2, sel >> 16);
                 I[2 * j] += scale * dp4a_s(lo, qv[2 * j]);
                 I[2 * j + 1] += scale * dp4a_s(hi, qv[2 * j + 1]);
@@ -143,7 +176,7 @@ __device__ __forceinline__ void block_lanes(const RowRaw& r, const int8_t* q, ui
                 const uint32_t code = (j & 1) ? (w >> 16) : (w & 0xffffu);
                 const uint32_t ga = (code & 511u) * 64u + (lb & 60u);
                 const uint32_t sa = (code >> 9) * 256u + 128u + lb;
-                const uint32_t sel = lds32(tab + kRowTabXS + ga) + lds32(tab + kRowTabXXS + sa);
+                const uint32_t sel = tab32(kRowTabXS + ga) + tab32(kRowTabXXS + sa);
                 const uint32_t lo = prmt2(kPos2, kNeg2, sel), hi = prmt2(kPos2, kNeg2, sel >> 16);
                 const int s = j < 2 ? s_lo : s_hi;
                 I[2 * j] += s * dp4a_s(lo, qv[2 * j]);
@@ -159,7 +192,7 @@ __device__ __forceinline__ void block_lanes(const RowRaw& r, const int8_t* q, ui
             for (int j = 0; j < 4; ++j) {
                 const uint32_t nib = (qh16 >> (4 * j)) & 15u;
                 const uint32_t idx = ((qsw >> (8 * j)) & 0xffu) | ((nib & 7u) << 8);
-                const uint32_t sel = lds32(tab + kRowTabIQ1 + idx * 16u + (lb & 12u));
+                const uint32_t sel = tab32(kRowTabIQ1 + idx * 16u + (lb & 12u));
                 const uint32_t lo = prmt2(kVal1, 0u, sel), hi = prmt2(kVal1, 0u, sel >> 16);
                 const int s = j < 2 ? s_lo : s_hi;
                 I[2 * j] += s * dp4a_s(lo, qv[2 * j]);
@@ -168,6 +201,73 @@ __device__ __forceinline__ void block_lanes(const RowRaw& r, const int8_t* q, ui
                 D[2 * j] += sd * __dp4a((int)qv[2 * j], 0x01010101, 0);
                 D[2 * j + 1] += sd * __dp4a((int)qv[2 * j + 1], 0x01010101, 0);
             }
+        }
+    }
+}
+
+// Fast-math form of block_lanes: the same exact integers, summed over the 8 lanes before
+// the sub-scale is applied (the scale is per chunk for IQ2_XXS, per chunk half for
+// IQ2_XS / IQ1_M), so a block yields one main integer M and, for IQ1_M, one delta
+// integer D. M = sum over lanes of the reference's I_L, D = sum of its delta lanes.
+template <int T>
+__device__ __forceinline__ void block_sum(const RowRaw& r, const int8_t* q, uint32_t lb, int& M, int& D) {
+    M = 0;
+    D = 0;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint4 qa = *reinterpret_cast<const uint4*>(q + 32 * c);
+        const uint4 qb = *reinterpret_cast<const uint4*>(q + 32 * c + 16);
+        const uint32_t qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        if (T == CLB_IQ2_XXS) {
+            const uint32_t gw = rw(r, 2 * c), sw = rw(r, 2 * c + 1);
+            const int scale = (int)((((sw & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27);
+            int a0 = 0, a1 = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t sel_j = 0x5504u | ((uint32_t)j << 4);
+                const uint32_t ga = prmt2(gw, lb, sel_j), sa = prmt2(sw, lb, sel_j);
+                const uint32_t sel = tab32(kRowTabXXS + ga) + tab32(kRowTabXXS + 128 + sa);
+                a0 = __dp4a((int)prmt2(kPos2, kNeg2, sel), (int)qv[2 * j], a0);
+                a1 = __dp4a((int)prmt2(kPos2, kNeg2, sel >> 16), (int)qv[2 * j + 1], a1);
+            }
+            M += scale * (a0 + a1);
+        } else if (T == CLB_IQ2_XS) {
+            const uint32_t scb = ((c < 4 ? r.sc.x : r.sc.y) >> (8 * (c & 3))) & 0xffu;
+            const int s_lo = (int)((scb & 15u) << 1) | 1, s_hi = (int)((scb >> 4) << 1) | 1;
+            int alo = 0, ahi = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t w = rw(r, 2 * c + (j >> 1));
+                const uint32_t code = (j & 1) ? (w >> 16) : (w & 0xffffu);
+                const uint32_t sel = tab32(kRowTabXS + (code & 511u) * 64u + (lb & 60u)) +
+                                     tab32(kRowTabXXS + (code >> 9) * 256u + 128u + lb);
+                int& a = j < 2 ? alo : ahi;
+                a = __dp4a((int)prmt2(kPos2, kNeg2, sel), (int)qv[2 * j], a);
+                a = __dp4a((int)prmt2(kPos2, kNeg2, sel >> 16), (int)qv[2 * j + 1], a);
+            }
+            M += s_lo * alo + s_hi * ahi;
+        } else {
+            const uint32_t qsw = rw(r, c);
+            const uint32_t qh16 = (rw(r, 8 + (c >> 1)) >> (16 * (c & 1))) & 0xffffu;
+            const uint32_t scw = ((c < 4 ? r.sc.x : r.sc.y) >> (16 * ((c >> 1) & 1))) & 0xffffu;
+            const int s_lo = (int)(((scw >> (6 * (c & 1))) & 7u) << 1) | 1;
+            const int s_hi = (int)(((scw >> (6 * (c & 1) + 3)) & 7u) << 1) | 1;
+            int alo = 0, ahi = 0, dlo = 0, dhi = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t nib = (qh16 >> (4 * j)) & 15u;
+                const uint32_t idx = ((qsw >> (8 * j)) & 0xffu) | ((nib & 7u) << 8);
+                const uint32_t sel = tab32(kRowTabIQ1 + idx * 16u + (lb & 12u));
+                int& a = j < 2 ? alo : ahi;
+                a = __dp4a((int)prmt2(kVal1, 0u, sel), (int)qv[2 * j], a);
+                a = __dp4a((int)prmt2(kVal1, 0u, sel >> 16), (int)qv[2 * j + 1], a);
+                // delta: +-1 per group times the group's 8 activations
+                const int qs8 = __dp4a((int)qv[2 * j], 0x01010101, __dp4a((int)qv[2 * j + 1], 0x01010101, 0));
+                int& dd = j < 2 ? dlo : dhi;
+                dd += (nib & 8u) ? -qs8 : qs8;
+            }
+            M += s_lo * alo + s_hi * ahi;
+            D += s_lo * dlo + s_hi * dhi;
         }
     }
 }

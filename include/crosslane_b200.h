@@ -103,8 +103,18 @@ typedef struct clb_bank_config_v1 {
     float limit;           /* SwiGLU clamp, 0 = none (crosslane's model uses 10) */
     int32_t expert_begin;  /* this bank owns experts [expert_begin, expert_end) of */
     int32_t expert_end;    /*   every layer (expert-ID sharding); 0,0 = all */
-    int32_t reserved[7];
+    int32_t flags;         /* CLB_BANK_* bits below; other bits must be 0 */
+    int32_t reserved[6];
 } clb_bank_config_v1;
+
+/* Summation order of the routed-expert row dots.
+ * Default (flag clear): each row's 256-value blocks are split into contiguous segments,
+ *   one per thread, whose fp32 partials are added in a fixed tree. Results are
+ *   run-to-run bit-identical and agree with the reference CPU lane to fp32
+ *   reassociation (well inside 1e-3 relative L2).
+ * CLB_BANK_EXACT_ORDER: the reference's own order (8 lane chains, per-block fma in block
+ *   order, q8k_core.hpp:43-91), bit-identical to the CPU lane, at lower throughput. */
+#define CLB_BANK_EXACT_ORDER 1
 
 /* Creates a bank and its fixed workspace on `device` (no allocation afterwards).
  * Replaces the construction half of HipResidentBank::load

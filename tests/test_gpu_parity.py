@@ -178,20 +178,32 @@ def _route(orc, rng, n_experts, k):
     return orc.route_sigmoid(logits, k)
 
 
-@pytest.fixture(scope="module")
-def bank_c1(cb):
+MODES = pytest.mark.parametrize("exact", [False, True], ids=["fast", "exact"])
+
+
+def _check_layer(got, want, exact):
+    """Both summation orders stay inside the tolerance; the exact order is bit-identical."""
+    assert rel_l2(got, want) <= REL_L2 and max_abs_rel(got, want) <= MAX_ABS_REL
+    if exact:
+        assert np.array_equal(bits(got), bits(want)), f"{np.count_nonzero(bits(got) != bits(want))} outputs differ"
+
+
+@pytest.fixture(scope="module", params=[False, True], ids=["fast", "exact"])
+def bank_c1(cb, request):
     """one layer, 384 IQ2_XXS experts, 7168 x 1536."""
-    b = cb.ExpertBank(n_layers=1, n_experts=384, dim=7168, ff=1536, max_picks=6)
+    b = cb.ExpertBank(n_layers=1, n_experts=384, dim=7168, ff=1536, max_picks=6, exact_order=request.param)
     b.fill_synthetic(1234, 0)
+    b.exact = request.param
     yield b
     b.close()
 
 
-@pytest.fixture(scope="module")
-def bank_c2(cb):
+@pytest.fixture(scope="module", params=[False, True], ids=["fast", "exact"])
+def bank_c2(cb, request):
     """one layer, experts 0-127 IQ2_XXS, 128-255 IQ2_XS, 256-383 IQ1_M."""
-    b = cb.ExpertBank(n_layers=1, n_experts=384, dim=7168, ff=1536, max_picks=6)
+    b = cb.ExpertBank(n_layers=1, n_experts=384, dim=7168, ff=1536, max_picks=6, exact_order=request.param)
     b.fill_synthetic(4321, 1)
+    b.exact = request.param
     yield b
     b.close()
 
@@ -203,8 +215,9 @@ def test_config1_layer(bank_c1, orc):
         x = rng.standard_normal(7168).astype(np.float32)
         got = bank_c1.layer_execute(0, ids, w, x)
         want = orc.layer_synth(0, 1234, 0, ids, w, x, 7168, 1536)
-        assert rel_l2(got, want) <= REL_L2 and max_abs_rel(got, want) <= MAX_ABS_REL
-        print(f"config1 trial {trial}: rel_l2={rel_l2(got, want):.3e} exact={np.mean(bits(got) == bits(want)):.4f}")
+        _check_layer(got, want, bank_c1.exact)
+        again = bank_c1.layer_execute(0, ids, w, x)
+        assert np.array_equal(bits(got), bits(again))  # run-to-run identical in both orders
 
 
 def test_config2_layer_mixed(bank_c2, orc):
@@ -216,7 +229,24 @@ def test_config2_layer_mixed(bank_c2, orc):
     shared = rng.standard_normal(7168).astype(np.float32) * 0.1
     got = bank_c2.layer_execute(0, ids, w, x, shared)
     want = orc.layer_synth(1, 4321, 0, ids, w, x, 7168, 1536, shared=shared)
-    assert rel_l2(got, want) <= REL_L2 and max_abs_rel(got, want) <= MAX_ABS_REL
+    _check_layer(got, want, bank_c2.exact)
+
+
+@pytest.mark.parametrize("dim,ff,seed", [(2048, 512, 11), (5120, 2304, 12), (1280, 768, 13), (256, 256, 14)])
+def test_fast_order_odd_segments(cb, orc, dim, ff, seed):
+    """Block counts that do not split evenly over the 4 (gate/up) and 2 (down) segments."""
+    b = cb.ExpertBank(n_layers=1, n_experts=8, dim=dim, ff=ff, max_picks=3)
+    try:
+        b.fill_synthetic(seed, 2)
+        rng = np.random.default_rng(seed)
+        ids = np.array([6, 1, 3], np.int32)
+        w = np.array([0.5, 0.3, 0.2], np.float32)
+        x = rng.standard_normal(dim).astype(np.float32)
+        got = b.layer_execute(0, ids, w, x)
+        want = orc.layer_synth(2, seed, 0, ids, w, x, dim, ff)
+        _check_layer(got, want, False)
+    finally:
+        b.close()
 
 
 def test_compute_many_rows(bank_c2, orc):
@@ -251,10 +281,11 @@ def test_reference_geometry_clamp(cb, orc):
         b.close()
 
 
-def test_stack_decode_three_layers(cb, orc):
+@MODES
+def test_stack_decode_three_layers(cb, orc, exact):
     """Config 3 shape on 3 layers: mixed types per (layer, expert), h += layer(RMSNorm(h))."""
     L, E = 3, 384
-    b = cb.ExpertBank(n_layers=L, n_experts=E, dim=7168, ff=1536, max_picks=6)
+    b = cb.ExpertBank(n_layers=L, n_experts=E, dim=7168, ff=1536, max_picks=6, exact_order=exact)
     try:
         b.fill_synthetic(2024, 2)
         rng = np.random.default_rng(5)
@@ -265,7 +296,7 @@ def test_stack_decode_three_layers(cb, orc):
         assert np.array_equal(bits(got), bits(got2))
         want = orc.stack(2, 2024, x0, logits, 7168, 1536)
         assert np.all(np.isfinite(got))
-        assert rel_l2(got, want) <= REL_L2 and max_abs_rel(got, want) <= MAX_ABS_REL
+        _check_layer(got, want, exact)
     finally:
         b.close()
 
