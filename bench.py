@@ -8,11 +8,14 @@ intermediate 1536, IQ2_XXS / IQ2_XS / IQ1_M drawn per (layer, expert) from the s
 logits (uniformly random experts), x_{l+1} = x_l + combine_l. One step = one token
 through all 40 layers.
 
-  value  : tokens/s with inputs resident in HBM, CUDA events on the bank stream.
-  e2e    : tokens/s through clb_stack_decode (host x and logits in, host x out).
-  roofline: the gate/up kernel, timed alone with CUDA events right after the timed
-           region on the same kind of inputs; algorithmic bytes = packed gate+up
-           payload of the picked experts + Q8_K(x) in + h out.
+  value  : tokens/s with inputs resident in HBM, CUDA events on the bank stream (one
+           routing kernel + one persistent stack kernel per token).
+  e2e    : tokens/s through clb_stack_decode (host x and logits in, host routing,
+           x + routes up, h down).
+  roofline: the persistent stack kernel (clb::k_stack), which is the whole timed step
+           apart from the routing kernel: achieved = algorithmic bytes of one token (the
+           packed gate+up+down payload of every picked expert of every layer + the
+           residual stream in/out) / the CUDA-event step time.
   cpu_baseline: crosslane's own CPU-lane arithmetic (q8k_core.hpp, built into
            oracle/_ref/libref.so) on a persistent 64-row-job team over all host
            threads, one token-layer sample, extrapolated to the 40-layer stack.
@@ -52,7 +55,7 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks/throttle reasons sampled every 50 ms during the timed region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -66,7 +69,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -171,7 +174,7 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS, help="smaller stacks for quick checks only")
@@ -265,64 +268,35 @@ def main():
         t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = {"value": world * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * DIM + 4 * L * EXPERTS,
+    e2e = {"value": world * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * DIM + 8 * L * PICKS,
            "d2h_bytes_per_step": 4 * DIM}
 
-    # ---- roofline pass: the gate/up kernel alone, events around each launch ----
+    # ---- roofline: algorithmic bytes of one token through the stack kernel ----
     peak, peak_kind = peaks()
-    d_ids = torch.empty(PICKS, dtype=torch.int32, device="cuda")
-    d_w = torch.empty(PICKS, dtype=torch.float32, device="cuda")
-    d_out = torch.empty(DIM, dtype=torch.float32, device="cuda")
-    gu_bytes, gu_ms, dn_bytes, dn_ms = 0, 0.0, 0, 0.0
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    launches_timed = 0
-    for tok in range(min(args.steps, 8)):
+    step_bytes = []
+    for i in range(args.steps):
+        tok = args.warmup + i
+        nbytes = 8 * DIM  # residual stream in and out
         for layer in range(L):
-            ids, w = cb.route_host(0, logits[tok, layer], PICKS)
-            with torch.cuda.stream(stream):
-                d_ids.copy_(torch.from_numpy(ids), non_blocking=False)
-                d_w.copy_(torch.from_numpy(w), non_blocking=False)
-                d_x.copy_(d_xs[tok])
-            bank.layer_phases_device(layer, d_ids, d_w, d_x, d_out, 1, stream=bank.stream)
-            evs[0].record(stream)
-            bank.layer_phases_device(layer, d_ids, d_w, d_x, d_out, 2, stream=bank.stream)
-            evs[1].record(stream)
-            evs[2].record(stream)
-            bank.layer_phases_device(layer, d_ids, d_w, d_x, d_out, 8, stream=bank.stream)
-            evs[3].record(stream)
-            evs[3].synchronize()
-            gu_ms += evs[0].elapsed_time(evs[1])
-            dn_ms += evs[2].elapsed_time(evs[3])
-            launches_timed += 1
-            for e in ids:
-                t, payload = bank.expert_info(layer, int(e))
-                per = payload // 3  # gate, up and down carry the same number of weights
-                gu_bytes += 2 * per
-                dn_bytes += per
-            gu_bytes += DIM + 4 * (DIM // 256) + PICKS * FF + 4 * PICKS * (FF // 256)  # Q8_K(x) in, Q8_K(h) out
-            dn_bytes += PICKS * FF + 4 * PICKS * (FF // 256) + 8 * DIM  # Q8_K(h) in, residual in, out
-    gu_avg_s = gu_ms / 1e3 / launches_timed
-    gu_achieved = gu_bytes / launches_timed / gu_avg_s / 1e9
-    dn_achieved = dn_bytes / launches_timed / (dn_ms / 1e3 / launches_timed) / 1e9
+            ids, _ = cb.route_host(0, logits[tok, layer], PICKS)
+            nbytes += sum(bank.expert_info(layer, int(e))[1] for e in ids)
+        step_bytes.append(nbytes)
+    bytes_per_step = float(np.mean(step_bytes))
+    step_gbs = bytes_per_step / (ms_per_step / 1e3) / 1e9
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "k_gateup2_traffic.json")
+    tp = os.path.join(ROOT, "profiles", "k_stack_traffic.json")
     if os.path.exists(tp):
         with open(tp) as f:
-            traffic = json.load(f).get("bytes_per_launch")
-    roofline = {"bound": "hbm", "achieved": round(gu_achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(gu_achieved / peak, 4), "traffic": traffic, "kernel": "clb::k_gateup2",
+            t = json.load(f)
+        # measured DRAM bytes per token-layer on a small capture, scaled to this stack
+        traffic = round(t["dram_bytes_per_token_layer"] * L) if "dram_bytes_per_token_layer" in t else None
+    roofline = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(step_gbs / peak, 4), "traffic": traffic, "kernel": "clb::k_stack",
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6650 GB/s",
-                "algorithmic_bytes_per_launch": int(gu_bytes / launches_timed),
-                "avg_launch_us": round(gu_avg_s * 1e6, 2),
-                "down_combine_achieved_gbs": round(dn_achieved, 1)}
-
-    # whole-step effective bandwidth (algorithmic bytes per token / time per token)
-    step_bytes = 0
-    for layer in range(L):
-        ids, _ = cb.route_host(0, logits[args.warmup, layer], PICKS)
-        step_bytes += sum(bank.expert_info(layer, int(e))[1] for e in ids) + 8 * DIM
-    step_gbs = step_bytes / (ms_per_step / 1e3) / 1e9
+                "algorithmic_bytes_per_launch": int(bytes_per_step),
+                "avg_launch_us": round(ms_per_step * 1e3, 2),
+                "launch_timing": "CUDA events around each step's routing + stack launches"}
 
     cpu = None
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
@@ -343,10 +317,9 @@ def main():
                    "bank_gb": round(bank.weight_bytes / 1e9, 2), "fill_s": round(fill_s, 1)},
         "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in e2e.items()},
         "roofline": roofline,
-        "step_hbm_gbs": round(step_gbs, 1), "step_frac": round(step_gbs / peak, 4),
         "cpu_baseline": cpu,
         "clocks": clk,
-        "gpu_launches": (1 + 3 * L) * args.steps,
+        "gpu_launches": 2 * args.steps if bank.persistent else (1 + 3 * L) * args.steps,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -16,6 +16,7 @@ from ._capi import BankConfigV1, ErrorV1, HOST_EXPERT_FN, check, lib
 IQ2_XXS, IQ2_XS, IQ1_M = 16, 17, 29
 BLOCK_BYTES = {IQ2_XXS: 66, IQ2_XS: 74, IQ1_M: 56}
 EXACT_ORDER = 1  # CLB_BANK_EXACT_ORDER
+PER_LAYER_KERNELS = 2  # CLB_BANK_PER_LAYER_KERNELS
 ROLE_GATE, ROLE_UP, ROLE_DOWN = 0, 1, 2
 Q8K_BLOCK_BYTES = 292
 
@@ -44,10 +45,11 @@ class ExpertBank:
 
     def __init__(self, *, n_layers: int, n_experts: int, dim: int, ff: int, max_picks: int = 6,
                  limit: float = 0.0, device: int = 0, expert_begin: int = 0, expert_end: int = 0,
-                 exact_order: bool = False):
+                 exact_order: bool = False, per_layer_kernels: bool = False):
+        flags = (EXACT_ORDER if exact_order else 0) | (PER_LAYER_KERNELS if per_layer_kernels else 0)
         cfg = BankConfigV1(device=device, n_layers=n_layers, n_experts=n_experts, dim=dim, ff=ff,
                            max_picks=max_picks, limit=limit, expert_begin=expert_begin, expert_end=expert_end,
-                           flags=EXACT_ORDER if exact_order else 0)
+                           flags=flags)
         err = ErrorV1()
         h = C.c_void_p()
         check(lib.clb_bank_create(C.byref(cfg), C.byref(h), C.byref(err)), err)
@@ -84,6 +86,11 @@ class ExpertBank:
         buf = np.ascontiguousarray(ggml, dtype=np.uint8)
         err = ErrorV1()
         check(lib.clb_bank_load_matrix(self._h, layer, expert, role, qtype, _ptr(buf), buf.nbytes, C.byref(err)), err)
+
+    @property
+    def persistent(self) -> bool:
+        """Stack decode runs as the persistent kernel (else the per-layer kernels)."""
+        return bool(lib.clb_bank_stack_persistent(self._h))
 
     @property
     def weight_bytes(self) -> int:

@@ -98,6 +98,34 @@ void ensure_device_ready(int dev, cudaStream_t s) {
     g_dev_ready.insert(dev);
 }
 
+// Routing mode A (route.cpp, mode A): the k largest logits, ties to the lower id, in
+// selection order (descending logit); w_i = sigmoid(l_i) / sum of the selected sigmoids
+// taken in that order. One pass with an insertion-sorted top-k list gives the same
+// order as k arg-max passes. Logits must be finite.
+void route_sigmoid_host(const float* logits, int n, int k, int32_t* ids, float* w) {
+    float tv[64];
+    int ti[64], cnt = 0;
+    for (int e = 0; e < n; ++e) {
+        const float v = logits[e];
+        if (cnt == k && !(v > tv[k - 1])) continue;
+        int pos = cnt < k ? cnt++ : k - 1;
+        while (pos > 0 && v > tv[pos - 1]) {
+            tv[pos] = tv[pos - 1];
+            ti[pos] = ti[pos - 1];
+            --pos;
+        }
+        tv[pos] = v;
+        ti[pos] = e;
+    }
+    float s[64], sum = 0.0f;
+    for (int i = 0; i < k; ++i) {
+        ids[i] = ti[i];
+        s[i] = 1.0f / (1.0f + std::exp(-tv[i]));
+        sum += s[i];
+    }
+    for (int i = 0; i < k; ++i) w[i] = s[i] / sum;
+}
+
 bool finite_all(const float* v, size_t n) {
     for (size_t i = 0; i < n; ++i)
         if (!std::isfinite(v[i])) return false;
@@ -128,10 +156,14 @@ struct clb_bank {
     float* d_gu = nullptr;          // gate/up rows [pick][2][ff]
     int* d_cnt_h = nullptr;         // last-arriver counters per (pick, 256-row block of h)
     int* d_cnt_y = nullptr;         // last-arriver counters per output row group (16 or 32 rows)
+    unsigned* d_bar = nullptr;      // grid barrier state of the persistent stack kernel
+    bool persistent = false;        // stack decode runs as one persistent kernel
     float* d_logits = nullptr;
     int* d_route_ids = nullptr;
     float* d_route_w = nullptr;
     float *h_x = nullptr, *h_out = nullptr, *h_logits = nullptr, *h_yrows = nullptr;
+    int32_t* h_route_ids = nullptr;  // host-routed stack: [layers][max_picks]
+    float* h_route_w = nullptr;
     std::map<std::pair<uint32_t, int>, cudaGraphExec_t> graphs, device_graphs;
     const float* graph_dx = nullptr;
 
@@ -139,6 +171,7 @@ struct clb_bank {
     size_t E() const { return (size_t)cfg.n_experts; }
     bool owns(int e) const { return e >= cfg.expert_begin && e < cfg.expert_end; }
     bool fast() const { return (cfg.flags & CLB_BANK_EXACT_ORDER) == 0; }
+    bool use_persistent() const { return persistent; }
 
     template <class T>
     T* dev_alloc(size_t count) {
@@ -179,6 +212,7 @@ struct clb_bank {
         cuda_check(cudaStreamSynchronize(stream), "stream sync");
         if (flag) {
             cuda_check(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "error flag reset");
+            if (flag == 2) throw Error(CLB_E_CUDA, "grid barrier of the stack kernel timed out");
             throw Error(CLB_E_INVALID, "a picked expert is not resident or has a mismatched shape");
         }
     }
@@ -227,9 +261,17 @@ struct clb_bank {
                        "down + combine");
     }
 
+    // dlogits == nullptr: d_route_ids / d_route_w already hold the routing of the range.
     void enqueue_stack(uint32_t first, int nl, float* dx, const float* dlogits, cudaStream_t s) {
         const int k = cfg.max_picks;
-        cuda_check(clb::launch_route_sigmoid(dlogits, cfg.n_experts, k, nl, d_route_ids, d_route_w, s), "route");
+        if (dlogits)
+            cuda_check(clb::launch_route_sigmoid(dlogits, cfg.n_experts, k, nl, d_route_ids, d_route_w, s), "route");
+        if (persistent) {
+            cuda_check(clb::launch_stack(d_desc, cfg.n_experts, (int)first, nl, k, d_route_ids, d_route_w, dx, dx,
+                                         cfg.dim, cfg.ff, cfg.limit, d_gu, d_yrows, d_bar, d_err, fast(), s),
+                       "persistent stack kernel");
+            return;
+        }
         for (int i = 0; i < nl; ++i)
             enqueue_layer(first + (uint32_t)i, d_route_ids + (size_t)i * k, d_route_w + (size_t)i * k, k, dx, nullptr,
                           dx, dx, nullptr, s, true);
@@ -372,7 +414,8 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         require(cfg.max_picks >= 1 && cfg.max_picks <= clb::kMaxPicks && cfg.max_picks <= cfg.n_experts,
                 CLB_E_INVALID, "max_picks must be in [1, 16]");
         require(std::isfinite(cfg.limit) && cfg.limit >= 0, CLB_E_INVALID, "SwiGLU limit must be finite and >= 0");
-        require((cfg.flags & ~CLB_BANK_EXACT_ORDER) == 0, CLB_E_INVALID, "unknown bank flags 0x%x", cfg.flags);
+        require((cfg.flags & ~(CLB_BANK_EXACT_ORDER | CLB_BANK_PER_LAYER_KERNELS)) == 0, CLB_E_INVALID,
+                "unknown bank flags 0x%x", cfg.flags);
         require(cfg.expert_begin >= 0 && cfg.expert_begin < cfg.expert_end && cfg.expert_end <= cfg.n_experts,
                 CLB_E_INVALID, "owned expert range invalid");
         require((size_t)cfg.max_picks * (cfg.ff / 256) <= 256, CLB_E_UNSUPPORTED,
@@ -403,6 +446,9 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         bank->d_cnt_y = bank->dev_alloc<int>((dim + 15) / 16);
         cuda_check(cudaMemsetAsync(bank->d_cnt_h, 0, sizeof(int) * k * ff / 256, bank->stream), "memset");
         cuda_check(cudaMemsetAsync(bank->d_cnt_y, 0, sizeof(int) * ((dim + 15) / 16), bank->stream), "memset");
+        bank->d_bar = bank->dev_alloc<unsigned>(2);
+        bank->persistent = (cfg.flags & CLB_BANK_PER_LAYER_KERNELS) == 0 &&
+                           clb::stack_supported(cfg.dim, cfg.ff, cfg.max_picks, bank->fast());
         bank->d_ids = bank->dev_alloc<int>(k);
         bank->d_w = bank->dev_alloc<float>(k);
         bank->d_err = bank->dev_alloc<int>(1);
@@ -413,6 +459,8 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         bank->h_out = bank->host_alloc<float>(dim);
         bank->h_yrows = bank->host_alloc<float>(k * dim);
         bank->h_logits = bank->host_alloc<float>(bank->L() * bank->E());
+        bank->h_route_ids = bank->host_alloc<int32_t>(bank->L() * k);
+        bank->h_route_w = bank->host_alloc<float>(bank->L() * k);
         cuda_check(cudaMemsetAsync(bank->d_err, 0, sizeof(int), bank->stream), "memset");
         bank->upload_desc();
     });
@@ -440,6 +488,8 @@ int32_t clb_bank_contains(const clb_bank* bank, uint32_t layer, int32_t expert) 
     if (!bank || layer >= (uint32_t)bank->cfg.n_layers || expert < 0 || expert >= bank->cfg.n_experts) return 0;
     return bank->resident[(size_t)layer * bank->E() + (size_t)expert] ? 1 : 0;
 }
+
+int32_t clb_bank_stack_persistent(const clb_bank* bank) { return bank && bank->persistent ? 1 : 0; }
 
 int32_t clb_bank_fill_synthetic(clb_bank* bank, uint64_t seed, int32_t policy, clb_error_v1* err) {
     if (!bank) return fail(err, CLB_E_INVALID, "null bank");
@@ -686,18 +736,7 @@ int32_t clb_route_host(int32_t mode, const float* logits, const float* bias, int
     if (!logits || !ids || !w || n <= 0 || k <= 0 || k > n || k > 64) return CLB_E_INVALID;
     if (!finite_all(logits, (size_t)n)) return CLB_E_NONFINITE;
     if (mode == 0) {
-        std::vector<char> used((size_t)n, 0);
-        float s[64], sum = 0.0f;
-        for (int i = 0; i < k; ++i) {
-            int best = -1;
-            for (int e = 0; e < n; ++e)
-                if (!used[(size_t)e] && (best < 0 || logits[e] > logits[best])) best = e;
-            used[(size_t)best] = 1;
-            ids[i] = best;
-            s[i] = 1.0f / (1.0f + std::exp(-logits[best]));
-            sum += s[i];
-        }
-        for (int i = 0; i < k; ++i) w[i] = s[i] / sum;
+        route_sigmoid_host(logits, n, k, ids, w);
         return CLB_OK;
     }
     if (mode != 1 || !bias) return CLB_E_INVALID;
@@ -739,25 +778,42 @@ int32_t clb_stack_decode(clb_bank* bank, uint32_t first, int32_t nl, const float
                 require(bank->resident[(size_t)(first + l) * bank->E() + (size_t)e], CLB_E_INVALID,
                         "expert (%u, %d) not resident", first + l, e);
         DeviceGuard g(c.device);
+        require(finite_all(logits, (size_t)nl * c.n_experts), CLB_E_NONFINITE, "non-finite router logits");
         bank->device_step([&] {
+            // Routing on the host (route.cpp's order and libm), then x and the routes go
+            // up; one stack launch (or the captured per-layer graph) and h comes back.
+            const int k = c.max_picks;
             std::memcpy(bank->h_x, x, sizeof(float) * c.dim);
-            std::memcpy(bank->h_logits, logits, sizeof(float) * (size_t)nl * c.n_experts);
+            for (int l = 0; l < nl; ++l)
+                route_sigmoid_host(logits + (size_t)l * c.n_experts, c.n_experts, k, bank->h_route_ids + (size_t)l * k,
+                                   bank->h_route_w + (size_t)l * k);
+            auto enqueue_all = [&] {
+                cuda_check(cudaMemcpyAsync(bank->d_x, bank->h_x, sizeof(float) * c.dim, cudaMemcpyHostToDevice,
+                                           bank->stream),
+                           "x H2D");
+                cuda_check(cudaMemcpyAsync(bank->d_route_ids, bank->h_route_ids, sizeof(int32_t) * (size_t)nl * k,
+                                           cudaMemcpyHostToDevice, bank->stream),
+                           "route ids H2D");
+                cuda_check(cudaMemcpyAsync(bank->d_route_w, bank->h_route_w, sizeof(float) * (size_t)nl * k,
+                                           cudaMemcpyHostToDevice, bank->stream),
+                           "route weights H2D");
+                bank->enqueue_stack(first, nl, bank->d_x, nullptr, bank->stream);
+                cuda_check(cudaMemcpyAsync(bank->h_out, bank->d_x, sizeof(float) * c.dim, cudaMemcpyDeviceToHost,
+                                           bank->stream),
+                           "out D2H");
+            };
+            if (bank->persistent) {  // one kernel: no graph needed
+                enqueue_all();
+                bank->check_err_flag();
+                return;
+            }
             auto key = std::make_pair(first, nl);
             auto it = bank->graphs.find(key);
             if (it == bank->graphs.end()) {
                 cudaGraph_t graph = nullptr;
                 cuda_check(cudaStreamBeginCapture(bank->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
                 try {
-                    cuda_check(cudaMemcpyAsync(bank->d_x, bank->h_x, sizeof(float) * c.dim, cudaMemcpyHostToDevice,
-                                               bank->stream),
-                               "x H2D");
-                    cuda_check(cudaMemcpyAsync(bank->d_logits, bank->h_logits, sizeof(float) * (size_t)nl * c.n_experts,
-                                               cudaMemcpyHostToDevice, bank->stream),
-                               "logits H2D");
-                    bank->enqueue_stack(first, nl, bank->d_x, bank->d_logits, bank->stream);
-                    cuda_check(cudaMemcpyAsync(bank->h_out, bank->d_x, sizeof(float) * c.dim, cudaMemcpyDeviceToHost,
-                                               bank->stream),
-                               "out D2H");
+                    enqueue_all();
                 } catch (...) {
                     cudaStreamEndCapture(bank->stream, &graph);
                     if (graph) cudaGraphDestroy(graph);
@@ -788,6 +844,10 @@ int32_t clb_stack_decode_device(clb_bank* bank, uint32_t first, int32_t nl, floa
                 "invalid stack arguments");
         DeviceGuard g(c.device);
         bank->device_step([&] {
+            if (bank->persistent) {
+                bank->enqueue_stack(first, nl, d_x, d_logits, bank->stream);
+                return;
+            }
             // Graphs are keyed by layer range and bound to (d_x, d_logits) of their capture.
             auto key = std::make_pair(first, nl);
             auto it = bank->device_graphs.find(key);

@@ -57,4 +57,11 @@ cudaError_t launch_down2(const ExpertDesc* experts, const int* ids, const float*
                          float* yrows, int* counters, int* err, bool fast, cudaStream_t s);
 cudaError_t launch_mv2(const PackedMat& m, const void* q, float* y, cudaStream_t s);
 
+// persistent whole-stack kernel (clb_stack.cu)
+size_t stack_smem(int dim, int ff, int k, bool fast);
+bool stack_supported(int dim, int ff, int k, bool fast);
+cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
+                         const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit, float* gu,
+                         float* yrows, unsigned* bar, int* err, bool fast, cudaStream_t s);
+
 }  // namespace clb

@@ -39,6 +39,14 @@ constexpr uint32_t kVal1 = 0x000100FFu;  // -1, 0, +1
 // Byte permute (PTX prmt.b32, default mode) through the intrinsic, so constant operands
 // become immediates instead of registers the compiler re-materialises.
 __device__ __forceinline__ uint32_t prmt2(uint32_t a, uint32_t b, uint32_t sel) { return __byte_perm(a, b, sel); }
+// The same permute with a run-time selector taken from the tables: every selector nibble
+// there is 0..6 (bit 3 clear), where prmt.b32 and __byte_perm agree, so the instruction
+// is issued as is (the intrinsic would first mask the selector to 3-bit nibbles).
+__device__ __forceinline__ uint32_t prmt_sel(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
 // Table word at byte offset `off` of the kernel's dynamic shared memory. Indexing the
 // extern __shared__ array directly lets the compiler fold its base into the load's
 // immediate and schedule the load early.
@@ -163,7 +171,7 @@ __device__ __forceinline__ void block_lanes(const RowRaw& r, const int8_t* q, ui
                 const uint32_t ga = prmt2(gw, lb, sel_j);  // grid byte * 256 + lane*4
                 const uint32_t sa = prmt2(sw, lb, sel_j);  // sign byte * 256 + lane*4
                 const uint32_t sel = tab32(kRowTabXXS + ga) + tab32(kRowTabXXS + 128 + sa);
-                const uint32_t lo = prmt2(kPos2, kNeg2, sel), hi = prmt2(kPos2, kNeg2, sel >> 16);
+                const uint32_t lo = prmt_sel(kPos2, kNeg2, sel), hi = prmt_sel(kPos2, kNeg2, sel >> 16);
                 I[2 * j] += scale * dp4a_s(lo, qv[2 * j]);
                 I[2 * j + 1] += scale * dp4a_s(hi, qv[2 * j + 1]);
             }
@@ -177,7 +185,7 @@ __device__ __forceinline__ void block_lanes(const RowRaw& r, const int8_t* q, ui
                 const uint32_t ga = (code & 511u) * 64u + (lb & 60u);
                 const uint32_t sa = (code >> 9) * 256u + 128u + lb;
                 const uint32_t sel = tab32(kRowTabXS + ga) + tab32(kRowTabXXS + sa);
-                const uint32_t lo = prmt2(kPos2, kNeg2, sel), hi = prmt2(kPos2, kNeg2, sel >> 16);
+                const uint32_t lo = prmt_sel(kPos2, kNeg2, sel), hi = prmt_sel(kPos2, kNeg2, sel >> 16);
                 const int s = j < 2 ? s_lo : s_hi;
                 I[2 * j] += s * dp4a_s(lo, qv[2 * j]);
                 I[2 * j + 1] += s * dp4a_s(hi, qv[2 * j + 1]);
@@ -193,7 +201,7 @@ __device__ __forceinline__ void block_lanes(const RowRaw& r, const int8_t* q, ui
                 const uint32_t nib = (qh16 >> (4 * j)) & 15u;
                 const uint32_t idx = ((qsw >> (8 * j)) & 0xffu) | ((nib & 7u) << 8);
                 const uint32_t sel = tab32(kRowTabIQ1 + idx * 16u + (lb & 12u));
-                const uint32_t lo = prmt2(kVal1, 0u, sel), hi = prmt2(kVal1, 0u, sel >> 16);
+                const uint32_t lo = prmt_sel(kVal1, 0u, sel), hi = prmt_sel(kVal1, 0u, sel >> 16);
                 const int s = j < 2 ? s_lo : s_hi;
                 I[2 * j] += s * dp4a_s(lo, qv[2 * j]);
                 I[2 * j + 1] += s * dp4a_s(hi, qv[2 * j + 1]);
@@ -227,8 +235,8 @@ __device__ __forceinline__ void block_sum(const RowRaw& r, const int8_t* q, uint
                 const uint32_t sel_j = 0x5504u | ((uint32_t)j << 4);
                 const uint32_t ga = prmt2(gw, lb, sel_j), sa = prmt2(sw, lb, sel_j);
                 const uint32_t sel = tab32(kRowTabXXS + ga) + tab32(kRowTabXXS + 128 + sa);
-                a0 = __dp4a((int)prmt2(kPos2, kNeg2, sel), (int)qv[2 * j], a0);
-                a1 = __dp4a((int)prmt2(kPos2, kNeg2, sel >> 16), (int)qv[2 * j + 1], a1);
+                a0 = __dp4a((int)prmt_sel(kPos2, kNeg2, sel), (int)qv[2 * j], a0);
+                a1 = __dp4a((int)prmt_sel(kPos2, kNeg2, sel >> 16), (int)qv[2 * j + 1], a1);
             }
             M += scale * (a0 + a1);
         } else if (T == CLB_IQ2_XS) {
@@ -242,8 +250,8 @@ __device__ __forceinline__ void block_sum(const RowRaw& r, const int8_t* q, uint
                 const uint32_t sel = tab32(kRowTabXS + (code & 511u) * 64u + (lb & 60u)) +
                                      tab32(kRowTabXXS + (code >> 9) * 256u + 128u + lb);
                 int& a = j < 2 ? alo : ahi;
-                a = __dp4a((int)prmt2(kPos2, kNeg2, sel), (int)qv[2 * j], a);
-                a = __dp4a((int)prmt2(kPos2, kNeg2, sel >> 16), (int)qv[2 * j + 1], a);
+                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel), (int)qv[2 * j], a);
+                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel >> 16), (int)qv[2 * j + 1], a);
             }
             M += s_lo * alo + s_hi * ahi;
         } else {
@@ -259,8 +267,8 @@ __device__ __forceinline__ void block_sum(const RowRaw& r, const int8_t* q, uint
                 const uint32_t idx = ((qsw >> (8 * j)) & 0xffu) | ((nib & 7u) << 8);
                 const uint32_t sel = tab32(kRowTabIQ1 + idx * 16u + (lb & 12u));
                 int& a = j < 2 ? alo : ahi;
-                a = __dp4a((int)prmt2(kVal1, 0u, sel), (int)qv[2 * j], a);
-                a = __dp4a((int)prmt2(kVal1, 0u, sel >> 16), (int)qv[2 * j + 1], a);
+                a = __dp4a((int)prmt_sel(kVal1, 0u, sel), (int)qv[2 * j], a);
+                a = __dp4a((int)prmt_sel(kVal1, 0u, sel >> 16), (int)qv[2 * j + 1], a);
                 // delta: +-1 per group times the group's 8 activations
                 const int qs8 = __dp4a((int)qv[2 * j], 0x01010101, __dp4a((int)qv[2 * j + 1], 0x01010101, 0));
                 int& dd = j < 2 ? dlo : dhi;

@@ -1,0 +1,456 @@
+// Persistent whole-stack decode kernel: one CTA per SM runs every layer of a token,
+// with two grid barriers per layer, so the tables are staged once per token and no
+// kernel launch or prologue sits between the phases.
+//
+// Per layer l (ids/w = the routing of layer l, fixed before the launch):
+//   1. every CTA: h += ascending-id fma combine of the previous layer's expert rows
+//      (runtime.cpp:184-187), x = RMSNorm(h), Q8_K(x) into shared memory (all CTAs
+//      compute the same bits: fixed-order fp64 sum of squares, as k_norm_quant);
+//   2. gate/up rows of every pick, spread over all warps of the grid -> gu (global);
+//   -- grid barrier --
+//   3. every CTA serves one pick in the down phase: SwiGLU + Q8_K(h) of that pick into
+//      shared memory, then its share of the pick's down rows -> yrows (global);
+//   -- grid barrier --
+// After the last layer the combine is applied once more and written to h_out.
+#include <cuda_runtime.h>
+
+#include "clb_device.cuh"
+#include "clb_kernels.h"
+#include "clb_v2.cuh"
+
+namespace clb {
+
+namespace {
+
+constexpr unsigned kBarrierSpinLimit = 1u << 26;  // well over a second of polling before giving up
+constexpr int kErrBarrier = 2;                     // err flag value of a timed-out barrier
+
+// Grid-wide barrier over gridDim.x co-resident CTAs (cooperative launch) on a counter
+// that only grows: barrier number e (1, 2, ...) is passed once the counter reaches
+// e * gridDim.x. Thread 0 of each CTA arrives with a release add (the CTA's writes,
+// ordered before it by the preceding __syncthreads, become visible first) and polls
+// with acquire loads. Bounded: after kBarrierSpinLimit polls the CTA sets *err and
+// every thread of it gets false, so the kernel can return instead of hanging.
+__device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err) {
+    __syncthreads();
+    int ok = 1;
+    if (threadIdx.x == 0) {
+        const unsigned target = epoch * gridDim.x;
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(count), "r"(1u) : "memory");
+        unsigned v = 0, spins = 0;
+        while (true) {
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(count) : "memory");
+            if ((int)(v - target) >= 0) break;
+            if (++spins > kBarrierSpinLimit) {
+                atomicExch(err, kErrBarrier);
+                ok = 0;
+                break;
+            }
+        }
+    }
+    return __syncthreads_and(ok) != 0;
+}
+
+// First CTA of pick p when gridDim.x CTAs are split over k picks (CTA c serves pick
+// c * k / gridDim.x).
+__device__ __forceinline__ int pick_cta_begin(int p, int k) { return (p * (int)gridDim.x + k - 1) / k; }
+
+}  // namespace
+
+struct StackParams {
+    const ExpertDesc* desc;  // [bank layers][E]
+    int E, first, nl, k;
+    const int* route_ids;    // [nl][k]
+    const float* route_w;    // [nl][k]
+    const float* h_in;       // dim
+    float* h_out;            // dim (may alias h_in)
+    int dim, ff;
+    float limit;
+    float* gu;               // [k][2][ff]
+    float* yrows;            // [k][dim]
+    unsigned* bar;           // grid barrier counter, zero before the launch
+    int* err;
+    const uint32_t* tables;  // compact selector tables (kTableWords)
+    int s_gu, s_dn;          // fast order: K segments of a row in the gate/up and down phases
+};
+
+// Shared memory carve-up (bytes), shared by the kernel and the host size query.
+// nt: threads per CTA.
+struct StackSmem {
+    size_t h, xq, xd, hq, hd, desc, ids, w, order, tree, xch, total;
+    // Every region starts on a 16-byte boundary (the activation blocks are read as uint4).
+    static __host__ __device__ size_t up16(size_t o) { return (o + 15) & ~(size_t)15; }
+    __host__ __device__ StackSmem(int dim, int ff, int k, bool exact, int nt) {
+        size_t o = kRowTableBytes;
+        h = o;     o = up16(o + (size_t)dim * 4);
+        xq = o;    o = up16(o + (size_t)(dim >> 8) * kActStride);
+        xd = o;    o = up16(o + (size_t)(dim >> 8) * 4);
+        hq = o;    o = up16(o + (size_t)k * (ff >> 8) * kActStride);  // fast order: every pick
+        hd = o;    o = up16(o + (size_t)k * (ff >> 8) * 4);
+        desc = o;  o = up16(o + (size_t)k * sizeof(ExpertDesc));
+        ids = o;   o = up16(o + (size_t)2 * kMaxPicks * 4);  // this and the previous layer
+        w = o;     o = up16(o + (size_t)2 * kMaxPicks * 4);
+        order = o; o = up16(o + (size_t)2 * kMaxPicks * 4);
+        tree = o;  o = up16(o + (size_t)nt * 8);  // also the K-segment partials [warp][lane]
+        // scratch: table staging (kTableWords), one pick's fp32 SwiGLU output (ff), and
+        // in the exact order the quad exchange records of every warp
+        xch = o;
+        size_t words = (size_t)kTableWords > (size_t)ff ? (size_t)kTableWords : (size_t)ff;
+        if (exact && (size_t)(nt / 32) * 32 * kXchWords > words) words = (size_t)(nt / 32) * 32 * kXchWords;
+        total = o + words * 4 + 16;
+    }
+};
+
+__device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+// Sum of (double)h[i]^2 over i = lane, lane + 1024, ... in order (one of 1024 lanes).
+__device__ __forceinline__ double lane_sumsq(const float* hs, int dim, int lane) {
+    double s = 0.0;
+    for (int i = lane; i < dim; i += 1024) {
+        const double v = (double)hs[i];
+        s = __dadd_rn(s, __dmul_rn(v, v));
+    }
+    return s;
+}
+
+template <bool FAST, int NT>
+__global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
+    constexpr int NW = NT / 32;
+    uint8_t* smem = clb_dyn_smem;
+    const StackSmem L(P.dim, P.ff, P.k, !FAST, NT);
+    float* hs = reinterpret_cast<float*>(smem + L.h);
+    int8_t* xq = reinterpret_cast<int8_t*>(smem + L.xq);
+    float* xd = reinterpret_cast<float*>(smem + L.xd);
+    int8_t* hq = reinterpret_cast<int8_t*>(smem + L.hq);
+    float* hd = reinterpret_cast<float*>(smem + L.hd);
+    ExpertDesc* dsc = reinterpret_cast<ExpertDesc*>(smem + L.desc);
+    int* sid = reinterpret_cast<int*>(smem + L.ids);      // [2][kMaxPicks], slot li & 1
+    float* sw = reinterpret_cast<float*>(smem + L.w);
+    int* sord = reinterpret_cast<int*>(smem + L.order);   // picks in ascending id order
+    double* tree = reinterpret_cast<double*>(smem + L.tree);
+    uint32_t* xch_all = reinterpret_cast<uint32_t*>(smem + L.xch);
+    float* hf = reinterpret_cast<float*>(smem + L.xch);   // SwiGLU output of this CTA's pick
+    float* part = reinterpret_cast<float*>(smem + L.tree);  // K-segment partials [warp][lane]
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int dim = P.dim, ff = P.ff, k = P.k;
+    const int nbx = dim >> 8, nbh = ff >> 8;
+    const int G = gridDim.x, W = G * NW, gw = blockIdx.x * NW + warp;
+    const int my_pick = blockIdx.x * k / G;
+    const int pc0 = pick_cta_begin(my_pick, k), pc1 = pick_cta_begin(my_pick + 1, k);
+    const int pick_warps = (pc1 - pc0) * NW, pick_warp = (blockIdx.x - pc0) * NW + warp;
+
+    fill_row_tables(P.tables, xch_all);
+    for (int i = tid; i < dim; i += NT) hs[i] = __ldcg(P.h_in + i);
+
+    for (int li = 0; li <= P.nl; ++li) {
+        const int cur = li & 1, prev = cur ^ 1;
+        // routing of this layer, and the ascending-id order of its picks
+        if (li < P.nl && tid < k) {
+            sid[cur * kMaxPicks + tid] = P.route_ids[(size_t)li * k + tid];
+            sw[cur * kMaxPicks + tid] = P.route_w[(size_t)li * k + tid];
+        }
+        __syncthreads();
+        if (li < P.nl && tid < k) {
+            const int me = sid[cur * kMaxPicks + tid];
+            int rank = 0;
+            for (int p = 0; p < k; ++p) rank += sid[cur * kMaxPicks + p] < me;
+            sord[cur * kMaxPicks + rank] = tid;
+        }
+        if (li < P.nl)
+            for (int i = tid; i < k * (int)(sizeof(ExpertDesc) / 4); i += NT) {
+                const int p = i / (int)(sizeof(ExpertDesc) / 4), wd = i % (int)(sizeof(ExpertDesc) / 4);
+                const uint32_t* src = reinterpret_cast<const uint32_t*>(
+                    P.desc + (size_t)(P.first + li) * P.E + sid[cur * kMaxPicks + p]);
+                reinterpret_cast<uint32_t*>(dsc + p)[wd] = src[wd];
+            }
+        __syncthreads();
+
+        // 1. h += combine of the previous layer (ascending expert id), in every CTA: four
+        //    rows per thread and two such quads at a time, the rows of up to 3 picks of both
+        //    loaded before the fma chains
+        if (li > 0) {
+            const float* yr = P.yrows;
+            const int nq = dim >> 2;
+            for (int q0 = tid; q0 < nq; q0 += 2 * NT) {
+                const int q1 = q0 + NT;
+                float4 a0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), a1 = a0;
+                for (int o0 = 0; o0 < k; o0 += 3) {
+                    float4 v0[3], v1[3];
+#pragma unroll
+                    for (int j = 0; j < 3; ++j)
+                        if (o0 + j < k) {
+                            const float* y = yr + (size_t)sord[prev * kMaxPicks + o0 + j] * dim;
+                            v0[j] = ldcg4(y + 4 * q0);
+                            if (q1 < nq) v1[j] = ldcg4(y + 4 * q1);
+                        }
+#pragma unroll
+                    for (int j = 0; j < 3; ++j)
+                        if (o0 + j < k) {
+                            const float wj = sw[prev * kMaxPicks + sord[prev * kMaxPicks + o0 + j]];
+                            a0.x = __fmaf_rn(wj, v0[j].x, a0.x);
+                            a0.y = __fmaf_rn(wj, v0[j].y, a0.y);
+                            a0.z = __fmaf_rn(wj, v0[j].z, a0.z);
+                            a0.w = __fmaf_rn(wj, v0[j].w, a0.w);
+                            if (q1 < nq) {
+                                a1.x = __fmaf_rn(wj, v1[j].x, a1.x);
+                                a1.y = __fmaf_rn(wj, v1[j].y, a1.y);
+                                a1.z = __fmaf_rn(wj, v1[j].z, a1.z);
+                                a1.w = __fmaf_rn(wj, v1[j].w, a1.w);
+                            }
+                        }
+                }
+                float4 hv = reinterpret_cast<float4*>(hs)[q0];
+                hv.x = __fadd_rn(hv.x, a0.x);
+                hv.y = __fadd_rn(hv.y, a0.y);
+                hv.z = __fadd_rn(hv.z, a0.z);
+                hv.w = __fadd_rn(hv.w, a0.w);
+                reinterpret_cast<float4*>(hs)[q0] = hv;
+                if (q1 < nq) {
+                    hv = reinterpret_cast<float4*>(hs)[q1];
+                    hv.x = __fadd_rn(hv.x, a1.x);
+                    hv.y = __fadd_rn(hv.y, a1.y);
+                    hv.z = __fadd_rn(hv.z, a1.z);
+                    hv.w = __fadd_rn(hv.w, a1.w);
+                    reinterpret_cast<float4*>(hs)[q1] = hv;
+                }
+            }
+            __syncthreads();
+        }
+        if (li == P.nl) break;
+
+        // x = RMSNorm(h), Q8_K(x): lane t of 1024 sums h[t + 1024 j]^2 in j order, then a
+        // binary tree over the lanes (k_norm_quant's order; with 512 threads, thread t
+        // holds lanes t and t + 512, the tree's first level)
+        {
+            double s = lane_sumsq(hs, dim, tid);
+            if (NT == 512) s = __dadd_rn(s, lane_sumsq(hs, dim, tid + 512));
+            tree[tid] = s;
+            __syncthreads();
+            for (int stride = NT / 2; stride >= 32; stride >>= 1) {
+                if (tid < stride) tree[tid] = __dadd_rn(tree[tid], tree[tid + stride]);
+                __syncthreads();
+            }
+            if (warp == 0) {  // strides 16 .. 1 of the same tree, lane t += lane t + stride
+                double v = tree[lane];
+#pragma unroll
+                for (int stride = 16; stride > 0; stride >>= 1) v = __dadd_rn(v, __shfl_down_sync(0xffffffffu, v, stride));
+                if (lane == 0) tree[0] = v;
+            }
+            __syncthreads();
+            const double mean = __ddiv_rn(tree[0], (double)dim);
+            const float sc = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(mean, 1e-6)));
+            for (int b = warp; b < nbx; b += NW) {
+                float v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(hs[b * 256 + lane * 8 + i], sc);
+                warp_quant_regs(v, xq + (size_t)b * kActStride, xd + b);
+            }
+        }
+        __syncthreads();
+
+        if (FAST) {
+            // 2. gate/up, one row per lane: a CTA round covers 8 / SG row groups of 32 rows of
+            //    both matrices, each split into SG K segments (one warp each); the segments
+            //    are added in order and SwiGLU(g, u) goes to hbuf [pick][ff]
+            const int SG = P.s_gu, RGR = 8 / SG, rgpp = ff >> 5, nrg = k * rgpp;
+            const int seg = warp % SG, mat = (warp / SG) & 1, rgl = warp / (2 * SG);
+            const int per = (nbx + SG - 1) / SG, b0 = min(nbx, seg * per), b1 = min(nbx, b0 + per);
+            for (int q = blockIdx.x; q * RGR < nrg; q += G) {
+                const int rg = q * RGR + rgl;
+                float y = 0.0f;
+                if (rg < nrg) {
+                    const int pick = rg / rgpp, row = (rg % rgpp) * 32 + lane;
+                    const PackedMat& m = mat ? dsc[pick].up : dsc[pick].gate;
+                    if (m.body != nullptr && m.k == dim && m.n == ff) y = lane_row_partial_any(m, row, b0, b1, xq, xd);
+                    else if (lane == 0) atomicExch(P.err, 1);
+                }
+                part[warp * 32 + lane] = y;
+                __syncthreads();
+                if (tid < RGR * 32) {
+                    const int r2 = tid >> 5, rg2 = q * RGR + r2;
+                    if (rg2 < nrg) {
+                        float g = 0.0f, u = 0.0f;
+                        for (int s2 = 0; s2 < SG; ++s2) {
+                            g = __fadd_rn(g, part[((r2 * 2 + 0) * SG + s2) * 32 + lane]);
+                            u = __fadd_rn(u, part[((r2 * 2 + 1) * SG + s2) * 32 + lane]);
+                        }
+                        P.gu[(size_t)(rg2 / rgpp) * ff + (rg2 % rgpp) * 32 + lane] = swiglu(g, u, P.limit);
+                    }
+                }
+                __syncthreads();
+            }
+            if (!grid_barrier(P.bar, 2 * li + 1, P.err)) return;
+
+            // 3. Q8_K(h) of every pick, then the down rows: a CTA round covers 16 / SD
+            //    (pick, 32-row group) pairs, each split into SD K segments (one warp each)
+            for (int hb0 = warp; hb0 < k * nbh; hb0 += 3 * NW) {  // up to 3 blocks per warp in flight
+                float v[3][8];
+#pragma unroll
+                for (int j = 0; j < 3; ++j)
+                    if (hb0 + j * NW < k * nbh) {
+                        const float4* src = reinterpret_cast<const float4*>(P.gu + (size_t)(hb0 + j * NW) * 256 + lane * 8);
+                        const float4 lo = __ldcg(src), hi = __ldcg(src + 1);
+                        v[j][0] = lo.x, v[j][1] = lo.y, v[j][2] = lo.z, v[j][3] = lo.w;
+                        v[j][4] = hi.x, v[j][5] = hi.y, v[j][6] = hi.z, v[j][7] = hi.w;
+                    }
+#pragma unroll
+                for (int j = 0; j < 3; ++j)
+                    if (hb0 + j * NW < k * nbh)
+                        warp_quant_regs(v[j], hq + (size_t)(hb0 + j * NW) * kActStride, hd + hb0 + j * NW);
+            }
+            __syncthreads();
+            const int SD = P.s_dn, PPR = 16 / SD, rgd = dim >> 5, npair = k * rgd;
+            const int slot = warp / SD, dseg = warp % SD;
+            const int dper = (nbh + SD - 1) / SD, d0 = min(nbh, dseg * dper), d1 = min(nbh, d0 + dper);
+            for (int q = blockIdx.x; q * PPR < npair; q += G) {
+                const int pr = q * PPR + slot;
+                float y = 0.0f;
+                if (slot < PPR && pr < npair) {
+                    const int pick = pr / rgd, row = (pr % rgd) * 32 + lane;
+                    const PackedMat& m = dsc[pick].down;
+                    if (m.body != nullptr && m.k == ff && m.n == dim)
+                        y = lane_row_partial_any(m, row, d0, d1, hq + (size_t)pick * nbh * kActStride, hd + pick * nbh);
+                    else if (lane == 0) atomicExch(P.err, 1);
+                }
+                part[warp * 32 + lane] = y;
+                __syncthreads();
+                if (tid < PPR * 32) {
+                    const int s2 = tid >> 5, pr2 = q * PPR + s2;
+                    if (pr2 < npair) {
+                        float t = 0.0f;
+                        for (int j = 0; j < SD; ++j) t = __fadd_rn(t, part[(s2 * SD + j) * 32 + lane]);
+                        P.yrows[(size_t)(pr2 / rgd) * dim + (pr2 % rgd) * 32 + lane] = t;
+                    }
+                }
+                __syncthreads();
+            }
+        } else {
+            // 2. gate/up rows (exact order: 4 threads per row, quad exchange) -> gu
+            const int rpw = 8, groups = ff / rpw, items = k * 2 * groups;
+            uint32_t* xch = xch_all + warp * 32 * kXchWords;
+            for (int it = gw; it < items; it += W) {
+                const int pick = it / (2 * groups), rem = it % (2 * groups);
+                const int group = rem >> 1, mat = rem & 1;
+                const PackedMat& m = mat ? dsc[pick].up : dsc[pick].gate;
+                const int row = group * rpw + lane / 4;
+                float y = 0.0f;
+                if (m.body != nullptr && m.k == dim && m.n == ff) y = quad_row_dot_any<false>(m, row, xq, xd, xch);
+                else if (lane == 0) atomicExch(P.err, 1);
+                if (lane % 4 == 0) P.gu[((size_t)pick * 2 + mat) * ff + row] = y;
+            }
+            if (!grid_barrier(P.bar, 2 * li + 1, P.err)) return;
+
+            // 3. SwiGLU of this CTA's pick over all threads, Q8_K(h) per 256-block, then the
+            //    pick's down rows (one thread per row, the reference's lane chains) -> yrows
+            const float* g = P.gu + ((size_t)my_pick * 2) * ff;
+            for (int i = tid; i < ff; i += NT) hf[i] = swiglu(__ldcg(g + i), __ldcg(g + ff + i), P.limit);
+            __syncthreads();
+            for (int hb = warp; hb < nbh; hb += NW) {
+                float v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = hf[hb * 256 + lane * 8 + i];
+                warp_quant_regs(v, hq + (size_t)hb * kActStride, hd + hb);
+            }
+            __syncthreads();
+            const PackedMat& m = dsc[my_pick].down;
+            const int groups_d = dim >> 5;
+            const bool ok = m.body != nullptr && m.k == ff && m.n == dim;
+            if (!ok && tid == 0) atomicExch(P.err, 1);
+            for (int g2 = pick_warp; g2 < groups_d; g2 += pick_warps) {
+                const int row = g2 * 32 + lane;
+                const float y = ok ? thread_row_dot_any<false>(m, row, hq, hd) : 0.0f;
+                P.yrows[(size_t)my_pick * dim + row] = y;
+            }
+        }
+        if (!grid_barrier(P.bar, 2 * li + 2, P.err)) return;
+    }
+    // h after the last layer: each CTA writes its slice
+    const int per = (dim + G - 1) / G;
+    for (int i = blockIdx.x * per + tid; i < min(dim, (blockIdx.x + 1) * per); i += NT) P.h_out[i] = hs[i];
+}
+
+// Threads per CTA of the persistent kernel (16 warps, up to 128 registers a thread).
+static int stack_threads(bool) { return 512; }
+
+size_t stack_smem(int dim, int ff, int k, bool fast) { return StackSmem(dim, ff, k, !fast, stack_threads(fast)).total; }
+
+// K segments of the fast-order phases, chosen to minimise the blocks one thread decodes
+// (CTA rounds x blocks per segment; the smaller count on ties).
+// gate/up: SG in {1, 2, 4, 8}, a round = 8 / SG row groups of 32 rows x 2 matrices.
+static int pick_gateup_segments(int k, int ff, int nb, int grid) {
+    int best = 1;
+    long best_cost = -1;
+    for (int SG : {1, 2, 4, 8}) {
+        const long rounds_total = ((long)k * (ff / 32) + (8 / SG) - 1) / (8 / SG);
+        const long cost = (rounds_total + grid - 1) / grid * ((nb + SG - 1) / SG);
+        if (best_cost < 0 || cost < best_cost) best_cost = cost, best = SG;
+    }
+    return best;
+}
+// down: SD in {1, 2, 3, 4}, a round = 16 / SD (pick, 32-row group) pairs.
+static int pick_down_segments(int k, int dim, int nb, int grid) {
+    int best = 1;
+    long best_cost = -1;
+    for (int SD : {1, 2, 3, 4}) {
+        const long rounds_total = ((long)k * (dim / 32) + (16 / SD) - 1) / (16 / SD);
+        const long cost = (rounds_total + grid - 1) / grid * ((nb + SD - 1) / SD);
+        if (best_cost < 0 || cost < best_cost) best_cost = cost, best = SD;
+    }
+    return best;
+}
+
+static int stack_grid() {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms > 0 ? sms : 148;
+}
+
+bool stack_supported(int dim, int ff, int k, bool fast) {
+    int dev = 0, optin = 0, coop = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+    if (!coop) return false;
+    const size_t need = stack_smem(dim, ff, k, fast);
+    return optin > 0 && need <= (size_t)optin && k <= stack_grid();
+}
+
+cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
+                         const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit, float* gu,
+                         float* yrows, unsigned* bar, int* err, bool fast, cudaStream_t s) {
+    const uint32_t* tables = nullptr;
+    cudaError_t e = tables_device_ptr(&tables);
+    if (e != cudaSuccess) return e;
+    const int G = stack_grid();
+    StackParams P{};
+    P.desc = desc;
+    P.E = E;
+    P.first = first;
+    P.nl = nl;
+    P.k = k;
+    P.route_ids = route_ids;
+    P.route_w = route_w;
+    P.h_in = h_in;
+    P.h_out = h_out;
+    P.dim = dim;
+    P.ff = ff;
+    P.limit = limit;
+    P.gu = gu;
+    P.yrows = yrows;
+    P.bar = bar;
+    P.err = err;
+    P.tables = tables;
+    const int nt = stack_threads(fast);
+    P.s_gu = pick_gateup_segments(k, ff, dim >> 8, G);
+    P.s_dn = pick_down_segments(k, dim, ff >> 8, G);
+    const size_t sm = stack_smem(dim, ff, k, fast);
+    void (*kern)(StackParams) = fast ? k_stack<true, 512> : k_stack<false, 512>;
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))) return e;
+    if ((e = cudaMemsetAsync(bar, 0, sizeof(unsigned), s))) return e;
+    void* args[] = {&P};
+    return cudaLaunchCooperativeKernel(reinterpret_cast<void*>(kern), dim3(G), dim3(nt), args, sm, s);
+}
+
+}  // namespace clb

@@ -115,6 +115,9 @@ typedef struct clb_bank_config_v1 {
  * CLB_BANK_EXACT_ORDER: the reference's own order (8 lane chains, per-block fma in block
  *   order, q8k_core.hpp:43-91), bit-identical to the CPU lane, at lower throughput. */
 #define CLB_BANK_EXACT_ORDER 1
+/* Stack decode (clb_stack_decode*) launches three kernels per layer instead of one
+ * persistent kernel holding one CTA on every SM (for processes that share the GPU). */
+#define CLB_BANK_PER_LAYER_KERNELS 2
 
 /* Creates a bank and its fixed workspace on `device` (no allocation afterwards).
  * Replaces the construction half of HipResidentBank::load
@@ -135,6 +138,9 @@ int32_t clb_bank_load_matrix(clb_bank* bank, uint32_t layer, int32_t expert, int
 
 /* Device bytes held by expert matrices (sum of packed sizes). */
 uint64_t clb_bank_weight_bytes(const clb_bank* bank);
+/* 1 when stack decode runs as the persistent kernel, 0 for the per-layer kernels
+ * (CLB_BANK_PER_LAYER_KERNELS, or a geometry / device the persistent kernel cannot hold). */
+int32_t clb_bank_stack_persistent(const clb_bank* bank);
 
 /* 1 if (layer, expert) is resident in this bank, else 0. Const, allocation free.
  * Replaces WarmRedirect::warm_contains (engine/strata/warm/runtime.hpp:14). */
@@ -195,13 +201,17 @@ int32_t clb_route_host(int32_t mode, const float* logits, const float* bias, int
  *   h_{l+1} = h_l + combine_l(route(logits_l), experts(x_l)).
  * The fp64 sum of squares has a fixed order (1024 strided lanes, then a binary
  * tree) so it is reproducible bit for bit on the CPU.
- * h: [dim] in, logits: [n_layers][n_experts], out: [dim]. Routing mode 0 on device.
- * The per-token graph is captured once and replayed. */
+ * h: [dim] in, logits: [n_layers][n_experts] (finite), out: [dim]. Routing mode 0 runs
+ * on the host (route.cpp's selection order and the host libm, as the CPU lane), only
+ * x and the routes cross to the device. One persistent kernel runs the layer range
+ * (CLB_BANK_PER_LAYER_KERNELS: a captured per-layer graph, replayed). */
 int32_t clb_stack_decode(clb_bank* bank, uint32_t first_layer, int32_t n_layers, const float* x,
                          const float* logits, float* out, clb_error_v1* err);
 
 /* Device-resident variant of clb_stack_decode on the bank's stream (no host copies,
- * no synchronisation): d_x [dim] is updated in place. */
+ * no synchronisation): d_x [dim] is updated in place. Routing runs on the device
+ * (clb_route_device): the same experts; each weight's sigmoid uses the correctly
+ * rounded exp, which glibc's expf matches on all but ~0.06% of arguments (1 ulp). */
 int32_t clb_stack_decode_device(clb_bank* bank, uint32_t first_layer, int32_t n_layers, float* d_x,
                                 const float* d_logits, clb_error_v1* err);
 

@@ -134,17 +134,30 @@ class Oracle:
         assert rc == 0
         return y
 
+    def stack_sensitivity(self, policy, seed, h0, logits, dim, ff, k=6, limit=0.0):
+        """rel_l2 between the stack of h0 and of h0 moved by +-1 ulp (alternating): how far
+        any non-bit-exact evaluation order can drift on this input (Q8_K re-quantisation
+        between layers turns ulp-level differences into whole quantisation steps)."""
+        a = self.stack(policy, seed, h0, logits, dim, ff, k, limit)
+        h0 = np.ascontiguousarray(h0, np.float32)
+        step = np.where(np.arange(h0.size) % 2 == 0, 1, -1).astype(np.int32)
+        b = self.stack(policy, seed, (h0.view(np.int32) + step).view(np.float32), logits, dim, ff, k, limit)
+        return rel_l2(b, a)
+
     def rmsnorm(self, h):
         h = np.ascontiguousarray(h, np.float32)
         out = np.zeros_like(h)
         self.L.orc_rmsnorm(ptr(h), h.size, ptr(out))
         return out
 
-    def stack(self, policy, seed, h0, logits, dim, ff, k=6, limit=0.0):
-        """h_{l+1} = h_l + layer_l(RMSNorm(h_l)) with mode-A routing (clb_stack_decode)."""
+    def stack(self, policy, seed, h0, logits, dim, ff, k=6, limit=0.0, first=0, routes=None):
+        """h_{l+1} = h_l + layer_l(RMSNorm(h_l)) with mode-A routing (clb_stack_decode),
+        for layers first .. first + len(logits) - 1; routes: optional [(ids, w)] per
+        layer used instead of routing the logits."""
         h = np.ascontiguousarray(h0, np.float32).copy()
-        for layer in range(logits.shape[0]):
-            ids, w = self.route_sigmoid(logits[layer], k)
+        for i in range(logits.shape[0]):
+            layer = first + i
+            ids, w = routes[i] if routes is not None else self.route_sigmoid(logits[i], k)
             y = self.layer_synth(policy, seed, layer, ids, w, self.rmsnorm(h), dim, ff, limit)
             h = (h + y).astype(np.float32)
         return h
