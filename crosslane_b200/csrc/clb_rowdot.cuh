@@ -170,7 +170,7 @@ __device__ __forceinline__ void block_lanes(const RowRaw& r, const int8_t* q, ui
                 const uint32_t sel_j = 0x5504u | ((uint32_t)j << 4);
                 const uint32_t ga = prmt2(gw, lb, sel_j);  // grid byte * 256 + lane*4
                 const uint32_t sa = prmt2(sw, lb, sel_j);  // sign byte * 256 + lane*4
-                const uint32_t sel = tab32(kRowTabXXS + ga) + tab32(kRowTabXXS + 128 + sa);
+                const uint32_t sel = (tab32(kRowTabXXS + ga) | tab32(kRowTabXXS + 128 + sa));
                 const uint32_t lo = prmt_sel(kPos2, kNeg2, sel), hi = prmt_sel(kPos2, kNeg2, sel >> 16);
                 I[2 * j] += scale * dp4a_s(lo, qv[2 * j]);
                 I[2 * j + 1] += scale * dp4a_s(hi, qv[2 * j + 1]);
@@ -184,7 +184,7 @@ __device__ __forceinline__ void block_lanes(const RowRaw& r, const int8_t* q, ui
                 const uint32_t code = (j & 1) ? (w >> 16) : (w & 0xffffu);
                 const uint32_t ga = (code & 511u) * 64u + (lb & 60u);
                 const uint32_t sa = (code >> 9) * 256u + 128u + lb;
-                const uint32_t sel = tab32(kRowTabXS + ga) + tab32(kRowTabXXS + sa);
+                const uint32_t sel = tab32(kRowTabXS + ga) | tab32(kRowTabXXS + sa);
                 const uint32_t lo = prmt_sel(kPos2, kNeg2, sel), hi = prmt_sel(kPos2, kNeg2, sel >> 16);
                 const int s = j < 2 ? s_lo : s_hi;
                 I[2 * j] += s * dp4a_s(lo, qv[2 * j]);
@@ -227,31 +227,39 @@ __device__ __forceinline__ void block_sum(const RowRaw& r, const int8_t* q, uint
         const uint4 qb = *reinterpret_cast<const uint4*>(q + 32 * c + 16);
         const uint32_t qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
         if (T == CLB_IQ2_XXS) {
+            // all four table lookups of the chunk first, then the decode (more loads in flight)
             const uint32_t gw = rw(r, 2 * c), sw = rw(r, 2 * c + 1);
             const int scale = (int)((((sw & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27);
-            int a0 = 0, a1 = 0;
+            uint32_t sel[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const uint32_t sel_j = 0x5504u | ((uint32_t)j << 4);
-                const uint32_t ga = prmt2(gw, lb, sel_j), sa = prmt2(sw, lb, sel_j);
-                const uint32_t sel = tab32(kRowTabXXS + ga) + tab32(kRowTabXXS + 128 + sa);
-                a0 = __dp4a((int)prmt_sel(kPos2, kNeg2, sel), (int)qv[2 * j], a0);
-                a1 = __dp4a((int)prmt_sel(kPos2, kNeg2, sel >> 16), (int)qv[2 * j + 1], a1);
+                sel[j] = tab32(kRowTabXXS + prmt2(gw, lb, sel_j)) | tab32(kRowTabXXS + 128 + prmt2(sw, lb, sel_j));
             }
-            M += scale * (a0 + a1);
+            int a = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel[j]), (int)qv[2 * j], a);
+                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel[j] >> 16), (int)qv[2 * j + 1], a);
+            }
+            M += scale * a;
         } else if (T == CLB_IQ2_XS) {
             const uint32_t scb = ((c < 4 ? r.sc.x : r.sc.y) >> (8 * (c & 3))) & 0xffu;
             const int s_lo = (int)((scb & 15u) << 1) | 1, s_hi = (int)((scb >> 4) << 1) | 1;
-            int alo = 0, ahi = 0;
+            uint32_t sel[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const uint32_t w = rw(r, 2 * c + (j >> 1));
                 const uint32_t code = (j & 1) ? (w >> 16) : (w & 0xffffu);
-                const uint32_t sel = tab32(kRowTabXS + (code & 511u) * 64u + (lb & 60u)) +
-                                     tab32(kRowTabXXS + (code >> 9) * 256u + 128u + lb);
+                sel[j] = tab32(kRowTabXS + (code & 511u) * 64u + (lb & 60u)) |
+                         tab32(kRowTabXXS + (code >> 9) * 256u + 128u + lb);
+            }
+            int alo = 0, ahi = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
                 int& a = j < 2 ? alo : ahi;
-                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel), (int)qv[2 * j], a);
-                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel >> 16), (int)qv[2 * j + 1], a);
+                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel[j]), (int)qv[2 * j], a);
+                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel[j] >> 16), (int)qv[2 * j + 1], a);
             }
             M += s_lo * alo + s_hi * ahi;
         } else {

@@ -219,10 +219,30 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
         }
         if (li == P.nl) break;
 
-        // x = RMSNorm(h), Q8_K(x): lane t of 1024 sums h[t + 1024 j]^2 in j order, then a
-        // binary tree over the lanes (k_norm_quant's order; with 512 threads, thread t
-        // holds lanes t and t + 512, the tree's first level)
-        {
+        // x = RMSNorm(h), Q8_K(x). Exact order: lane t of 1024 sums h[t + 1024 j]^2 in j
+        // order in fp64, then a binary tree over the lanes (k_norm_quant's order; with 512
+        // threads, thread t holds lanes t and t + 512, the tree's first level). Fast order:
+        // fp32 fma chains per thread, butterfly sums in each warp, then over the warps; every
+        // CTA evaluates the same expression, so all get the same scale.
+        if (FAST) {
+            float s = 0.0f;
+            for (int i = tid; i < dim; i += NT) s = __fmaf_rn(hs[i], hs[i], s);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+            float* red = reinterpret_cast<float*>(tree);
+            if (lane == 0) red[warp] = s;
+            __syncthreads();
+            float t = lane < NW ? red[lane] : 0.0f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
+            const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)dim), 1e-6f)));
+            for (int b = warp; b < nbx; b += NW) {
+                float v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(hs[b * 256 + lane * 8 + i], sc);
+                warp_quant_regs(v, xq + (size_t)b * kActStride, xd + b);
+            }
+        } else {
             double s = lane_sumsq(hs, dim, tid);
             if (NT == 512) s = __dadd_rn(s, lane_sumsq(hs, dim, tid + 512));
             tree[tid] = s;
@@ -284,42 +304,58 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
 
             // 3. Q8_K(h) of every pick, then the down rows: a CTA round covers 16 / SD
             //    (pick, 32-row group) pairs, each split into SD K segments (one warp each)
-            for (int hb0 = warp; hb0 < k * nbh; hb0 += 3 * NW) {  // up to 3 blocks per warp in flight
+            const int SD = P.s_dn, PPR = 16 / SD, rgd = dim >> 5, npair = k * rgd;
+            uint32_t need = 0;  // picks whose rows this CTA's down rounds touch
+            for (int q = blockIdx.x; q * PPR < npair; q += G)
+                for (int j = 0; j < PPR && q * PPR + j < npair; ++j) need |= 1u << ((q * PPR + j) / rgd);
+            const int nneed = __popc(need);
+            for (int w0 = warp; w0 < nneed * nbh; w0 += 3 * NW) {  // up to 3 blocks per warp in flight
                 float v[3][8];
+                int hbs[3];
 #pragma unroll
-                for (int j = 0; j < 3; ++j)
-                    if (hb0 + j * NW < k * nbh) {
-                        const float4* src = reinterpret_cast<const float4*>(P.gu + (size_t)(hb0 + j * NW) * 256 + lane * 8);
+                for (int j = 0; j < 3; ++j) {
+                    hbs[j] = -1;
+                    const int wi = w0 + j * NW;
+                    if (wi < nneed * nbh) {
+                        const int nth = wi / nbh;  // nth set bit of `need`
+                        uint32_t m = need;
+                        for (int c = 0; c < nth; ++c) m &= m - 1;
+                        hbs[j] = (__ffs(m) - 1) * nbh + wi % nbh;
+                        const float4* src = reinterpret_cast<const float4*>(P.gu + (size_t)hbs[j] * 256 + lane * 8);
                         const float4 lo = __ldcg(src), hi = __ldcg(src + 1);
                         v[j][0] = lo.x, v[j][1] = lo.y, v[j][2] = lo.z, v[j][3] = lo.w;
                         v[j][4] = hi.x, v[j][5] = hi.y, v[j][6] = hi.z, v[j][7] = hi.w;
                     }
+                }
 #pragma unroll
                 for (int j = 0; j < 3; ++j)
-                    if (hb0 + j * NW < k * nbh)
-                        warp_quant_regs(v[j], hq + (size_t)(hb0 + j * NW) * kActStride, hd + hb0 + j * NW);
+                    if (hbs[j] >= 0) warp_quant_regs(v[j], hq + (size_t)hbs[j] * kActStride, hd + hbs[j]);
             }
             __syncthreads();
-            const int SD = P.s_dn, PPR = 16 / SD, rgd = dim >> 5, npair = k * rgd;
             const int slot = warp / SD, dseg = warp % SD;
             const int dper = (nbh + SD - 1) / SD, d0 = min(nbh, dseg * dper), d1 = min(nbh, d0 + dper);
-            for (int q = blockIdx.x; q * PPR < npair; q += G) {
-                const int pr = q * PPR + slot;
-                float y = 0.0f;
-                if (slot < PPR && pr < npair) {
-                    const int pick = pr / rgd, row = (pr % rgd) * 32 + lane;
-                    const PackedMat& m = dsc[pick].down;
-                    if (m.body != nullptr && m.k == ff && m.n == dim)
-                        y = lane_row_partial_any(m, row, d0, d1, hq + (size_t)pick * nbh * kActStride, hd + pick * nbh);
-                    else if (lane == 0) atomicExch(P.err, 1);
+            // two CTA rounds per pass: a warp decodes both of its units back to back and the
+            // segments are added once per pass
+            for (int q0 = blockIdx.x; q0 * PPR < npair; q0 += 2 * G) {
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) {
+                    const int q = q0 + rr * G, pr = q * PPR + slot;
+                    float y = 0.0f;
+                    if (slot < PPR && pr < npair) {
+                        const int pick = pr / rgd, row = (pr % rgd) * 32 + lane;
+                        const PackedMat& m = dsc[pick].down;
+                        if (m.body != nullptr && m.k == ff && m.n == dim)
+                            y = lane_row_partial_any(m, row, d0, d1, hq + (size_t)pick * nbh * kActStride, hd + pick * nbh);
+                        else if (lane == 0) atomicExch(P.err, 1);
+                    }
+                    part[(rr * NW + warp) * 32 + lane] = y;
                 }
-                part[warp * 32 + lane] = y;
                 __syncthreads();
-                if (tid < PPR * 32) {
-                    const int s2 = tid >> 5, pr2 = q * PPR + s2;
+                if (tid < 2 * PPR * 32) {
+                    const int rr = tid / (PPR * 32), s2 = (tid >> 5) % PPR, pr2 = (q0 + rr * G) * PPR + s2;
                     if (pr2 < npair) {
                         float t = 0.0f;
-                        for (int j = 0; j < SD; ++j) t = __fadd_rn(t, part[(s2 * SD + j) * 32 + lane]);
+                        for (int j = 0; j < SD; ++j) t = __fadd_rn(t, part[(rr * NW + s2 * SD + j) * 32 + lane]);
                         P.yrows[(size_t)(pr2 / rgd) * dim + (pr2 % rgd) * 32 + lane] = t;
                     }
                 }
