@@ -181,6 +181,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--policy", type=int, default=POLICY, help="quant type policy of the bank (2 = config 3 mix)")
     ap.add_argument("--quick", action="store_true", help="skip the e2e pass and the CPU baseline (tuning sweeps)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with N>1: independent full-bank replicas per GPU instead of expert-ID sharding")
     ap.add_argument("--exact-order", action="store_true",
                     help="reference summation order (CLB_BANK_EXACT_ORDER): bit-identical to the CPU lane")
     args = ap.parse_args()
@@ -204,14 +206,22 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
 
     L = args.layers
-    bank = cb.ExpertBank(n_layers=L, n_experts=EXPERTS, dim=DIM, ff=FF, max_picks=PICKS, device=local,
-                         exact_order=args.exact_order)
+    sharded = world > 1 and not args.replicas
+    if sharded:  # expert-ID sharding: rank r holds experts [r*E/N, (r+1)*E/N), rows exchanged over NVLink
+        from crosslane_b200.sharded import ShardedBank
+        bank = ShardedBank(n_layers=L, n_experts=EXPERTS, dim=DIM, ff=FF, max_picks=PICKS, device=local, rank=rank,
+                           world=world, exact_order=args.exact_order)
+    else:
+        bank = cb.ExpertBank(n_layers=L, n_experts=EXPERTS, dim=DIM, ff=FF, max_picks=PICKS, device=local,
+                             exact_order=args.exact_order)
     t0 = time.time()
     bank.fill_synthetic(SEED, args.policy)
     fill_s = time.time() - t0
+    if world > 1:
+        dist.barrier()  # every bank filled before the first (exchanging) launch
     stream = torch.cuda.ExternalStream(bank.stream)
 
-    rng = np.random.default_rng(1000 + rank)
+    rng = np.random.default_rng(1000 if sharded else 1000 + rank)  # sharded: every rank decodes the same tokens
     n_in = args.warmup + args.steps
     xs, logits = make_inputs(rng, n_in)
     logits = logits[:, :L]
@@ -249,7 +259,8 @@ def main():
         ms = float(t.item())
         dist.barrier()
     ms_per_step = ms / args.steps
-    value = world * args.steps / (ms / 1e3)
+    units = 1 if sharded else world  # tokens per step of the whole job
+    value = units * args.steps / (ms / 1e3)
 
     # ---- e2e through the host-buffer C ABI call (copies inside the timed region) ----
     hx = np.ascontiguousarray(xs)
@@ -268,20 +279,26 @@ def main():
         t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = {"value": world * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * DIM + 8 * L * PICKS,
+    e2e = {"value": units * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * DIM + 8 * L * PICKS,
            "d2h_bytes_per_step": 4 * DIM}
 
     # ---- roofline: algorithmic bytes of one token through the stack kernel ----
     peak, peak_kind = peaks()
     step_bytes = []
+    own_b, own_e = bank.expert_begin, bank.expert_end
     for i in range(args.steps):
         tok = args.warmup + i
-        nbytes = 8 * DIM  # residual stream in and out
+        nbytes = 0 if (sharded and rank != 0) else 8 * DIM  # residual stream in and out, once per token
         for layer in range(L):
             ids, _ = cb.route_host(0, logits[tok, layer], PICKS)
-            nbytes += sum(bank.expert_info(layer, int(e))[1] for e in ids)
+            nbytes += sum(bank.expert_info(layer, int(e))[1] for e in ids if own_b <= int(e) < own_e)
         step_bytes.append(nbytes)
-    bytes_per_step = float(np.mean(step_bytes))
+    bytes_per_step = float(np.mean(step_bytes))  # this rank's share
+    if world > 1:
+        t = torch.tensor([bytes_per_step], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)  # whole job: every rank's share (replicas: every rank's own token)
+        bytes_per_step = float(t.item())
+    peak_job = peak * world  # each GPU streams its own HBM
     step_gbs = bytes_per_step / (ms_per_step / 1e3) / 1e9
     traffic = None
     tp = os.path.join(ROOT, "profiles", "k_stack_traffic.json")
@@ -290,8 +307,8 @@ def main():
             t = json.load(f)
         # measured DRAM bytes per token-layer on a small capture, scaled to this stack
         traffic = round(t["dram_bytes_per_token_layer"] * L) if "dram_bytes_per_token_layer" in t else None
-    roofline = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(step_gbs / peak, 4), "traffic": traffic, "kernel": "clb::k_stack",
+    roofline = {"bound": "hbm", "achieved": round(step_gbs, 1), "peak": peak_job, "unit": "GB/s",
+                "frac": round(step_gbs / peak_job, 4), "traffic": traffic, "kernel": "clb::k_stack",
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6650 GB/s",
                 "algorithmic_bytes_per_launch": int(bytes_per_step),
@@ -305,12 +322,14 @@ def main():
     clk = clocks.summary()
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "strong" if sharded else "weak",
         "vs_baseline": None, "dtype": "int8xIQ/fp32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "layers": L, "experts": EXPERTS, "dim": DIM, "ff": FF, "picks": PICKS,
                    "types": "IQ2_XXS/IQ2_XS/IQ1_M per (layer, expert), seed-drawn", "batch": 1,
                    "routing": "top-6 by sigmoid of N(0,1) logits, renormalised",
-                   "parallelism": f"replica x{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"expert-ID sharded x{world} (peer-store row exchange in the stack kernel)"
+                                   if sharded else f"replica x{world}" if world > 1 else "single GPU"),
                    "summation": "exact reference order" if args.exact_order
                    else "segmented rows, fixed-tree partials (run-to-run identical)",
                    "l2": "inputs larger than L2: each token streams ~2 GB of distinct expert weights",

@@ -67,6 +67,8 @@ SIGNATURES = {
     "clb_bank_load_matrix": (_I, [_P, _U32, _I, _I, _I, _P, _SZ, _PE]),
     "clb_bank_weight_bytes": (C.c_uint64, [_P]),
     "clb_bank_stack_persistent": (_I, [_P]),
+    "clb_bank_exchange_handle": (_I, [_P, _P, _PE]),
+    "clb_bank_connect": (_I, [_P, _I, _I, _P, _PE]),
     "clb_bank_contains": (_I, [_P, _U32, _I]),
     "clb_bank_compute": (_I, [_P, _U32, _I, _P, _P, _PE]),
     "clb_bank_compute_many": (_I, [_P, _U32, _P, _I, _P, _P, _PE]),

@@ -17,6 +17,7 @@ IQ2_XXS, IQ2_XS, IQ1_M = 16, 17, 29
 BLOCK_BYTES = {IQ2_XXS: 66, IQ2_XS: 74, IQ1_M: 56}
 EXACT_ORDER = 1  # CLB_BANK_EXACT_ORDER
 PER_LAYER_KERNELS = 2  # CLB_BANK_PER_LAYER_KERNELS
+EXCHANGE_HANDLE_BYTES = 64  # CLB_EXCHANGE_HANDLE_BYTES
 ROLE_GATE, ROLE_UP, ROLE_DOWN = 0, 1, 2
 Q8K_BLOCK_BYTES = 292
 
@@ -169,6 +170,22 @@ class ExpertBank:
         check(lib.clb_stack_decode(self._h, first_layer, n_layers, _ptr(x), _ptr(logits), _ptr(out), C.byref(err)),
               err)
         return out
+
+    # -- expert-ID sharding over GPUs (clb_bank_exchange_handle / clb_bank_connect) --
+    def exchange_handle(self) -> bytes:
+        """CUDA IPC handle (64 bytes) of this bank's exchange region, for the peer processes."""
+        buf = (C.c_ubyte * EXCHANGE_HANDLE_BYTES)()
+        err = ErrorV1()
+        check(lib.clb_bank_exchange_handle(self._h, buf, C.byref(err)), err)
+        return bytes(buf)
+
+    def connect(self, rank: int, world: int, handles) -> None:
+        """Open the peers' exchange regions; handles[r] is rank r's exchange_handle()."""
+        blob = b"".join(bytes(h) for h in handles)
+        assert len(blob) == world * EXCHANGE_HANDLE_BYTES
+        buf = (C.c_ubyte * len(blob)).from_buffer_copy(blob)
+        err = ErrorV1()
+        check(lib.clb_bank_connect(self._h, rank, world, buf, C.byref(err)), err)
 
     def stack_decode_device(self, first_layer: int, n_layers: int, d_x, d_logits) -> None:
         """d_x: torch float32 [dim] on this device, updated in place on the bank stream."""

@@ -158,6 +158,12 @@ struct clb_bank {
     int* d_cnt_y = nullptr;         // last-arriver counters per output row group (16 or 32 rows)
     unsigned* d_bar = nullptr;      // grid barrier state of the persistent stack kernel
     bool persistent = false;        // stack decode runs as one persistent kernel
+    // expert-ID sharding over GPUs: exchange region [2][k][dim] floats + kMaxPeers flags,
+    // exported through a CUDA IPC handle; peers' regions opened by clb_bank_connect
+    uint8_t* d_xchg = nullptr;
+    size_t xchg_bytes = 0;
+    clb::StackShard shard;
+    std::vector<void*> opened_peers;
     float* d_logits = nullptr;
     int* d_route_ids = nullptr;
     float* d_route_w = nullptr;
@@ -268,8 +274,9 @@ struct clb_bank {
             cuda_check(clb::launch_route_sigmoid(dlogits, cfg.n_experts, k, nl, d_route_ids, d_route_w, s), "route");
         if (persistent) {
             cuda_check(clb::launch_stack(d_desc, cfg.n_experts, (int)first, nl, k, d_route_ids, d_route_w, dx, dx,
-                                         cfg.dim, cfg.ff, cfg.limit, d_gu, d_yrows, d_bar, d_err, fast(), s),
+                                         cfg.dim, cfg.ff, cfg.limit, d_gu, d_yrows, d_bar, d_err, fast(), shard, s),
                        "persistent stack kernel");
+            if (shard.world > 1) shard.epoch += (unsigned)nl;  // every GPU runs the same launches
             return;
         }
         for (int i = 0; i < nl; ++i)
@@ -304,6 +311,7 @@ struct clb_bank {
     }
 
     ~clb_bank() {
+        for (void* p : opened_peers) cudaIpcCloseMemHandle(p);
         for (auto& g : graphs) cudaGraphExecDestroy(g.second);
         for (auto& g : device_graphs) cudaGraphExecDestroy(g.second);
         for (void* p : allocations) cudaFree(p);
@@ -447,6 +455,13 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         cuda_check(cudaMemsetAsync(bank->d_cnt_h, 0, sizeof(int) * k * ff / 256, bank->stream), "memset");
         cuda_check(cudaMemsetAsync(bank->d_cnt_y, 0, sizeof(int) * ((dim + 15) / 16), bank->stream), "memset");
         bank->d_bar = bank->dev_alloc<unsigned>(2);
+        bank->xchg_bytes = 2 * k * dim * sizeof(float) + clb::kMaxPeers * sizeof(unsigned);
+        bank->d_xchg = bank->dev_alloc<uint8_t>(bank->xchg_bytes);
+        cuda_check(cudaMemsetAsync(bank->d_xchg, 0, bank->xchg_bytes, bank->stream), "memset");
+        bank->shard.own_begin = cfg.expert_begin;
+        bank->shard.own_end = cfg.expert_end;
+        bank->shard.yx = reinterpret_cast<float*>(bank->d_xchg);
+        bank->shard.flags = reinterpret_cast<unsigned*>(bank->d_xchg + 2 * k * dim * sizeof(float));
         bank->persistent = (cfg.flags & CLB_BANK_PER_LAYER_KERNELS) == 0 &&
                            clb::stack_supported(cfg.dim, cfg.ff, cfg.max_picks, bank->fast());
         bank->d_ids = bank->dev_alloc<int>(k);
@@ -490,6 +505,55 @@ int32_t clb_bank_contains(const clb_bank* bank, uint32_t layer, int32_t expert) 
 }
 
 int32_t clb_bank_stack_persistent(const clb_bank* bank) { return bank && bank->persistent ? 1 : 0; }
+
+int32_t clb_bank_exchange_handle(clb_bank* bank, void* handle_out, clb_error_v1* err) {
+    if (!bank || !handle_out) return fail(err, CLB_E_INVALID, "null bank/handle");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        DeviceGuard g(bank->cfg.device);
+        cudaIpcMemHandle_t h;
+        cuda_check(cudaIpcGetMemHandle(&h, bank->d_xchg), "cudaIpcGetMemHandle");
+        static_assert(sizeof(h) == CLB_EXCHANGE_HANDLE_BYTES, "IPC handle size");
+        std::memcpy(handle_out, &h, sizeof(h));
+    });
+}
+
+int32_t clb_bank_connect(clb_bank* bank, int32_t rank, int32_t world, const void* handles, clb_error_v1* err) {
+    if (!bank || !handles) return fail(err, CLB_E_INVALID, "null bank/handles");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        bank->check_usable();
+        require(world >= 2 && world <= clb::kMaxPeers && rank >= 0 && rank < world, CLB_E_INVALID,
+                "rank %d / world %d outside [0, %d)", rank, world, clb::kMaxPeers);
+        require(bank->shard.world == 1, CLB_E_STATE, "bank already connected");
+        require(bank->persistent, CLB_E_UNSUPPORTED,
+                "expert-ID sharding runs in the persistent stack kernel (not available for this geometry/flags)");
+        DeviceGuard g(bank->cfg.device);
+        clb::StackShard sh = bank->shard;
+        std::vector<void*> opened;
+        try {
+            for (int r = 0; r < world; ++r) {
+                if (r == rank) continue;
+                cudaIpcMemHandle_t h;
+                std::memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)r * CLB_EXCHANGE_HANDLE_BYTES, sizeof(h));
+                void* p = nullptr;
+                cuda_check(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+                opened.push_back(p);
+                const size_t k = (size_t)bank->cfg.max_picks, dim = (size_t)bank->cfg.dim;
+                sh.peer_yx[r] = static_cast<float*>(p);
+                sh.peer_flags[r] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(p) + 2 * k * dim * sizeof(float));
+            }
+        } catch (...) {
+            for (void* p : opened) cudaIpcCloseMemHandle(p);
+            throw;
+        }
+        sh.world = world;
+        sh.rank = rank;
+        sh.epoch = 0;
+        bank->shard = sh;
+        bank->opened_peers = opened;
+    });
+}
 
 int32_t clb_bank_fill_synthetic(clb_bank* bank, uint64_t seed, int32_t policy, clb_error_v1* err) {
     if (!bank) return fail(err, CLB_E_INVALID, "null bank");
@@ -771,10 +835,10 @@ int32_t clb_stack_decode(clb_bank* bank, uint32_t first, int32_t nl, const float
         const auto& c = bank->cfg;
         require(x && logits && out, CLB_E_INVALID, "null buffer");
         require(nl >= 1 && first + (uint32_t)nl <= (uint32_t)c.n_layers, CLB_E_INVALID, "layer range out of bounds");
-        require(c.expert_begin == 0 && c.expert_end == c.n_experts, CLB_E_INVALID,
-                "stack decode needs every expert resident (use the sharded driver for partial banks)");
+        require(bank->shard.world > 1 || (c.expert_begin == 0 && c.expert_end == c.n_experts), CLB_E_INVALID,
+                "stack decode of a partial bank needs clb_bank_connect (expert-ID sharding over GPUs)");
         for (int l = 0; l < nl; ++l)
-            for (int e = 0; e < c.n_experts; ++e)
+            for (int e = c.expert_begin; e < c.expert_end; ++e)
                 require(bank->resident[(size_t)(first + l) * bank->E() + (size_t)e], CLB_E_INVALID,
                         "expert (%u, %d) not resident", first + l, e);
         DeviceGuard g(c.device);
@@ -842,6 +906,8 @@ int32_t clb_stack_decode_device(clb_bank* bank, uint32_t first, int32_t nl, floa
         const auto& c = bank->cfg;
         require(d_x && d_logits && nl >= 1 && first + (uint32_t)nl <= (uint32_t)c.n_layers, CLB_E_INVALID,
                 "invalid stack arguments");
+        require(bank->shard.world > 1 || (c.expert_begin == 0 && c.expert_end == c.n_experts), CLB_E_INVALID,
+                "stack decode of a partial bank needs clb_bank_connect (expert-ID sharding over GPUs)");
         DeviceGuard g(c.device);
         bank->device_step([&] {
             if (bank->persistent) {

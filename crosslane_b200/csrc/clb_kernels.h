@@ -58,10 +58,23 @@ cudaError_t launch_down2(const ExpertDesc* experts, const int* ids, const float*
 cudaError_t launch_mv2(const PackedMat& m, const void* q, float* y, cudaStream_t s);
 
 // persistent whole-stack kernel (clb_stack.cu)
+constexpr int kMaxPeers = 8;  // GPUs of one node
+// Expert-ID sharding of the stack over `world` GPUs: this GPU holds experts [own_begin,
+// own_end) of every layer and computes only those picks; the expert rows of every layer
+// go to all GPUs through peer stores into double-buffered slots (yx: [2][k][dim] floats,
+// then `flags`: one counter per source GPU). world == 1: no sharding.
+struct StackShard {
+    int world = 1, rank = 0, own_begin = 0, own_end = 0x7fffffff;
+    unsigned epoch = 0;               // layers this bank has run sharded before this launch
+    float* yx = nullptr;
+    unsigned* flags = nullptr;
+    float* peer_yx[kMaxPeers] = {};
+    unsigned* peer_flags[kMaxPeers] = {};
+};
 size_t stack_smem(int dim, int ff, int k, bool fast);
 bool stack_supported(int dim, int ff, int k, bool fast);
 cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
                          const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit, float* gu,
-                         float* yrows, unsigned* bar, int* err, bool fast, cudaStream_t s);
+                         float* yrows, unsigned* bar, int* err, bool fast, const StackShard& shard, cudaStream_t s);
 
 }  // namespace clb

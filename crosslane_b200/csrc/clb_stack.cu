@@ -22,7 +22,7 @@ namespace clb {
 
 namespace {
 
-constexpr unsigned kBarrierSpinLimit = 1u << 26;  // well over a second of polling before giving up
+constexpr unsigned kBarrierSpinLimit = 1u << 22;  // a few seconds of polling before giving up
 constexpr int kErrBarrier = 2;                     // err flag value of a timed-out barrier
 
 // Grid-wide barrier over gridDim.x co-resident CTAs (cooperative launch) on a counter
@@ -51,6 +51,37 @@ __device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err) {
     return __syncthreads_and(ok) != 0;
 }
 
+// After a layer's down phase (all local CTAs past the grid barrier, their peer stores
+// fenced at system scope): CTA 0 tells every peer that this GPU's rows of layer li are in
+// place (a release add on the peer's flag for this rank), then every CTA waits until each
+// peer has said the same for its rows here. Flags only grow: layer li of the launch with
+// layer count `epoch` before it is complete at epoch + li + 1. Bounded like grid_barrier.
+__device__ bool exchange_rows(const StackShard& sh, int li, int* err) {
+    int ok = 1;
+    if (threadIdx.x == 0) {
+        if (blockIdx.x == 0)
+            for (int r = 0; r < sh.world; ++r)
+                if (r != sh.rank)
+                    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(sh.peer_flags[r] + sh.rank), "r"(1u)
+                                 : "memory");
+        const unsigned target = sh.epoch + (unsigned)li + 1u;
+        for (int r = 0; r < sh.world && ok; ++r) {
+            if (r == sh.rank) continue;
+            unsigned v = 0, spins = 0;
+            while (true) {
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(sh.flags + r) : "memory");
+                if ((int)(v - target) >= 0) break;
+                if (++spins > kBarrierSpinLimit) {
+                    atomicExch(err, kErrBarrier);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+    }
+    return __syncthreads_and(ok) != 0;
+}
+
 // First CTA of pick p when gridDim.x CTAs are split over k picks (CTA c serves pick
 // c * k / gridDim.x).
 __device__ __forceinline__ int pick_cta_begin(int p, int k) { return (p * (int)gridDim.x + k - 1) / k; }
@@ -72,12 +103,13 @@ struct StackParams {
     int* err;
     const uint32_t* tables;  // compact selector tables (kTableWords)
     int s_gu, s_dn;          // fast order: K segments of a row in the gate/up and down phases
+    StackShard sh;           // expert-ID sharding over GPUs (world == 1: none)
 };
 
 // Shared memory carve-up (bytes), shared by the kernel and the host size query.
 // nt: threads per CTA.
 struct StackSmem {
-    size_t h, xq, xd, hq, hd, desc, ids, w, order, tree, xch, total;
+    size_t h, xq, xd, hq, hd, desc, ids, w, order, own, tree, xch, total;
     // Every region starts on a 16-byte boundary (the activation blocks are read as uint4).
     static __host__ __device__ size_t up16(size_t o) { return (o + 15) & ~(size_t)15; }
     __host__ __device__ StackSmem(int dim, int ff, int k, bool exact, int nt) {
@@ -91,6 +123,7 @@ struct StackSmem {
         ids = o;   o = up16(o + (size_t)2 * kMaxPicks * 4);  // this and the previous layer
         w = o;     o = up16(o + (size_t)2 * kMaxPicks * 4);
         order = o; o = up16(o + (size_t)2 * kMaxPicks * 4);
+        own = o;   o = up16(o + (size_t)2 * (kMaxPicks + 1) * 4);  // owned pick indices + count
         tree = o;  o = up16(o + (size_t)nt * 8);  // also the K-segment partials [warp][lane]
         // scratch: table staging (kTableWords), one pick's fp32 SwiGLU output (ff), and
         // in the exact order the quad exchange records of every warp
@@ -131,14 +164,16 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
     uint32_t* xch_all = reinterpret_cast<uint32_t*>(smem + L.xch);
     float* hf = reinterpret_cast<float*>(smem + L.xch);   // SwiGLU output of this CTA's pick
     float* part = reinterpret_cast<float*>(smem + L.tree);  // K-segment partials [warp][lane]
+    int* sown = reinterpret_cast<int*>(smem + L.own);       // [2][kMaxPicks + 1]: picks this GPU owns, count last
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int dim = P.dim, ff = P.ff, k = P.k;
     const int nbx = dim >> 8, nbh = ff >> 8;
     const int G = gridDim.x, W = G * NW, gw = blockIdx.x * NW + warp;
-    const int my_pick = blockIdx.x * k / G;
-    const int pc0 = pick_cta_begin(my_pick, k), pc1 = pick_cta_begin(my_pick + 1, k);
-    const int pick_warps = (pc1 - pc0) * NW, pick_warp = (blockIdx.x - pc0) * NW + warp;
+    const StackShard& sh = P.sh;
+    const size_t yslot = (size_t)k * dim;  // one layer's expert rows
+    // expert rows of layer li: the bank's buffer, or (sharded) the exchange slot of its parity
+    auto ybuf = [&](int li) -> float* { return sh.world == 1 ? P.yrows : sh.yx + ((sh.epoch + li) & 1) * yslot; };
 
     fill_row_tables(P.tables, xch_all);
     for (int i = tid; i < dim; i += NT) hs[i] = __ldcg(P.h_in + i);
@@ -157,6 +192,13 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             for (int p = 0; p < k; ++p) rank += sid[cur * kMaxPicks + p] < me;
             sord[cur * kMaxPicks + rank] = tid;
         }
+        if (li < P.nl && warp == 0) {  // picks whose expert this GPU holds, in pick order
+            const int e = lane < k ? sid[cur * kMaxPicks + lane] : -1;
+            const bool mine = lane < k && e >= sh.own_begin && e < sh.own_end;
+            const uint32_t m = __ballot_sync(0xffffffffu, mine);
+            if (mine) sown[cur * (kMaxPicks + 1) + __popc(m & ((1u << lane) - 1u))] = lane;
+            if (lane == 0) sown[cur * (kMaxPicks + 1) + kMaxPicks] = __popc(m);
+        }
         if (li < P.nl)
             for (int i = tid; i < k * (int)(sizeof(ExpertDesc) / 4); i += NT) {
                 const int p = i / (int)(sizeof(ExpertDesc) / 4), wd = i % (int)(sizeof(ExpertDesc) / 4);
@@ -170,7 +212,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
         //    rows per thread and two such quads at a time, the rows of up to 3 picks of both
         //    loaded before the fma chains
         if (li > 0) {
-            const float* yr = P.yrows;
+            const float* yr = ybuf(li - 1);
             const int nq = dim >> 2;
             for (int q0 = tid; q0 < nq; q0 += 2 * NT) {
                 const int q1 = q0 + NT;
@@ -273,14 +315,16 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             // 2. gate/up, one row per lane: a CTA round covers 8 / SG row groups of 32 rows of
             //    both matrices, each split into SG K segments (one warp each); the segments
             //    are added in order and SwiGLU(g, u) goes to hbuf [pick][ff]
-            const int SG = P.s_gu, RGR = 8 / SG, rgpp = ff >> 5, nrg = k * rgpp;
+            const int* own = sown + cur * (kMaxPicks + 1);
+            const int kown = own[kMaxPicks];
+            const int SG = P.s_gu, RGR = 8 / SG, rgpp = ff >> 5, nrg = kown * rgpp;
             const int seg = warp % SG, mat = (warp / SG) & 1, rgl = warp / (2 * SG);
             const int per = (nbx + SG - 1) / SG, b0 = min(nbx, seg * per), b1 = min(nbx, b0 + per);
             for (int q = blockIdx.x; q * RGR < nrg; q += G) {
                 const int rg = q * RGR + rgl;
                 float y = 0.0f;
                 if (rg < nrg) {
-                    const int pick = rg / rgpp, row = (rg % rgpp) * 32 + lane;
+                    const int pick = own[rg / rgpp], row = (rg % rgpp) * 32 + lane;
                     const PackedMat& m = mat ? dsc[pick].up : dsc[pick].gate;
                     if (m.body != nullptr && m.k == dim && m.n == ff) y = lane_row_partial_any(m, row, b0, b1, xq, xd);
                     else if (lane == 0) atomicExch(P.err, 1);
@@ -295,7 +339,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                             g = __fadd_rn(g, part[((r2 * 2 + 0) * SG + s2) * 32 + lane]);
                             u = __fadd_rn(u, part[((r2 * 2 + 1) * SG + s2) * 32 + lane]);
                         }
-                        P.gu[(size_t)(rg2 / rgpp) * ff + (rg2 % rgpp) * 32 + lane] = swiglu(g, u, P.limit);
+                        P.gu[(size_t)own[rg2 / rgpp] * ff + (rg2 % rgpp) * 32 + lane] = swiglu(g, u, P.limit);
                     }
                 }
                 __syncthreads();
@@ -304,10 +348,10 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
 
             // 3. Q8_K(h) of every pick, then the down rows: a CTA round covers 16 / SD
             //    (pick, 32-row group) pairs, each split into SD K segments (one warp each)
-            const int SD = P.s_dn, PPR = 16 / SD, rgd = dim >> 5, npair = k * rgd;
+            const int SD = P.s_dn, PPR = 16 / SD, rgd = dim >> 5, npair = kown * rgd;
             uint32_t need = 0;  // picks whose rows this CTA's down rounds touch
             for (int q = blockIdx.x; q * PPR < npair; q += G)
-                for (int j = 0; j < PPR && q * PPR + j < npair; ++j) need |= 1u << ((q * PPR + j) / rgd);
+                for (int j = 0; j < PPR && q * PPR + j < npair; ++j) need |= 1u << own[(q * PPR + j) / rgd];
             const int nneed = __popc(need);
             for (int w0 = warp; w0 < nneed * nbh; w0 += 3 * NW) {  // up to 3 blocks per warp in flight
                 float v[3][8];
@@ -342,7 +386,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                     const int q = q0 + rr * G, pr = q * PPR + slot;
                     float y = 0.0f;
                     if (slot < PPR && pr < npair) {
-                        const int pick = pr / rgd, row = (pr % rgd) * 32 + lane;
+                        const int pick = own[pr / rgd], row = (pr % rgd) * 32 + lane;
                         const PackedMat& m = dsc[pick].down;
                         if (m.body != nullptr && m.k == ff && m.n == dim)
                             y = lane_row_partial_any(m, row, d0, d1, hq + (size_t)pick * nbh * kActStride, hd + pick * nbh);
@@ -356,17 +400,22 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                     if (pr2 < npair) {
                         float t = 0.0f;
                         for (int j = 0; j < SD; ++j) t = __fadd_rn(t, part[(rr * NW + s2 * SD + j) * 32 + lane]);
-                        P.yrows[(size_t)(pr2 / rgd) * dim + (pr2 % rgd) * 32 + lane] = t;
+                        const size_t o = (size_t)own[pr2 / rgd] * dim + (pr2 % rgd) * 32 + lane;
+                        ybuf(li)[o] = t;
+                        for (int r = 0; r < sh.world; ++r)  // the peers' copies of this layer's slot
+                            if (r != sh.rank) sh.peer_yx[r][((sh.epoch + li) & 1) * yslot + o] = t;
                     }
                 }
                 __syncthreads();
             }
         } else {
             // 2. gate/up rows (exact order: 4 threads per row, quad exchange) -> gu
-            const int rpw = 8, groups = ff / rpw, items = k * 2 * groups;
+            const int* own = sown + cur * (kMaxPicks + 1);
+            const int kown = own[kMaxPicks];
+            const int rpw = 8, groups = ff / rpw, items = kown * 2 * groups;
             uint32_t* xch = xch_all + warp * 32 * kXchWords;
             for (int it = gw; it < items; it += W) {
-                const int pick = it / (2 * groups), rem = it % (2 * groups);
+                const int pick = own[it / (2 * groups)], rem = it % (2 * groups);
                 const int group = rem >> 1, mat = rem & 1;
                 const PackedMat& m = mat ? dsc[pick].up : dsc[pick].gate;
                 const int row = group * rpw + lane / 4;
@@ -379,6 +428,10 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
 
             // 3. SwiGLU of this CTA's pick over all threads, Q8_K(h) per 256-block, then the
             //    pick's down rows (one thread per row, the reference's lane chains) -> yrows
+            // CTA c serves owned pick c * kown / G (none when this GPU owns no pick)
+            const int mi = blockIdx.x * max(kown, 1) / G, my_pick = kown > 0 ? own[mi] : 0;
+            const int pc0 = pick_cta_begin(mi, max(kown, 1)), pc1 = pick_cta_begin(mi + 1, max(kown, 1));
+            const int pick_warps = (pc1 - pc0) * NW, pick_warp = (blockIdx.x - pc0) * NW + warp;
             const float* g = P.gu + ((size_t)my_pick * 2) * ff;
             for (int i = tid; i < ff; i += NT) hf[i] = swiglu(__ldcg(g + i), __ldcg(g + ff + i), P.limit);
             __syncthreads();
@@ -392,14 +445,19 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             const PackedMat& m = dsc[my_pick].down;
             const int groups_d = dim >> 5;
             const bool ok = m.body != nullptr && m.k == ff && m.n == dim;
-            if (!ok && tid == 0) atomicExch(P.err, 1);
-            for (int g2 = pick_warp; g2 < groups_d; g2 += pick_warps) {
+            if (kown > 0 && !ok && tid == 0) atomicExch(P.err, 1);
+            for (int g2 = pick_warp; kown > 0 && g2 < groups_d; g2 += pick_warps) {
                 const int row = g2 * 32 + lane;
                 const float y = ok ? thread_row_dot_any<false>(m, row, hq, hd) : 0.0f;
-                P.yrows[(size_t)my_pick * dim + row] = y;
+                const size_t o = (size_t)my_pick * dim + row;
+                ybuf(li)[o] = y;
+                for (int r = 0; r < sh.world; ++r)
+                    if (r != sh.rank) sh.peer_yx[r][((sh.epoch + li) & 1) * yslot + o] = y;
             }
         }
+        if (sh.world > 1) __threadfence_system();  // this CTA's peer stores before the barrier
         if (!grid_barrier(P.bar, 2 * li + 2, P.err)) return;
+        if (sh.world > 1 && !exchange_rows(sh, li, P.err)) return;
     }
     // h after the last layer: each CTA writes its slice
     const int per = (dim + G - 1) / G;
@@ -455,7 +513,7 @@ bool stack_supported(int dim, int ff, int k, bool fast) {
 
 cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
                          const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit, float* gu,
-                         float* yrows, unsigned* bar, int* err, bool fast, cudaStream_t s) {
+                         float* yrows, unsigned* bar, int* err, bool fast, const StackShard& shard, cudaStream_t s) {
     const uint32_t* tables = nullptr;
     cudaError_t e = tables_device_ptr(&tables);
     if (e != cudaSuccess) return e;
@@ -478,6 +536,7 @@ cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k
     P.bar = bar;
     P.err = err;
     P.tables = tables;
+    P.sh = shard;
     const int nt = stack_threads(fast);
     P.s_gu = pick_gateup_segments(k, ff, dim >> 8, G);
     P.s_dn = pick_down_segments(k, dim, ff >> 8, G);

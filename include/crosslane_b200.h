@@ -142,6 +142,21 @@ uint64_t clb_bank_weight_bytes(const clb_bank* bank);
  * (CLB_BANK_PER_LAYER_KERNELS, or a geometry / device the persistent kernel cannot hold). */
 int32_t clb_bank_stack_persistent(const clb_bank* bank);
 
+/* ---- expert-ID sharding over the GPUs of one node (one process or thread per GPU) ----
+ * Each GPU's bank owns experts [expert_begin, expert_end) of every layer (contiguous
+ * blocks, together covering all experts). In clb_stack_decode* every GPU routes the same
+ * token, computes only the picks it owns, and stores their expert rows straight into every
+ * peer's exchange slot over NVLink; a per-layer counter per peer (bounded waits) says when
+ * a peer's rows are in place, and every GPU then runs the same combine, so all GPUs keep
+ * bit-identical residual streams. All GPUs must make the same stack calls in the same
+ * order. Replaces the per-layer gather that runtime.cpp:121-189 does across lanes. */
+#define CLB_EXCHANGE_HANDLE_BYTES 64
+/* The bank's exchange region as a CUDA IPC handle (64 bytes) for the other processes. */
+int32_t clb_bank_exchange_handle(clb_bank* bank, void* handle_out, clb_error_v1* err);
+/* Opens the peers' regions: handles = world x 64 bytes, indexed by rank (own entry
+ * ignored). world in [2, 8]; needs the persistent stack kernel. */
+int32_t clb_bank_connect(clb_bank* bank, int32_t rank, int32_t world, const void* handles, clb_error_v1* err);
+
 /* 1 if (layer, expert) is resident in this bank, else 0. Const, allocation free.
  * Replaces WarmRedirect::warm_contains (engine/strata/warm/runtime.hpp:14). */
 int32_t clb_bank_contains(const clb_bank* bank, uint32_t layer, int32_t expert);
