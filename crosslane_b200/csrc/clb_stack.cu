@@ -82,6 +82,36 @@ __device__ bool exchange_rows(const StackShard& sh, int li, int* err) {
     return __syncthreads_and(ok) != 0;
 }
 
+// K segments of the fast-order phases for `kown` picks on `grid` CTAs of 16 warps, chosen
+// to minimise the blocks one thread decodes (CTA rounds x blocks per segment; the smaller
+// count on ties). gate/up: SG in {1, 2, 4, 8}, a round = 8 / SG row groups of 32 rows x 2
+// matrices x SG segments. down: SD in {1, 2, 3, 4, 6, 8}, a round = 16 / SD (pick, row
+// group) pairs x SD segments. Every thread evaluates the same expression.
+__host__ __device__ inline int gateup_segments(int kown, int ff, int nb, int grid) {
+    int best = 1;
+    long best_cost = -1;
+    const int choices[4] = {1, 2, 4, 8};
+    for (int i = 0; i < 4; ++i) {
+        const int SG = choices[i];
+        const long rounds = ((long)kown * (ff / 32) + (8 / SG) - 1) / (8 / SG);
+        const long cost = (rounds + grid - 1) / grid * ((nb + SG - 1) / SG);
+        if (best_cost < 0 || cost < best_cost) best_cost = cost, best = SG;
+    }
+    return best;
+}
+__host__ __device__ inline int down_segments(int kown, int dim, int nb, int grid) {
+    int best = 1;
+    long best_cost = -1;
+    const int choices[6] = {1, 2, 3, 4, 6, 8};
+    for (int i = 0; i < 6; ++i) {
+        const int SD = choices[i];
+        const long rounds = ((long)kown * (dim / 32) + (16 / SD) - 1) / (16 / SD);
+        const long cost = (rounds + grid - 1) / grid * ((nb + SD - 1) / SD);
+        if (best_cost < 0 || cost < best_cost) best_cost = cost, best = SD;
+    }
+    return best;
+}
+
 // First CTA of pick p when gridDim.x CTAs are split over k picks (CTA c serves pick
 // c * k / gridDim.x).
 __device__ __forceinline__ int pick_cta_begin(int p, int k) { return (p * (int)gridDim.x + k - 1) / k; }
@@ -102,7 +132,6 @@ struct StackParams {
     unsigned* bar;           // grid barrier counter, zero before the launch
     int* err;
     const uint32_t* tables;  // compact selector tables (kTableWords)
-    int s_gu, s_dn;          // fast order: K segments of a row in the gate/up and down phases
     StackShard sh;           // expert-ID sharding over GPUs (world == 1: none)
 };
 
@@ -180,6 +209,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
 
     for (int li = 0; li <= P.nl; ++li) {
         const int cur = li & 1, prev = cur ^ 1;
+        bool stored_peer = false;  // this thread stored expert rows into a peer's slot
         // routing of this layer, and the ascending-id order of its picks
         if (li < P.nl && tid < k) {
             sid[cur * kMaxPicks + tid] = P.route_ids[(size_t)li * k + tid];
@@ -317,7 +347,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             //    are added in order and SwiGLU(g, u) goes to hbuf [pick][ff]
             const int* own = sown + cur * (kMaxPicks + 1);
             const int kown = own[kMaxPicks];
-            const int SG = P.s_gu, RGR = 8 / SG, rgpp = ff >> 5, nrg = kown * rgpp;
+            const int SG = gateup_segments(kown, ff, nbx, G), RGR = 8 / SG, rgpp = ff >> 5, nrg = kown * rgpp;
             const int seg = warp % SG, mat = (warp / SG) & 1, rgl = warp / (2 * SG);
             const int per = (nbx + SG - 1) / SG, b0 = min(nbx, seg * per), b1 = min(nbx, b0 + per);
             for (int q = blockIdx.x; q * RGR < nrg; q += G) {
@@ -348,7 +378,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
 
             // 3. Q8_K(h) of every pick, then the down rows: a CTA round covers 16 / SD
             //    (pick, 32-row group) pairs, each split into SD K segments (one warp each)
-            const int SD = P.s_dn, PPR = 16 / SD, rgd = dim >> 5, npair = kown * rgd;
+            const int SD = down_segments(kown, dim, nbh, G), PPR = 16 / SD, rgd = dim >> 5, npair = kown * rgd;
             uint32_t need = 0;  // picks whose rows this CTA's down rounds touch
             for (int q = blockIdx.x; q * PPR < npair; q += G)
                 for (int j = 0; j < PPR && q * PPR + j < npair; ++j) need |= 1u << own[(q * PPR + j) / rgd];
@@ -404,6 +434,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                         ybuf(li)[o] = t;
                         for (int r = 0; r < sh.world; ++r)  // the peers' copies of this layer's slot
                             if (r != sh.rank) sh.peer_yx[r][((sh.epoch + li) & 1) * yslot + o] = t;
+                        stored_peer = sh.world > 1;
                     }
                 }
                 __syncthreads();
@@ -453,9 +484,10 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                 ybuf(li)[o] = y;
                 for (int r = 0; r < sh.world; ++r)
                     if (r != sh.rank) sh.peer_yx[r][((sh.epoch + li) & 1) * yslot + o] = y;
+                stored_peer = sh.world > 1;
             }
         }
-        if (sh.world > 1) __threadfence_system();  // this CTA's peer stores before the barrier
+        if (stored_peer) __threadfence_system();  // this thread's peer stores before the barrier
         if (!grid_barrier(P.bar, 2 * li + 2, P.err)) return;
         if (sh.world > 1 && !exchange_rows(sh, li, P.err)) return;
     }
@@ -468,31 +500,6 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
 static int stack_threads(bool) { return 512; }
 
 size_t stack_smem(int dim, int ff, int k, bool fast) { return StackSmem(dim, ff, k, !fast, stack_threads(fast)).total; }
-
-// K segments of the fast-order phases, chosen to minimise the blocks one thread decodes
-// (CTA rounds x blocks per segment; the smaller count on ties).
-// gate/up: SG in {1, 2, 4, 8}, a round = 8 / SG row groups of 32 rows x 2 matrices.
-static int pick_gateup_segments(int k, int ff, int nb, int grid) {
-    int best = 1;
-    long best_cost = -1;
-    for (int SG : {1, 2, 4, 8}) {
-        const long rounds_total = ((long)k * (ff / 32) + (8 / SG) - 1) / (8 / SG);
-        const long cost = (rounds_total + grid - 1) / grid * ((nb + SG - 1) / SG);
-        if (best_cost < 0 || cost < best_cost) best_cost = cost, best = SG;
-    }
-    return best;
-}
-// down: SD in {1, 2, 3, 4}, a round = 16 / SD (pick, 32-row group) pairs.
-static int pick_down_segments(int k, int dim, int nb, int grid) {
-    int best = 1;
-    long best_cost = -1;
-    for (int SD : {1, 2, 3, 4}) {
-        const long rounds_total = ((long)k * (dim / 32) + (16 / SD) - 1) / (16 / SD);
-        const long cost = (rounds_total + grid - 1) / grid * ((nb + SD - 1) / SD);
-        if (best_cost < 0 || cost < best_cost) best_cost = cost, best = SD;
-    }
-    return best;
-}
 
 static int stack_grid() {
     int dev = 0, sms = 0;
@@ -538,8 +545,6 @@ cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k
     P.tables = tables;
     P.sh = shard;
     const int nt = stack_threads(fast);
-    P.s_gu = pick_gateup_segments(k, ff, dim >> 8, G);
-    P.s_dn = pick_down_segments(k, dim, ff >> 8, G);
     const size_t sm = stack_smem(dim, ff, k, fast);
     void (*kern)(StackParams) = fast ? k_stack<true, 512> : k_stack<false, 512>;
     if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))) return e;
