@@ -111,9 +111,9 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def make_inputs(rng, n):
+def make_inputs(rng, n, layers=LAYERS, experts=EXPERTS):
     xs = rng.standard_normal((n, DIM)).astype(np.float32)
-    logits = rng.standard_normal((n, LAYERS, EXPERTS)).astype(np.float32)
+    logits = rng.standard_normal((n, layers, experts)).astype(np.float32)
     return xs, logits
 
 
@@ -178,6 +178,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS, help="smaller stacks for quick checks only")
+    ap.add_argument("--experts", type=int, default=EXPERTS,
+                    help="experts per layer (profiling captures only: a small bank, same per-token work)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--policy", type=int, default=POLICY, help="quant type policy of the bank (2 = config 3 mix)")
     ap.add_argument("--quick", action="store_true", help="skip the e2e pass and the CPU baseline (tuning sweeps)")
@@ -209,10 +211,10 @@ def main():
     sharded = world > 1 and not args.replicas
     if sharded:  # expert-ID sharding: rank r holds experts [r*E/N, (r+1)*E/N), rows exchanged over NVLink
         from crosslane_b200.sharded import ShardedBank
-        bank = ShardedBank(n_layers=L, n_experts=EXPERTS, dim=DIM, ff=FF, max_picks=PICKS, device=local, rank=rank,
+        bank = ShardedBank(n_layers=L, n_experts=args.experts, dim=DIM, ff=FF, max_picks=PICKS, device=local, rank=rank,
                            world=world, exact_order=args.exact_order)
     else:
-        bank = cb.ExpertBank(n_layers=L, n_experts=EXPERTS, dim=DIM, ff=FF, max_picks=PICKS, device=local,
+        bank = cb.ExpertBank(n_layers=L, n_experts=args.experts, dim=DIM, ff=FF, max_picks=PICKS, device=local,
                              exact_order=args.exact_order)
     t0 = time.time()
     bank.fill_synthetic(SEED, args.policy)
@@ -223,12 +225,11 @@ def main():
 
     rng = np.random.default_rng(1000 if sharded else 1000 + rank)  # sharded: every rank decodes the same tokens
     n_in = args.warmup + args.steps
-    xs, logits = make_inputs(rng, n_in)
-    logits = logits[:, :L]
+    xs, logits = make_inputs(rng, n_in, L, args.experts)
     d_xs = torch.from_numpy(xs).cuda()
     d_logits_all = torch.from_numpy(np.ascontiguousarray(logits)).cuda()
     d_x = torch.empty(DIM, dtype=torch.float32, device="cuda")
-    d_lg = torch.empty((L, EXPERTS), dtype=torch.float32, device="cuda")
+    d_lg = torch.empty((L, args.experts), dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
 
     def step(i):
@@ -325,7 +326,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
         "scaling": "strong" if sharded else "weak",
         "vs_baseline": None, "dtype": "int8xIQ/fp32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "layers": L, "experts": EXPERTS, "dim": DIM, "ff": FF, "picks": PICKS,
+        "config": {"workload": WORKLOAD, "layers": L, "experts": args.experts, "dim": DIM, "ff": FF, "picks": PICKS,
                    "types": "IQ2_XXS/IQ2_XS/IQ1_M per (layer, expert), seed-drawn", "batch": 1,
                    "routing": "top-6 by sigmoid of N(0,1) logits, renormalised",
                    "parallelism": (f"expert-ID sharded x{world} (peer-store row exchange in the stack kernel)"
