@@ -200,6 +200,43 @@ class ExpertBank:
             C.c_void_p(d_x.data_ptr()), C.c_void_p(d_out.data_ptr()), phase_mask,
             C.c_void_p(stream) if stream else None, C.byref(err)), err)
 
+    # -- batched prefill (clb_prefill_*) --
+    def prefill_workspace_bytes(self, tokens: int, k: int) -> int:
+        return int(lib.clb_prefill_workspace_bytes(self._h, tokens, k))
+
+    def prefill_reserve(self, tokens: int, k: int) -> None:
+        err = ErrorV1()
+        check(lib.clb_prefill_reserve(self._h, tokens, k, C.byref(err)), err)
+
+    def prefill_layer(self, layer: int, ids, w, x) -> np.ndarray:
+        """ids/w [T][k], x [T][dim] host arrays -> out [T][dim] (synchronous)."""
+        ids, w, x = _i32(ids), _f32(w), _f32(x)
+        T, k = ids.shape
+        assert w.shape == (T, k) and x.shape == (T, self.dim)
+        out = np.empty((T, self.dim), np.float32)
+        err = ErrorV1()
+        check(lib.clb_prefill_layer(self._h, layer, T, k, _ptr(ids), _ptr(w), _ptr(x), _ptr(out), C.byref(err)), err)
+        return out
+
+    def prefill_layer_device(self, layer: int, d_ids, d_w, d_x, d_out, d_ws, d_resid=None, stream=None) -> None:
+        """torch tensors on this device: d_ids int32 [T][k], d_w [T][k], d_x/d_out [T][dim],
+        d_ws uint8 workspace (prefill_workspace_bytes); runs on the bank stream."""
+        T, k = d_ids.shape
+        err = ErrorV1()
+        check(lib.clb_prefill_layer_device(
+            self._h, layer, T, k, C.c_void_p(d_ids.data_ptr()), C.c_void_p(d_w.data_ptr()),
+            C.c_void_p(d_x.data_ptr()), C.c_void_p(d_resid.data_ptr()) if d_resid is not None else None,
+            C.c_void_p(d_out.data_ptr()), C.c_void_p(d_ws.data_ptr()), d_ws.numel(),
+            C.c_void_p(stream) if stream else None, C.byref(err)), err)
+
+    def prefill_phases_device(self, layer: int, d_ids, d_w, d_x, d_out, d_ws, phase_mask: int, stream=None) -> None:
+        T, k = d_ids.shape
+        err = ErrorV1()
+        check(lib.clb_prefill_phases_device(
+            self._h, layer, T, k, C.c_void_p(d_ids.data_ptr()), C.c_void_p(d_w.data_ptr()),
+            C.c_void_p(d_x.data_ptr()), C.c_void_p(d_out.data_ptr()), C.c_void_p(d_ws.data_ptr()), d_ws.numel(),
+            phase_mask, C.c_void_p(stream) if stream else None, C.byref(err)), err)
+
     def expert_info(self, layer: int, expert: int):
         """(ggml type id, payload bytes of gate+up+down) of a resident expert."""
         t = C.c_int32()

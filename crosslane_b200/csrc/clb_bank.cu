@@ -172,6 +172,12 @@ struct clb_bank {
     float* h_route_w = nullptr;
     std::map<std::pair<uint32_t, int>, cudaGraphExec_t> graphs, device_graphs;
     const float* graph_dx = nullptr;
+    // batched prefill (clb_prefill_*): grow-only device workspace and pinned host staging
+    void* pf_ws = nullptr;
+    size_t pf_ws_bytes = 0;
+    float *pf_hx = nullptr, *pf_hw = nullptr, *pf_dx = nullptr, *pf_dw = nullptr, *pf_dout = nullptr;
+    int32_t *pf_hids = nullptr, *pf_dids = nullptr;
+    int pf_tokens = 0, pf_k = 0;
 
     size_t L() const { return (size_t)cfg.n_layers; }
     size_t E() const { return (size_t)cfg.n_experts; }
@@ -219,6 +225,7 @@ struct clb_bank {
         if (flag) {
             cuda_check(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "error flag reset");
             if (flag == 2) throw Error(CLB_E_CUDA, "grid barrier of the stack kernel timed out");
+            if (flag == 3) throw Error(CLB_E_CUDA, "a tensor-core pipeline wait of the prefill kernel timed out");
             throw Error(CLB_E_INVALID, "a picked expert is not resident or has a mismatched shape");
         }
     }
@@ -310,7 +317,17 @@ struct clb_bank {
         cuda_check(cudaStreamSynchronize(stream), "descriptor sync");
     }
 
+    void free_prefill() {
+        for (void* p : {(void*)pf_ws, (void*)pf_dx, (void*)pf_dw, (void*)pf_dout, (void*)pf_dids})
+            if (p) cudaFree(p);
+        for (void* p : {(void*)pf_hx, (void*)pf_hw, (void*)pf_hids})
+            if (p) cudaFreeHost(p);
+        pf_ws = nullptr, pf_dx = pf_dw = pf_dout = nullptr, pf_dids = nullptr, pf_hx = pf_hw = nullptr;
+        pf_hids = nullptr, pf_ws_bytes = 0, pf_tokens = pf_k = 0;
+    }
+
     ~clb_bank() {
+        free_prefill();
         for (void* p : opened_peers) cudaIpcCloseMemHandle(p);
         for (auto& g : graphs) cudaGraphExecDestroy(g.second);
         for (auto& g : device_graphs) cudaGraphExecDestroy(g.second);
@@ -942,6 +959,136 @@ int32_t clb_stack_decode_device(clb_bank* bank, uint32_t first, int32_t nl, floa
             }
             cuda_check(cudaGraphLaunch(it->second, bank->stream), "graph launch");
         });
+    });
+}
+
+// ---- batched prefill ----
+static void prefill_check_layer(clb_bank* bank, uint32_t layer, int32_t tokens, int32_t k) {
+    const auto& c = bank->cfg;
+    require(layer < (uint32_t)c.n_layers, CLB_E_INVALID, "layer %u out of range", layer);
+    require(tokens >= 1 && tokens <= (1 << 20) && k >= 1 && k <= c.max_picks && k <= c.n_experts &&
+                (int64_t)tokens * k <= (1 << 24),
+            CLB_E_INVALID, "invalid prefill size (%d tokens x %d picks)", tokens, k);
+    require(clb::prefill_shape_supported(c.dim, c.ff), CLB_E_UNSUPPORTED, "prefill needs dim, ff multiples of 256");
+    for (size_t e = 0; e < bank->E(); ++e) {
+        if (!bank->resident[(size_t)layer * bank->E() + e]) continue;
+        const auto& d = bank->desc[(size_t)layer * bank->E() + e];
+        require(d.gate.type == CLB_IQ2_XXS && d.up.type == CLB_IQ2_XXS && d.down.type == CLB_IQ2_XXS,
+                CLB_E_UNSUPPORTED, "prefill supports IQ2_XXS experts only (expert %zu of layer %u)", e, layer);
+    }
+}
+
+uint64_t clb_prefill_workspace_bytes(const clb_bank* bank, int32_t tokens, int32_t k) {
+    if (!bank || tokens < 1 || k < 1) return 0;
+    return clb::prefill_workspace_bytes(tokens, k, bank->cfg.dim, bank->cfg.ff, bank->cfg.n_experts);
+}
+
+static int32_t prefill_device(clb_bank* bank, uint32_t layer, int32_t tokens, int32_t k, const int32_t* d_ids,
+                              const float* d_w, const float* d_x, const float* d_resid, float* d_out, void* d_ws,
+                              uint64_t ws_bytes, int32_t phase_mask, void* stream, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    return guarded(err, [&] {
+        bank->check_usable();
+        prefill_check_layer(bank, layer, tokens, k);
+        require(d_ids && d_w && d_x && d_out && d_ws, CLB_E_INVALID, "null device buffer");
+        require(ws_bytes >= clb_prefill_workspace_bytes(bank, tokens, k), CLB_E_INVALID, "prefill workspace too small");
+        require(phase_mask > 0 && phase_mask < 32, CLB_E_INVALID, "invalid phase mask");
+        DeviceGuard g(bank->cfg.device);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : bank->stream;
+        bank->device_step([&] {
+            const auto& c = bank->cfg;
+            cuda_check(clb::launch_prefill(bank->d_desc + (size_t)layer * bank->E(), c.n_experts, d_x, d_ids, d_w,
+                                           tokens, k, c.dim, c.ff, c.limit, d_resid, d_out, d_ws, bank->d_err,
+                                           phase_mask, s),
+                       "prefill launch");
+        });
+    });
+}
+
+int32_t clb_prefill_layer_device(clb_bank* bank, uint32_t layer, int32_t tokens, int32_t k, const int32_t* d_ids,
+                                 const float* d_w, const float* d_x, const float* d_resid, float* d_out, void* d_ws,
+                                 uint64_t ws_bytes, void* stream, clb_error_v1* err) {
+    return prefill_device(bank, layer, tokens, k, d_ids, d_w, d_x, d_resid, d_out, d_ws, ws_bytes, 31, stream, err);
+}
+
+int32_t clb_prefill_phases_device(clb_bank* bank, uint32_t layer, int32_t tokens, int32_t k, const int32_t* d_ids,
+                                  const float* d_w, const float* d_x, float* d_out, void* d_ws, uint64_t ws_bytes,
+                                  int32_t phase_mask, void* stream, clb_error_v1* err) {
+    return prefill_device(bank, layer, tokens, k, d_ids, d_w, d_x, nullptr, d_out, d_ws, ws_bytes, phase_mask, stream,
+                          err);
+}
+
+int32_t clb_prefill_reserve(clb_bank* bank, int32_t tokens, int32_t k, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        bank->check_usable();
+        const auto& c = bank->cfg;
+        require(tokens >= 1 && k >= 1 && k <= c.max_picks, CLB_E_INVALID, "invalid prefill reservation");
+        if (tokens <= bank->pf_tokens && k <= bank->pf_k) return;
+        DeviceGuard g(c.device);
+        cuda_check(cudaStreamSynchronize(bank->stream), "stream sync");
+        const int T = std::max(tokens, bank->pf_tokens), K = std::max(k, bank->pf_k);
+        bank->free_prefill();
+        const size_t ws = clb::prefill_workspace_bytes(T, K, c.dim, c.ff, c.n_experts);
+        auto dmal = [&](void** p, size_t n) {
+            cudaError_t e = cudaMalloc(p, std::max<size_t>(n, 256));
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                bank->free_prefill();
+                throw Error(CLB_E_NOMEM, std::string("cudaMalloc (prefill): ") + cudaGetErrorString(e));
+            }
+        };
+        dmal(&bank->pf_ws, ws);
+        dmal(reinterpret_cast<void**>(&bank->pf_dx), (size_t)T * c.dim * 4);
+        dmal(reinterpret_cast<void**>(&bank->pf_dout), (size_t)T * c.dim * 4);
+        dmal(reinterpret_cast<void**>(&bank->pf_dw), (size_t)T * K * 4);
+        dmal(reinterpret_cast<void**>(&bank->pf_dids), (size_t)T * K * 4);
+        cuda_check(cudaMallocHost(reinterpret_cast<void**>(&bank->pf_hx), (size_t)T * c.dim * 4), "cudaMallocHost");
+        cuda_check(cudaMallocHost(reinterpret_cast<void**>(&bank->pf_hw), (size_t)T * K * 4), "cudaMallocHost");
+        cuda_check(cudaMallocHost(reinterpret_cast<void**>(&bank->pf_hids), (size_t)T * K * 4), "cudaMallocHost");
+        bank->pf_ws_bytes = ws;
+        bank->pf_tokens = T;
+        bank->pf_k = K;
+    });
+}
+
+int32_t clb_prefill_layer(clb_bank* bank, uint32_t layer, int32_t tokens, int32_t k, const int32_t* ids,
+                          const float* w, const float* x, float* out, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    if (tokens > bank->pf_tokens || k > bank->pf_k) {
+        const int32_t rc = clb_prefill_reserve(bank, tokens, k, err);
+        if (rc != CLB_OK) return rc;
+    }
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        bank->check_usable();
+        const auto& c = bank->cfg;
+        prefill_check_layer(bank, layer, tokens, k);
+        require(ids && w && x && out, CLB_E_INVALID, "null buffer");
+        for (int32_t t = 0; t < tokens; ++t) bank->validate_ids(layer, ids + (size_t)t * k, k, true);
+        require(finite_all(w, (size_t)tokens * k), CLB_E_NONFINITE, "non-finite route weight");
+        require(finite_all(x, (size_t)tokens * c.dim), CLB_E_NONFINITE, "non-finite activation");
+        DeviceGuard g(c.device);
+        const size_t nx = (size_t)tokens * c.dim, np = (size_t)tokens * k;
+        bank->device_step([&] {
+            std::memcpy(bank->pf_hx, x, nx * 4);
+            std::memcpy(bank->pf_hids, ids, np * 4);
+            std::memcpy(bank->pf_hw, w, np * 4);
+            cuda_check(cudaMemcpyAsync(bank->pf_dx, bank->pf_hx, nx * 4, cudaMemcpyHostToDevice, bank->stream), "x H2D");
+            cuda_check(cudaMemcpyAsync(bank->pf_dids, bank->pf_hids, np * 4, cudaMemcpyHostToDevice, bank->stream),
+                       "ids H2D");
+            cuda_check(cudaMemcpyAsync(bank->pf_dw, bank->pf_hw, np * 4, cudaMemcpyHostToDevice, bank->stream), "w H2D");
+            cuda_check(clb::launch_prefill(bank->d_desc + (size_t)layer * bank->E(), c.n_experts, bank->pf_dx,
+                                           bank->pf_dids, bank->pf_dw, tokens, k, c.dim, c.ff, c.limit, nullptr,
+                                           bank->pf_dout, bank->pf_ws, bank->d_err, 31, bank->stream),
+                       "prefill launch");
+            cuda_check(cudaMemcpyAsync(bank->pf_hx, bank->pf_dout, nx * 4, cudaMemcpyDeviceToHost, bank->stream),
+                       "out D2H");
+            bank->check_err_flag();
+        });
+        std::memcpy(out, bank->pf_hx, nx * 4);
+        require(finite_all(out, nx), CLB_E_NONFINITE, "non-finite prefill output");
     });
 }
 

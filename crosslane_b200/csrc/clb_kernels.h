@@ -57,6 +57,14 @@ cudaError_t launch_down2(const ExpertDesc* experts, const int* ids, const float*
                          float* yrows, int* counters, int* err, bool fast, cudaStream_t s);
 cudaError_t launch_mv2(const PackedMat& m, const void* q, float* y, cudaStream_t s);
 
+// batched prefill through one layer (clb_prefill.cu): grouped tcgen05 GEMMs over IQ2_XXS experts.
+// phase_mask: 1 group + quantise x, 2 gate/up GEMM, 4 SwiGLU + quantise h, 8 down GEMM, 16 combine.
+size_t prefill_workspace_bytes(int T, int k, int dim, int ff, int E);
+bool prefill_shape_supported(int dim, int ff);
+cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const int* ids, const float* w, int T, int k,
+                           int dim, int ff, float limit, const float* resid, float* out, void* ws, int* err,
+                           int phase_mask, cudaStream_t s);
+
 // persistent whole-stack kernel (clb_stack.cu)
 constexpr int kMaxPeers = 8;  // GPUs of one node
 // Expert-ID sharding of the stack over `world` GPUs: this GPU holds experts [own_begin,

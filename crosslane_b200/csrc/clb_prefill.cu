@@ -1,0 +1,819 @@
+// Batched prefill through one routed-expert layer: the T x k picks of T tokens are grouped
+// per expert and each expert's FFN runs as two grouped tensor-core GEMMs over its tokens
+// (gate/up over Q8_K(x), then down over Q8_K(h)), followed by the per-token combine in
+// ascending expert id (engine/strata/warm/runtime.cpp:184-187 applied to every token).
+//
+// Arithmetic. Per 256-value block b the reference forms exact integers
+// sum_k w_int[k] * q[k] (q8k_core.hpp:43-91), with w_int = (2s+1) * sign * mag for
+// IQ2_XXS (|w_int| <= 43 * 31 = 1333, an exact fp16 integer) and q the Q8_K activation
+// (|q| <= 127, exact in fp16). tcgen05.mma (kind::f16, fp32 accumulators in tensor memory)
+// forms that block sum exactly for a 128-row x N-token tile (every partial sum is an
+// integer below 2^24); the epilogue adds (d_w[row, b] * d_x[token, b]) * sum_b into fp32
+// registers block by block and scales by 1/8 at the end (an IQ2 weight is
+// d * (2s+1)/8 * sign * mag). Per (token, row) that is the decode kernels' fast order.
+//
+// Data layout. The picks are grouped by expert into a list of slots (t*k + p), each
+// expert's run padded to a multiple of 16 entries; activations are gathered into list
+// order once (fp16 Q8_K values [list][K], scales [K/256][list]), so the token rows of a
+// tile are contiguous. Gate/up outputs and Q8_K(h) stay in list order; the down GEMM
+// writes expert rows by slot for the combine.
+//
+// GEMM kernel: one CTA per SM, persistent over tiles (expert, 128 weight rows, up to 128
+// list entries), warp-specialised around one pipeline of 64-value K stages that runs
+// across tiles, synchronised by mbarriers only:
+//  * weight warp: bulk copies (cp.async.bulk) of the packed weight pieces of a stage
+//    (16 B per row, 2 KB) and of the rows' block scales into rings kPfRA stages deep;
+//  * B warp: the B operand of each stage by TMA (2-D tensor map over the list-order
+//    activations, 128-byte swizzle, box height = the tile's entries rounded up to 16) into
+//    a ring kPfRB stages deep, and each tile's activation scales;
+//  * MMA warp: per stage, four tcgen05.mma (A from tensor memory, B from shared memory)
+//    into one of two block accumulators, and commits that free the operands;
+//  * 8 decoder warps: each thread turns one 32-weight chunk of one row per stage into exact
+//    fp16 integers and stores them to the A operand in tensor memory (tcgen05.st, row m in
+//    lane m, values k, k+1 in one column), double-buffered; one stage after a block's
+//    accumulator is complete each warp reads its 32 lanes x 64 columns (tcgen05.ld) and
+//    applies the block's scales in registers.
+// Control loops keep ring positions as counters (no divisions in the per-stage path).
+// Every wait is bounded: on time-out the CTA flags *err and an abort flag that ends every
+// loop, lets copies in flight land, waits (bounded) for its MMAs and frees its tensor memory.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "clb_device.cuh"
+#include "clb_kernels.h"
+#include "clb_v2.cuh"
+
+namespace clb {
+
+namespace {
+
+constexpr int kPfDecWarps = 8;                // warp w: TMEM lane quarter w & 3, chunk w >> 2 of the stage
+constexpr int kPfProducerWarp = kPfDecWarps, kPfMmaWarp = kPfDecWarps + 1, kPfBWarp = kPfDecWarps + 2;
+constexpr int kPfThreads = 32 * (kPfDecWarps + 3);
+constexpr int kPfMaxN = 128;                  // list entries per tile (MMA N <= 128)
+constexpr int kPfStageK = 64;                 // K values per stage (4 MMAs of K = 16)
+constexpr int kPfRA = 8;                      // weight-piece ring (stages)
+constexpr int kPfRB = 6;                      // B operand ring (stages)
+constexpr int kPfRawStage = 128 * 16;         // one 16-byte piece per weight row
+constexpr int kPfBStage = kPfMaxN * 128;      // 128 rows x 64 fp16, 128-byte swizzled
+constexpr int kPfMaxNb = 32;                  // K <= 8192
+constexpr int kPfTmemCols = 512;
+constexpr uint32_t kPfACol = 256;             // A buffers at columns 256, 288 (accumulators 0, 128)
+constexpr uint32_t kPfSpin = 1u << 22;
+constexpr int kErrPrefillWait = 3;
+
+// Magnitudes biased by +128 so that 0x64XX = 1024 + XX as fp16: +8, +25, +43 and -8, -25, -43.
+constexpr uint32_t kPos2b = 0x00AB9988u;
+constexpr uint32_t kNeg2b = 0x00556778u;
+
+// mbarriers
+enum : int {
+    kRawFull = 0,
+    kRawEmpty = kRawFull + kPfRA,
+    kDwFull = kRawEmpty + kPfRA,
+    kDwEmpty = kDwFull + 4,
+    kBFull = kDwEmpty + 4,
+    kBEmpty = kBFull + kPfRB,
+    kAFull = kBEmpty + kPfRB,
+    kAEmpty = kAFull + 2,
+    kAccFull = kAEmpty + 2,
+    kAccEmpty = kAccFull + 2,
+    kDxsFull = kAccEmpty + 2,
+    kDxsEmpty = kDxsFull + 2,
+    kDrain = kDxsEmpty + 2,
+    kNumBars = kDrain + 1
+};
+__host__ __device__ constexpr bool pf_warp_counted(int i) {  // barriers that every decoder warp arrives on
+    return (i >= kRawEmpty && i < kRawEmpty + kPfRA) || (i >= kDwEmpty && i < kDwEmpty + 4) ||
+           (i >= kAFull && i < kAFull + 2) || (i >= kAccEmpty && i < kAccEmpty + 2) ||
+           (i >= kDxsEmpty && i < kDxsEmpty + 2);
+}
+
+struct PfSmem {
+    // [0, 64K) IQ2_XXS tables; the B ring starts at the first 1024-byte boundary after them
+    static constexpr uint32_t braw = 64 * 1024;                            // + alignment pad
+    static constexpr uint32_t raw = braw + 1024 + kPfRB * kPfBStage;       // weight pieces ring
+    static constexpr uint32_t dw = raw + kPfRA * kPfRawStage;              // [4][128] fp16 row scales
+    static constexpr uint32_t dxs = dw + 4 * 256;                          // [2][kPfMaxNb][kPfMaxN] floats
+    static constexpr uint32_t bars = dxs + 2 * kPfMaxNb * kPfMaxN * 4;
+    static constexpr uint32_t tslot = bars + kNumBars * 8;
+    static constexpr uint32_t abort_flag = tslot + 4;
+    static constexpr uint32_t total = abort_flag + 12;
+};
+static_assert(PfSmem::raw % 16 == 0 && PfSmem::dxs % 16 == 0 && PfSmem::bars % 8 == 0, "aligned regions");
+static_assert(PfSmem::total <= 227 * 1024, "fits one CTA per SM");
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, P1;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+// Bounded wait; gives up early once another thread has raised the abort flag.
+__device__ __noinline__ bool pf_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+    for (uint32_t it = 0; it < kPfSpin; ++it) {
+        if (mbar_try(bar, parity)) return true;
+        if ((it & 255u) == 255u && *abort_flag) return false;
+    }
+    atomicExch(err, kErrPrefillWait);
+    *abort_flag = 1;
+    return false;
+}
+__device__ __forceinline__ bool pf_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+    return mbar_try(bar, parity) || pf_wait_slow(bar, parity, abort_flag, err);
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_2d(uint32_t dst, const void* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(dst),
+        "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+// IQ2_XXS grid and sign selector tables (the first 64 KB of the decode kernels' tables).
+__device__ __forceinline__ void fill_xxs_tables(const uint32_t* __restrict__ compact) {
+    uint4* a = reinterpret_cast<uint4*>(clb_dyn_smem + kRowTabXXS);
+    for (int s = threadIdx.x; s < 4096; s += blockDim.x) {
+        const int slot = s >> 4, part = s & 15;
+        const uint32_t v = __ldg(compact + (part < 8 ? slot : 2816 + (slot & 127)));
+        a[s] = make_uint4(v, v, v, v);
+    }
+}
+
+// Four biased bytes (value + 128) -> four fp16 (value * scale), exact because |value * scale|
+// <= 1333: (1024 + byte) * scale - 1152 * scale in one fused rounding.
+__device__ __forceinline__ void biased4_to_half(uint32_t w, __half2 s2, __half2 noff, uint32_t& h01, uint32_t& h23) {
+    const uint32_t a = __byte_perm(w, 0x64646464u, 0x5140), b = __byte_perm(w, 0x64646464u, 0x7362);
+    const __half2 ra = __hfma2(*reinterpret_cast<const __half2*>(&a), s2, noff);
+    const __half2 rb = __hfma2(*reinterpret_cast<const __half2*>(&b), s2, noff);
+    h01 = *reinterpret_cast<const uint32_t*>(&ra);
+    h23 = *reinterpret_cast<const uint32_t*>(&rb);
+}
+
+// Position in a ring of R slots: slot and the parity of the slot's current use.
+template <int R>
+struct Ring {
+    int slot = 0;
+    uint32_t phase = 0;
+    int round = 0;
+    __device__ __forceinline__ void next() {
+        if (++slot == R) {
+            slot = 0;
+            phase ^= 1u;
+            ++round;
+        }
+    }
+};
+
+}  // namespace
+
+struct PrefillGemm {
+    CUtensorMap bmaps[kPfMaxN / 16];  // B rows of the activations [P][K] fp16, box 64 x 16(i+1)
+    const ExpertDesc* desc;           // this layer's descriptors [E]
+    int role;                         // 0: gate + up (64 rows of each per tile), 1: down (128 rows)
+    const int4* tiles;                // (expert, first list entry, entries, 0) per chunk of an expert's run
+    const int* ntiles;                // chunks
+    const int* list;                  // slot (t * k + p) per list entry, -1 for padding
+    const float* actd;                // activation Q8_K scales [K/256][P]
+    int P;                            // list length (multiple of 16)
+    int K, nrows, mtiles;             // K, rows of one weight matrix, 128-row tiles per chunk
+    float* out;                       // role 0: [P][2][ff] in list order; role 1: [T*k][dim] by slot
+    int* err;
+    const uint32_t* tables;
+};
+
+struct PfTile {
+    int e, mt, first, ntok;
+};
+__device__ __forceinline__ PfTile pf_tile(const PrefillGemm& G, int i) {  // CTA-local tile i
+    const int t = blockIdx.x + i * gridDim.x;
+    const int4 c = G.tiles[t / G.mtiles];
+    return PfTile{c.x, t % G.mtiles, c.y, c.z};
+}
+
+__global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_constant__ PrefillGemm G) {
+    uint8_t* sm = clb_dyn_smem;
+    const uint32_t sbase = smem_u32(sm);
+    const uint32_t sb0 = (sbase + PfSmem::braw + 1023u) & ~1023u;  // B ring (1024-byte aligned for the swizzle)
+    const uint32_t sraw = sbase + PfSmem::raw, sdw = sbase + PfSmem::dw, sdxs = sbase + PfSmem::dxs;
+    const uint32_t bar0 = sbase + PfSmem::bars;
+    auto bar = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + PfSmem::abort_flag);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nb = G.K >> 8, S = nb * (256 / kPfStageK);
+    const int ntot = *G.ntiles * G.mtiles;
+    const int my_tiles = (int)blockIdx.x < ntot ? (ntot - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total = my_tiles * S;  // stages of this CTA
+
+    fill_xxs_tables(G.tables);
+    if (tid == 0) {
+        for (int i = 0; i < kNumBars; ++i) mbar_init(bar(i), pf_warp_counted(i) ? kPfDecWarps : 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sbase + PfSmem::tslot),
+                     "r"(kPfTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + PfSmem::tslot);
+
+    if (warp == kPfProducerWarp) {
+        // ---------------- weight pieces and row scales, kPfRA stages ahead ----------------
+        if (lane == 0 && total > 0) {
+            Ring<kPfRA> rr;
+            Ring<4> dr;
+            int tile = 0, s = 0;
+            bool ok = false;
+            const uint8_t *pa0 = nullptr, *pa1 = nullptr;
+            const uint16_t *pd0 = nullptr, *pd1 = nullptr;
+            size_t plane = 0, dstride = 0;
+            for (int g = 0; g < total; ++g) {
+                if (s == 0) {  // tile setup
+                    const PfTile t = pf_tile(G, tile);
+                    const ExpertDesc& ex = G.desc[t.e];
+                    const PackedMat& m0 = G.role == 0 ? ex.gate : ex.down;
+                    const PackedMat& m1 = G.role == 0 ? ex.up : ex.down;
+                    const int row0 = G.role == 0 ? t.mt * 64 : t.mt * 128, rows = G.role == 0 ? 64 : 128;
+                    ok = m0.body && m1.body && m0.type == CLB_IQ2_XXS && m1.type == CLB_IQ2_XXS && m0.k == G.K &&
+                         m1.k == G.K && m0.n == m1.n && row0 + rows <= m0.n;
+                    if (!ok) atomicExch(G.err, 1);
+                    plane = (size_t)m0.n * 16;
+                    dstride = (size_t)m0.n;
+                    pa0 = m0.body + (size_t)row0 * 16;
+                    pa1 = m1.body + (size_t)row0 * 16;
+                    pd0 = m0.d + row0;
+                    pd1 = m1.d + row0;
+                }
+                if (rr.round > 0 && !pf_wait(bar(kRawEmpty + rr.slot), rr.phase ^ 1u, abort_flag, G.err)) break;
+                const uint32_t full = bar(kRawFull + rr.slot), dst = sraw + (uint32_t)rr.slot * kPfRawStage;
+                if (!ok) {
+                    mbar_arrive(full);
+                } else {
+                    mbar_expect_tx(full, kPfRawStage);
+                    if (G.role == 0) {
+                        bulk_g2s(dst, pa0, kPfRawStage / 2, full);
+                        bulk_g2s(dst + kPfRawStage / 2, pa1, kPfRawStage / 2, full);
+                    } else {
+                        bulk_g2s(dst, pa0, kPfRawStage, full);
+                    }
+                }
+                pa0 += plane;
+                pa1 += plane;
+                rr.next();
+                if ((s & 3) == 0) {
+                    if (dr.round > 0 && !pf_wait(bar(kDwEmpty + dr.slot), dr.phase ^ 1u, abort_flag, G.err)) break;
+                    const uint32_t dfull = bar(kDwFull + dr.slot), ddst = sdw + (uint32_t)dr.slot * 256;
+                    if (!ok) {
+                        mbar_arrive(dfull);
+                    } else {
+                        mbar_expect_tx(dfull, 256);
+                        if (G.role == 0) {
+                            bulk_g2s(ddst, pd0, 128, dfull);
+                            bulk_g2s(ddst + 128, pd1, 128, dfull);
+                        } else {
+                            bulk_g2s(ddst, pd0, 256, dfull);
+                        }
+                    }
+                    pd0 += dstride;
+                    pd1 += dstride;
+                    dr.next();
+                }
+                if (++s == S) {
+                    s = 0;
+                    ++tile;
+                }
+            }
+        }
+    } else if (warp == kPfBWarp) {
+        // ---------------- B operand (TMA) and the tiles' activation scales, kPfRB stages ahead ----------------
+        if (lane == 0 && total > 0) {
+            Ring<kPfRB> br;
+            int tile = 0, s = 0, first = 0, n = 16, x = 0;
+            for (int g = 0; g < total; ++g) {
+                if (s == 0) {
+                    const PfTile t = pf_tile(G, tile);
+                    first = t.first;
+                    n = (t.ntok + 15) & ~15;
+                    x = 0;
+                    const int xs = tile & 1;
+                    if (tile >= 2 && !pf_wait(bar(kDxsEmpty + xs), ((tile >> 1) & 1) ^ 1u, abort_flag, G.err)) break;
+                    const uint32_t dfull = bar(kDxsFull + xs);
+                    mbar_expect_tx(dfull, (uint32_t)(nb * n * 4));
+                    for (int bb = 0; bb < nb; ++bb)
+                        bulk_g2s(sdxs + (uint32_t)(xs * kPfMaxNb + bb) * (kPfMaxN * 4), G.actd + (size_t)bb * G.P + first,
+                                 (uint32_t)n * 4, dfull);
+                }
+                if (br.round > 0 && !pf_wait(bar(kBEmpty + br.slot), br.phase ^ 1u, abort_flag, G.err)) break;
+                const uint32_t full = bar(kBFull + br.slot);
+                mbar_expect_tx(full, (uint32_t)n * 128);
+                tma_2d(sb0 + (uint32_t)br.slot * kPfBStage, &G.bmaps[(n >> 4) - 1], x, first, full);
+                x += kPfStageK;
+                br.next();
+                if (++s == S) {
+                    s = 0;
+                    ++tile;
+                }
+            }
+        }
+    } else if (warp == kPfMmaWarp) {
+        // ---------------- MMAs: four per stage into one of two block accumulators ----------------
+        if (lane == 0 && total > 0) {
+            // B descriptors: K-major, 128-byte swizzle, 8-row groups 1024 B apart
+            const uint64_t bdesc0 = ((uint64_t)1 << 16) | ((uint64_t)64 << 32) | ((uint64_t)1 << 46) |
+                                    ((uint64_t)2 << 61) | (uint64_t)((sb0 >> 4) & 0x3FFFu);
+            Ring<kPfRB> br;
+            int tile = 0, s = 0, q = 0, blk = 0;
+            uint32_t idesc = 0;
+            int next_n = (pf_tile(G, 0).ntok + 15) & ~15;
+            for (int g = 0; g < total; ++g) {
+                if (s == 0) {
+                    idesc = (1u << 4) | ((uint32_t)(next_n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+                    if (tile + 1 < my_tiles) next_n = (pf_tile(G, tile + 1).ntok + 15) & ~15;
+                }
+                if (!pf_wait(bar(kAFull + (g & 1)), (g >> 1) & 1, abort_flag, G.err)) break;
+                if (!pf_wait(bar(kBFull + br.slot), br.phase, abort_flag, G.err)) break;
+                const int a = blk & 1;
+                if (q == 0 && blk >= 2 && !pf_wait(bar(kAccEmpty + a), ((blk >> 1) & 1) ^ 1u, abort_flag, G.err)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint64_t bdesc = bdesc0 + (uint64_t)(br.slot * (kPfBStage >> 4));
+                const uint32_t da = tmem + kPfACol + (uint32_t)(g & 1) * 32, dd = tmem + (uint32_t)a * kPfMaxN;
+#pragma unroll
+                for (int j = 0; j < kPfStageK / 16; ++j) {
+                    const uint32_t accum = (q > 0 || j > 0) ? 1u : 0u;
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %3, 0;\n\t"
+                        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, p;\n\t}\n" ::"r"(dd),
+                        "r"(da + 8u * j), "l"(bdesc + 2u * j), "r"(accum), "r"(idesc)
+                        : "memory");
+                }
+                umma_commit(bar(kBEmpty + br.slot));
+                umma_commit(bar(kAEmpty + (g & 1)));
+                if (q == 3) umma_commit(bar(kAccFull + a));
+                br.next();
+                if (++q == 4) {
+                    q = 0;
+                    ++blk;
+                }
+                if (++s == S) {
+                    s = 0;
+                    ++tile;
+                }
+            }
+        }
+    } else {
+        // ---------------- decoders / epilogue (warps 0-7) ----------------
+        const uint32_t lb = (uint32_t)lane * 4u;
+        const int dr = 32 * (warp & 3) + lane, dj = warp >> 2;  // row, 32-value chunk of the stage
+        const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
+        const __half2 off2 = __float2half2_rn(1152.0f);
+        const int ecol0 = 64 * dj;                              // epilogue columns [ecol0, ecol0 + 64)
+        const __half* dwring = reinterpret_cast<const __half*>(sm + PfSmem::dw);
+        int te_i = -1, te_first = 0, te_ntok = 0, te_mt = 0;
+        float acc[64];
+#pragma unroll
+        for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+
+        auto uwait = [&](int b, uint32_t parity) {  // warp-uniform bounded wait
+            return __all_sync(0xffffffffu, pf_wait(bar(b), parity, abort_flag, G.err));
+        };
+        auto half_block = [&](uint32_t taddr, const float* dv, float dw, float* a32) {
+            uint32_t r[32];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                  "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                  "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+                  "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+                  "=r"(r[30]), "=r"(r[31])
+                : "r"(taddr));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+                const float4 d4 = reinterpret_cast<const float4*>(dv)[j4];
+                a32[4 * j4 + 0] = __fmaf_rn(__fmul_rn(dw, d4.x), __uint_as_float(r[4 * j4 + 0]), a32[4 * j4 + 0]);
+                a32[4 * j4 + 1] = __fmaf_rn(__fmul_rn(dw, d4.y), __uint_as_float(r[4 * j4 + 1]), a32[4 * j4 + 1]);
+                a32[4 * j4 + 2] = __fmaf_rn(__fmul_rn(dw, d4.z), __uint_as_float(r[4 * j4 + 2]), a32[4 * j4 + 2]);
+                a32[4 * j4 + 3] = __fmaf_rn(__fmul_rn(dw, d4.w), __uint_as_float(r[4 * j4 + 3]), a32[4 * j4 + 3]);
+            }
+        };
+        auto epilogue = [&](int e) -> bool {
+            const int i = e / nb, b = e - i * nb, a = e & 1;
+            if (i != te_i) {
+                te_i = i;
+                const PfTile t = pf_tile(G, i);
+                te_first = t.first;
+                te_ntok = t.ntok;
+                te_mt = t.mt;
+            }
+            if (!uwait(kDwFull + (e & 3), (e >> 2) & 1)) return false;
+            if (b == 0 && !uwait(kDxsFull + (i & 1), (i >> 1) & 1)) return false;
+            if (!uwait(kAccFull + a, (e >> 1) & 1)) return false;
+            const float dw = __half2float(dwring[(e & 3) * 128 + dr]);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const float* dv = reinterpret_cast<const float*>(sm + PfSmem::dxs) + ((i & 1) * kPfMaxNb + b) * kPfMaxN + ecol0;
+            const uint32_t taddr = tmem + tlane + (uint32_t)(a * kPfMaxN + ecol0);
+            if (ecol0 < te_ntok) half_block(taddr, dv, dw, acc);
+            if (ecol0 + 32 < te_ntok) half_block(taddr + 32, dv + 32, dw, acc + 32);
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(bar(kAccEmpty + a));
+                mbar_arrive(bar(kDwEmpty + (e & 3)));
+            }
+            if (b == nb - 1) {  // the tile is complete: store its rows, start the next one from zero
+#pragma unroll
+                for (int j = 0; j < 64; ++j) {
+                    const int n = ecol0 + j;
+                    if (n < te_ntok) {
+                        const float v = __fmul_rn(0.125f, acc[j]);
+                        if (G.role == 0)
+                            G.out[((size_t)(te_first + n) * 2 + (dr >> 6)) * G.nrows + te_mt * 64 + (dr & 63)] = v;
+                        else
+                            G.out[(size_t)G.list[te_first + n] * G.nrows + te_mt * 128 + dr] = v;
+                    }
+                    acc[j] = 0.0f;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kDxsEmpty + (i & 1)));
+            }
+            return true;
+        };
+
+        Ring<kPfRA> rr;
+        bool live = true;
+        for (int g = 0; g < total && live; ++g) {
+            if (!uwait(kRawFull + rr.slot, rr.phase)) break;
+            const uint2 cw = *reinterpret_cast<const uint2*>(sm + PfSmem::raw + rr.slot * kPfRawStage + dr * 16 + dj * 8);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kRawEmpty + rr.slot));
+            rr.next();
+            const uint32_t gw = cw.x, sw = cw.y;
+            const uint32_t sc = (((sw & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27;  // 2s + 1
+            const __half2 s2 = __float2half2_rn((float)sc);
+            const __half2 noff = __hneg2(__hmul2(off2, s2));
+            uint32_t v[16];
+#pragma unroll
+            for (int grp = 0; grp < 4; ++grp) {
+                const uint32_t selj = 0x5504u | ((uint32_t)grp << 4);
+                const uint32_t sel = tab32(kRowTabXXS + prmt2(gw, lb, selj)) | tab32(kRowTabXXS + 128 + prmt2(sw, lb, selj));
+                biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel), s2, noff, v[4 * grp], v[4 * grp + 1]);
+                biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel >> 16), s2, noff, v[4 * grp + 2], v[4 * grp + 3]);
+            }
+            // A buffer g & 1 was last read by the MMAs of stage g - 2
+            if (g >= 2 && !uwait(kAEmpty + (g & 1), ((g >> 1) & 1) ^ 1u)) break;
+            asm volatile(
+                "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+                "%14, %15, %16};" ::"r"(tmem + tlane + kPfACol + (uint32_t)(g & 1) * 32 + (uint32_t)dj * 16),
+                "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+                "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+                : "memory");
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kAFull + (g & 1)));
+            if ((g & 3) == 1 && g >= 4) live = epilogue((g >> 2) - 1);
+        }
+        if (live && !*abort_flag && total > 0) epilogue(total / 4 - 1);
+    }
+
+    __syncthreads();
+    if (*abort_flag) {  // let copies already in flight land before the shared memory is released
+        uint64_t t0, t1;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        do {
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+        } while (t1 - t0 < 200000u);
+    }
+    // drain: every MMA this CTA issued has completed before the tensor memory is freed
+    if (warp == kPfMmaWarp && lane == 0 && total > 0) {
+        umma_commit(bar(kDrain));
+        bool done = false;
+        for (uint32_t it = 0; it < kPfSpin && !done; ++it) done = mbar_try(bar(kDrain), 0);
+        if (!done) atomicExch(G.err, kErrPrefillWait);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols));
+}
+
+// ---------------------------------------------------------------------------------------
+// Grouping of the T x k picks by expert (one CTA of 1024 threads): list[] holds the slots
+// t*k+p expert after expert, in slot order within an expert, each expert's run padded with
+// -1 to a multiple of 16 entries; tiles[] one entry per chunk of at most kPfMaxN entries.
+__global__ void __launch_bounds__(1024) k_prefill_group(const int* __restrict__ ids, int T, int k, int E, int P,
+                                                        int* __restrict__ list, int4* __restrict__ tiles,
+                                                        int* __restrict__ ntiles, int* __restrict__ err) {
+    __shared__ int cnt[kMaxExperts], off[kMaxExperts], toff[kMaxExperts];
+    const int n = T * k;
+    for (int p = threadIdx.x; p < P; p += blockDim.x) list[p] = -1;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = ids[i];
+        if (e < 0 || e >= E) atomicExch(err, 1);
+        else atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int o = 0, to = 0;
+        for (int e = 0; e < E; ++e) {
+            off[e] = o, toff[e] = to;
+            o += (cnt[e] + 15) & ~15;
+            to += (cnt[e] + kPfMaxN - 1) / kPfMaxN;
+        }
+        *ntiles = to;
+    }
+    __syncthreads();
+    // stable placement by one warp, 32 slots at a time: slot i goes after every smaller slot
+    // of the same expert (rank among equal lanes from __match_any_sync)
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        for (int i0 = 0; i0 < n; i0 += 32) {
+            const int i = i0 + lane;
+            const int e = i < n ? ids[i] : -1;
+            const bool valid = e >= 0 && e < E;
+            const unsigned m = __match_any_sync(0xffffffffu, valid ? e : -1);
+            const int rank = __popc(m & ((1u << lane) - 1u));
+            const int base = valid ? off[e] : 0;
+            __syncwarp();
+            if (valid) {
+                list[base + rank] = i;
+                if (rank == 0) off[e] = base + __popc(m);
+            }
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const int start = off[e] - cnt[e];
+        for (int j = 0; j * kPfMaxN < cnt[e]; ++j)
+            tiles[toff[e] + j] = make_int4(e, start + j * kPfMaxN, min(kPfMaxN, cnt[e] - j * kPfMaxN), 0);
+    }
+}
+
+// Q8_K of 256 values held 8 per lane into int8 (qs), the scale (*d) and fp16 copies (q16).
+__device__ __forceinline__ void quant_block_fp16(float v[8], int8_t* qs, float* d, __half* q16) {
+    const int lane = threadIdx.x & 31;
+    warp_quant_regs(v, qs, d);
+    const uint2 w = *reinterpret_cast<const uint2*>(qs + lane * 8);
+    const uint32_t ws[2] = {w.x, w.y};
+    __align__(16) __half h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = __int2half_rn((int)(int8_t)(ws[i >> 2] >> (8 * (i & 3))));
+    *reinterpret_cast<uint4*>(q16 + lane * 8) = *reinterpret_cast<const uint4*>(h);
+}
+
+// Q8_K of the token rows (one warp per 256-value block).
+__global__ void __launch_bounds__(256) k_prefill_quant(const float* __restrict__ x, int nrows, int cols,
+                                                       int8_t* __restrict__ qs, float* __restrict__ d,
+                                                       __half* __restrict__ q16) {
+    const int nbr = cols >> 8;
+    const int blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (blk >= nrows * nbr) return;
+    const int row = blk / nbr, b = blk % nbr;
+    const float4* src = reinterpret_cast<const float4*>(x + (size_t)row * cols + b * 256 + lane * 8);
+    const float4 lo = src[0], hi = src[1];
+    float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    const size_t o = (size_t)row * cols + b * 256;
+    quant_block_fp16(v, qs + o, d + blk, q16 + o);
+}
+
+// Token rows of Q8_K(x) into list order: xg16[p] = q16[token of list[p]], dxg[b][p] its scales
+// (zeros for padding entries). One warp per (entry, 256-value block).
+__global__ void __launch_bounds__(256) k_prefill_gather(const int* __restrict__ list, int P, int k, int cols,
+                                                        const __half* __restrict__ q16, const float* __restrict__ d,
+                                                        __half* __restrict__ xg16, float* __restrict__ dxg) {
+    const int nbr = cols >> 8;
+    const int blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (blk >= P * nbr) return;
+    const int p = blk / nbr, b = blk % nbr, sl = list[p];
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    float dv = 0.0f;
+    if (sl >= 0) {
+        const int t = sl / k;
+        v = *reinterpret_cast<const uint4*>(q16 + (size_t)t * cols + b * 256 + lane * 8);
+        dv = d[(size_t)t * nbr + b];
+    }
+    *reinterpret_cast<uint4*>(xg16 + (size_t)p * cols + b * 256 + lane * 8) = v;
+    if (lane == 0) dxg[(size_t)b * P + p] = dv;
+}
+
+// SwiGLU of the gate/up rows (list order) and Q8_K of h: qh16[p] fp16 values, dhg[b][p]
+// scales; padding entries get zeros. One warp per (entry, 256-value block).
+__global__ void __launch_bounds__(256) k_prefill_act(const int* __restrict__ list, int P, int ff, float limit,
+                                                     const float* __restrict__ gu, int8_t* __restrict__ qh,
+                                                     __half* __restrict__ qh16, float* __restrict__ dhg) {
+    const int nbr = ff >> 8;
+    const int blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (blk >= P * nbr) return;
+    const int p = blk / nbr, b = blk % nbr;
+    const size_t o = (size_t)p * ff + b * 256;
+    if (list[p] < 0) {
+        *reinterpret_cast<uint4*>(qh16 + o + lane * 8) = make_uint4(0u, 0u, 0u, 0u);
+        if (lane == 0) dhg[(size_t)b * P + p] = 0.0f;
+        return;
+    }
+    const float* g = gu + (size_t)p * 2 * ff + b * 256 + lane * 8;
+    const float* u = g + ff;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = swiglu(g[i], u[i], limit);
+    quant_block_fp16(v, qh + o, dhg + (size_t)b * P + p, qh16 + o);
+}
+
+// out[t] = fma over the token's picks in ascending expert id of (w, expert row), then
+// + resid when given (runtime.cpp:184-187).
+__global__ void k_prefill_combine(const float* __restrict__ y, const int* __restrict__ ids, const float* __restrict__ w,
+                                  int k, int dim, const float* __restrict__ resid, float* __restrict__ out) {
+    const int t = blockIdx.y;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= dim) return;
+    const int* id = ids + (size_t)t * k;
+    float acc = 0.0f;
+    int prev = -1;
+    for (int o = 0; o < k; ++o) {
+        int best = -1;
+        for (int p = 0; p < k; ++p)
+            if (id[p] > prev && (best < 0 || id[p] < id[best])) best = p;
+        if (best < 0) break;
+        prev = id[best];
+        acc = __fmaf_rn(w[(size_t)t * k + best], y[((size_t)t * k + best) * dim + c], acc);
+    }
+    if (resid) acc = __fadd_rn(resid[(size_t)t * dim + c], acc);
+    out[(size_t)t * dim + c] = acc;
+}
+
+namespace {
+struct PrefillWs {
+    int P;
+    int* list;
+    int4* tiles;
+    int* ntiles;
+    int8_t* qx;
+    float* dx;
+    __half* qx16;
+    __half* xg16;
+    float* dxg;
+    float* gu;
+    int8_t* qh;
+    __half* qh16;
+    float* dhg;
+    float* y;
+};
+
+size_t carve(void* base, int T, int k, int dim, int ff, int E, PrefillWs* ws) {
+    const size_t slots = (size_t)T * k;
+    const size_t P = (slots + 15 * std::min<size_t>((size_t)E, slots) + 15) & ~(size_t)15;
+    const size_t nbx = dim / 256, nbh = ff / 256;
+    size_t off = 0;
+    auto take = [&](size_t n) {
+        const size_t r = off;
+        off += (n + 255) & ~(size_t)255;
+        return r;
+    };
+    const size_t o_list = take(P * 4), o_tiles = take(((size_t)E + slots / kPfMaxN + 1) * 16), o_nt = take(16);
+    const size_t o_qx = take((size_t)T * dim), o_dx = take((size_t)T * nbx * 4), o_qx16 = take((size_t)T * dim * 2);
+    const size_t o_xg16 = take(P * dim * 2), o_dxg = take(nbx * P * 4), o_gu = take(P * 2 * ff * 4);
+    const size_t o_qh = take(P * ff), o_qh16 = take(P * ff * 2), o_dhg = take(nbh * P * 4), o_y = take(slots * dim * 4);
+    if (ws && base) {
+        uint8_t* p = static_cast<uint8_t*>(base);
+        ws->P = (int)P;
+        ws->list = reinterpret_cast<int*>(p + o_list);
+        ws->tiles = reinterpret_cast<int4*>(p + o_tiles);
+        ws->ntiles = reinterpret_cast<int*>(p + o_nt);
+        ws->qx = reinterpret_cast<int8_t*>(p + o_qx);
+        ws->dx = reinterpret_cast<float*>(p + o_dx);
+        ws->qx16 = reinterpret_cast<__half*>(p + o_qx16);
+        ws->xg16 = reinterpret_cast<__half*>(p + o_xg16);
+        ws->dxg = reinterpret_cast<float*>(p + o_dxg);
+        ws->gu = reinterpret_cast<float*>(p + o_gu);
+        ws->qh = reinterpret_cast<int8_t*>(p + o_qh);
+        ws->qh16 = reinterpret_cast<__half*>(p + o_qh16);
+        ws->dhg = reinterpret_cast<float*>(p + o_dhg);
+        ws->y = reinterpret_cast<float*>(p + o_y);
+    }
+    return off;
+}
+}  // namespace
+
+size_t prefill_workspace_bytes(int T, int k, int dim, int ff, int E) { return carve(nullptr, T, k, dim, ff, E, nullptr); }
+
+bool prefill_shape_supported(int dim, int ff) {
+    return dim % 256 == 0 && ff % 256 == 0 && dim >= 512 && ff >= 512 && dim / 256 <= kPfMaxNb &&
+           ff / 256 <= kPfMaxNb;
+}
+
+namespace {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// Tensor maps over B rows [P][K] fp16 (list order): box 64 values x 16 (i + 1) rows, 128-byte swizzle.
+cudaError_t encode_bmaps(CUtensorMap* maps, const __half* base, int P, int K) {
+    static EncodeTiledFn encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess) return e;
+        if (!fn || q != cudaDriverEntryPointSuccess) return cudaErrorNotSupported;
+        encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)P};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t es[2] = {1, 1};
+    for (int i = 0; i < kPfMaxN / 16; ++i) {
+        const cuuint32_t box[2] = {(cuuint32_t)kPfStageK, (cuuint32_t)(16 * (i + 1))};
+        if (encode(&maps[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    return cudaSuccess;
+}
+}  // namespace
+
+cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const int* ids, const float* w, int T, int k,
+                           int dim, int ff, float limit, const float* resid, float* out, void* wsp, int* err,
+                           int phase_mask, cudaStream_t s) {
+    PrefillWs ws{};
+    carve(wsp, T, k, dim, ff, E, &ws);
+    const int P = ws.P;
+    const uint32_t* tables = nullptr;
+    cudaError_t e = tables_device_ptr(&tables);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    if ((e = cudaFuncSetAttribute(k_prefill_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PfSmem::total)) !=
+        cudaSuccess)
+        return e;
+    const int nbx = dim / 256, nbh = ff / 256;
+    if (phase_mask & 1) {
+        k_prefill_group<<<1, 1024, 0, s>>>(ids, T, k, E, P, ws.list, ws.tiles, ws.ntiles, err);
+        k_prefill_quant<<<(T * nbx + 7) / 8, 256, 0, s>>>(x, T, dim, ws.qx, ws.dx, ws.qx16);
+        k_prefill_gather<<<(P * nbx + 7) / 8, 256, 0, s>>>(ws.list, P, k, dim, ws.qx16, ws.dx, ws.xg16, ws.dxg);
+    }
+    PrefillGemm g{};
+    g.desc = desc;
+    g.tiles = ws.tiles;
+    g.ntiles = ws.ntiles;
+    g.list = ws.list;
+    g.P = P;
+    g.err = err;
+    g.tables = tables;
+    if (phase_mask & 2) {
+        if ((e = encode_bmaps(g.bmaps, ws.xg16, P, dim)) != cudaSuccess) return e;
+        g.role = 0;
+        g.actd = ws.dxg;
+        g.K = dim;
+        g.nrows = ff;
+        g.mtiles = ff / 64;
+        g.out = ws.gu;
+        k_prefill_gemm<<<sms, kPfThreads, PfSmem::total, s>>>(g);
+    }
+    if (phase_mask & 4)
+        k_prefill_act<<<(P * nbh + 7) / 8, 256, 0, s>>>(ws.list, P, ff, limit, ws.gu, ws.qh, ws.qh16, ws.dhg);
+    if (phase_mask & 8) {
+        if ((e = encode_bmaps(g.bmaps, ws.qh16, P, ff)) != cudaSuccess) return e;
+        g.role = 1;
+        g.actd = ws.dhg;
+        g.K = ff;
+        g.nrows = dim;
+        g.mtiles = dim / 128;
+        g.out = ws.y;
+        k_prefill_gemm<<<sms, kPfThreads, PfSmem::total, s>>>(g);
+    }
+    if (phase_mask & 16) k_prefill_combine<<<dim3((dim + 255) / 256, T), 256, 0, s>>>(ws.y, ids, w, k, dim, resid, out);
+    return cudaGetLastError();
+}
+
+}  // namespace clb

@@ -230,6 +230,43 @@ int32_t clb_stack_decode(clb_bank* bank, uint32_t first_layer, int32_t n_layers,
 int32_t clb_stack_decode_device(clb_bank* bank, uint32_t first_layer, int32_t n_layers, float* d_x,
                                 const float* d_logits, clb_error_v1* err);
 
+/* ---- batched prefill through one layer (grouped tensor-core GEMMs) ----
+ * For T tokens with k picks each: out[t] = [resid[t] +] sum over token t's picks in
+ * ascending expert id of fma(w, expert(x[t])), i.e. clb_layer_execute applied to every
+ * token (warm_execute's combine, runtime.cpp:184-187). The T*k picks are grouped by
+ * expert; each expert's gate/up and down run as tcgen05 GEMMs with the IQ2_XXS weights
+ * decoded once per 128 tokens into exact fp16 integers and the Q8_K activations as fp16
+ * integers, per-256-block scales applied from fp32 tensor-memory accumulators. Results
+ * agree with the CPU lane to fp32 reassociation (not bit for bit). Every resident expert
+ * of the layer must be IQ2_XXS (else CLB_E_UNSUPPORTED); dim and ff multiples of 256,
+ * at most 8192. No counterpart in crosslane's lanes (they decode one token at a time). */
+
+/* Device bytes of workspace clb_prefill_layer_device needs for `tokens` x `k` picks. */
+uint64_t clb_prefill_workspace_bytes(const clb_bank* bank, int32_t tokens, int32_t k);
+
+/* Device-pointer prefill on the bank's stream (or `stream`), no synchronisation:
+ * d_ids/d_w [tokens][k] (distinct ids per token, all resident; an id out of range or not
+ * resident sets the bank's error flag, reported by the next host-synchronising call),
+ * d_x/d_out [tokens][dim], d_resid NULL or [tokens][dim], d_ws >= the workspace size. */
+int32_t clb_prefill_layer_device(clb_bank* bank, uint32_t layer, int32_t tokens, int32_t k, const int32_t* d_ids,
+                                 const float* d_w, const float* d_x, const float* d_resid, float* d_out, void* d_ws,
+                                 uint64_t ws_bytes, void* stream, clb_error_v1* err);
+
+/* Profiling form: only the kernels in phase_mask (1 grouping + Q8_K(x), 2 gate/up GEMM,
+ * 4 SwiGLU + Q8_K(h), 8 down GEMM, 16 combine); later phases read what earlier ones left
+ * in d_ws, so a phase runs alone only after a full call with the same arguments. */
+int32_t clb_prefill_phases_device(clb_bank* bank, uint32_t layer, int32_t tokens, int32_t k, const int32_t* d_ids,
+                                  const float* d_w, const float* d_x, float* d_out, void* d_ws, uint64_t ws_bytes,
+                                  int32_t phase_mask, void* stream, clb_error_v1* err);
+
+/* Allocates (grow-only) the bank's own prefill workspace and pinned staging for up to
+ * `tokens` x `k`; clb_prefill_layer calls it when a call is larger than the reservation. */
+int32_t clb_prefill_reserve(clb_bank* bank, int32_t tokens, int32_t k, clb_error_v1* err);
+
+/* Host-buffer prefill, synchronous: ids/w [tokens][k], x/out [tokens][dim]. */
+int32_t clb_prefill_layer(clb_bank* bank, uint32_t layer, int32_t tokens, int32_t k, const int32_t* ids,
+                          const float* w, const float* x, float* out, clb_error_v1* err);
+
 /* The bank's CUDA stream (cudaStream_t) and a synchronisation helper. */
 void* clb_bank_stream(clb_bank* bank);
 int32_t clb_bank_synchronize(clb_bank* bank, clb_error_v1* err);
