@@ -18,7 +18,7 @@
 // tile are contiguous. Gate/up outputs and Q8_K(h) stay in list order; the down GEMM
 // writes expert rows by slot for the combine.
 //
-// GEMM kernel: one CTA per SM, persistent over tiles (expert, 128 weight rows, up to 128
+// GEMM kernel: one CTA per SM, persistent over tiles (expert, 128 weight rows, up to 64
 // list entries), warp-specialised around one pipeline of 64-value K stages that runs
 // across tiles, synchronised by mbarriers only:
 //  * weight warp: bulk copies (cp.async.bulk) of the packed weight pieces of a stage
@@ -27,12 +27,15 @@
 //    activations, 128-byte swizzle, box height = the tile's entries rounded up to 16) into
 //    a ring kPfRB stages deep, and each tile's activation scales;
 //  * MMA warp: per stage, four tcgen05.mma (A from tensor memory, B from shared memory)
-//    into one of two block accumulators, and commits that free the operands;
-//  * 8 decoder warps: each thread turns one 32-weight chunk of one row per stage into exact
-//    fp16 integers and stores them to the A operand in tensor memory (tcgen05.st, row m in
-//    lane m, values k, k+1 in one column), double-buffered; one stage after a block's
-//    accumulator is complete each warp reads its 32 lanes x 64 columns (tcgen05.ld) and
-//    applies the block's scales in registers.
+//    into one of kPfAcc block accumulators, and one commit that frees the stage's operands
+//    (one loop iteration per block, ring slots and accumulate flags known at compile time);
+//  * 16 decoder warps: each thread turns 16 weights of one row per stage into exact fp16
+//    integers and stores them to the A operand in tensor memory (tcgen05.st, row m in lane
+//    m, values k, k+1 in one column; kPfABuf buffers), the store of one stage overlapping
+//    the decode of the next;
+//  * 4 epilogue warps (one per tensor-memory lane quarter): per block, D * d_w * d_x added
+//    into running tile sums that also live in tensor memory; the tile's last block writes
+//    the rows out.
 // Control loops keep ring positions as counters (no divisions in the per-stage path).
 // Every wait is bounded: on time-out the CTA flags *err and an abort flag that ends every
 // loop, lets copies in flight land, waits (bounded) for its MMAs and frees its tensor memory.
@@ -48,18 +51,25 @@ namespace clb {
 
 namespace {
 
-constexpr int kPfDecWarps = 8;                // warp w: TMEM lane quarter w & 3, chunk w >> 2 of the stage
-constexpr int kPfProducerWarp = kPfDecWarps, kPfMmaWarp = kPfDecWarps + 1, kPfBWarp = kPfDecWarps + 2;
-constexpr int kPfThreads = 32 * (kPfDecWarps + 3);
-constexpr int kPfMaxN = 128;                  // list entries per tile (MMA N <= 128)
+constexpr int kPfDecWarps = 16;               // warp w: TMEM lane quarter w & 3, 16-value part w >> 2 of the stage
+constexpr int kPfEpiWarps = 4;                // warp kPfDecWarps + r: lane quarter r
+constexpr int kPfEpiWarp0 = kPfDecWarps;
+constexpr int kPfProducerWarp = kPfDecWarps + kPfEpiWarps, kPfMmaWarp = kPfProducerWarp + 1, kPfBWarp = kPfProducerWarp + 2;
+constexpr int kPfThreads = 32 * (kPfDecWarps + kPfEpiWarps + 3);
+constexpr int kPfMaxN = 64;                   // list entries per tile (MMA N <= 64)
 constexpr int kPfStageK = 64;                 // K values per stage (4 MMAs of K = 16)
 constexpr int kPfRA = 8;                      // weight-piece ring (stages)
-constexpr int kPfRB = 6;                      // B operand ring (stages)
+constexpr int kPfRB = 8;                      // B operand ring (stages; two blocks)
 constexpr int kPfRawStage = 128 * 16;         // one 16-byte piece per weight row
-constexpr int kPfBStage = kPfMaxN * 128;      // 128 rows x 64 fp16, 128-byte swizzled
+constexpr int kPfBStage = kPfMaxN * 128;      // 64 rows x 64 fp16, 128-byte swizzled
 constexpr int kPfMaxNb = 32;                  // K <= 8192
+constexpr int kPfAcc = 4;                     // block accumulators (64 columns each, from column 0)
+constexpr int kPfABuf = 4;                    // A operand buffers (32 columns each)
+constexpr int kPfDwRing = 8;                  // row-scale ring (blocks)
 constexpr int kPfTmemCols = 512;
-constexpr uint32_t kPfACol = 256;             // A buffers at columns 256, 288 (accumulators 0, 128)
+constexpr uint32_t kPfRCol = kPfAcc * kPfMaxN;          // running tile sums
+constexpr uint32_t kPfACol = kPfRCol + kPfMaxN;         // A buffers
+static_assert(kPfACol + 32 * kPfABuf <= kPfTmemCols, "tensor memory budget");
 constexpr uint32_t kPfSpin = 1u << 22;
 constexpr int kErrPrefillWait = 3;
 
@@ -72,30 +82,31 @@ enum : int {
     kRawFull = 0,
     kRawEmpty = kRawFull + kPfRA,
     kDwFull = kRawEmpty + kPfRA,
-    kDwEmpty = kDwFull + 4,
-    kBFull = kDwEmpty + 4,
-    kBEmpty = kBFull + kPfRB,
-    kAFull = kBEmpty + kPfRB,
-    kAEmpty = kAFull + 2,
-    kAccFull = kAEmpty + 2,
-    kAccEmpty = kAccFull + 2,
-    kDxsFull = kAccEmpty + 2,
+    kDwEmpty = kDwFull + kPfDwRing,
+    kBFull = kDwEmpty + kPfDwRing,
+    kStageDone = kBFull + kPfRB,  // MMAs of the stage complete: its B slot and A buffer are free
+    kAFull = kStageDone + kPfRB,
+    kAccFull = kAFull + kPfABuf,
+    kAccEmpty = kAccFull + kPfAcc,
+    kDxsFull = kAccEmpty + kPfAcc,
     kDxsEmpty = kDxsFull + 2,
     kDrain = kDxsEmpty + 2,
     kNumBars = kDrain + 1
 };
-__host__ __device__ constexpr bool pf_warp_counted(int i) {  // barriers that every decoder warp arrives on
-    return (i >= kRawEmpty && i < kRawEmpty + kPfRA) || (i >= kDwEmpty && i < kDwEmpty + 4) ||
-           (i >= kAFull && i < kAFull + 2) || (i >= kAccEmpty && i < kAccEmpty + 2) ||
-           (i >= kDxsEmpty && i < kDxsEmpty + 2);
+__host__ __device__ constexpr uint32_t pf_bar_count(int i) {
+    return ((i >= kRawEmpty && i < kRawEmpty + kPfRA) || (i >= kAFull && i < kAFull + kPfABuf)) ? kPfDecWarps
+           : ((i >= kDwEmpty && i < kDwEmpty + kPfDwRing) || (i >= kAccEmpty && i < kAccEmpty + kPfAcc) ||
+              (i >= kDxsEmpty && i < kDxsEmpty + 2))
+               ? kPfEpiWarps
+               : 1;
 }
 
 struct PfSmem {
     // [0, 64K) IQ2_XXS tables; the B ring starts at the first 1024-byte boundary after them
     static constexpr uint32_t braw = 64 * 1024;                            // + alignment pad
     static constexpr uint32_t raw = braw + 1024 + kPfRB * kPfBStage;       // weight pieces ring
-    static constexpr uint32_t dw = raw + kPfRA * kPfRawStage;              // [4][128] fp16 row scales
-    static constexpr uint32_t dxs = dw + 4 * 256;                          // [2][kPfMaxNb][kPfMaxN] floats
+    static constexpr uint32_t dw = raw + kPfRA * kPfRawStage;              // [kPfDwRing][128] fp16 row scales
+    static constexpr uint32_t dxs = dw + kPfDwRing * 256;                  // [2][kPfMaxNb][kPfMaxN] floats
     static constexpr uint32_t bars = dxs + 2 * kPfMaxNb * kPfMaxN * 4;
     static constexpr uint32_t tslot = bars + kNumBars * 8;
     static constexpr uint32_t abort_flag = tslot + 4;
@@ -139,6 +150,22 @@ __device__ __forceinline__ bool pf_wait(uint32_t bar, uint32_t parity, volatile 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
+// D (+)= A . B^T with A in tensor memory and B described by a shared-memory descriptor.
+template <bool ACCUMULATE>
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc) {
+    if (ACCUMULATE)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 1, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+            "r"(a), "l"(bdesc), "r"(idesc)
+            : "memory");
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 0, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+            "r"(a), "l"(bdesc), "r"(idesc)
+            : "memory");
+}
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
                  "l"(src), "r"(bytes), "r"(bar)
@@ -149,6 +176,21 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const void* map, int x, int
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
             "r"(dst),
         "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
 
@@ -172,7 +214,8 @@ __device__ __forceinline__ void biased4_to_half(uint32_t w, __half2 s2, __half2 
     h23 = *reinterpret_cast<const uint32_t*>(&rb);
 }
 
-// Position in a ring of R slots: slot and the parity of the slot's current use.
+// Position in a ring of R slots: slot, the parity of the slot's current use, and how many
+// times the ring has wrapped.
 template <int R>
 struct Ring {
     int slot = 0;
@@ -229,7 +272,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
 
     fill_xxs_tables(G.tables);
     if (tid == 0) {
-        for (int i = 0; i < kNumBars; ++i) mbar_init(bar(i), pf_warp_counted(i) ? kPfDecWarps : 1);
+        for (int i = 0; i < kNumBars; ++i) mbar_init(bar(i), pf_bar_count(i));
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -247,7 +290,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
         // ---------------- weight pieces and row scales, kPfRA stages ahead ----------------
         if (lane == 0 && total > 0) {
             Ring<kPfRA> rr;
-            Ring<4> dr;
+            Ring<kPfDwRing> dr;
             int tile = 0, s = 0;
             bool ok = false;
             const uint8_t *pa0 = nullptr, *pa1 = nullptr;
@@ -329,7 +372,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
                         bulk_g2s(sdxs + (uint32_t)(xs * kPfMaxNb + bb) * (kPfMaxN * 4), G.actd + (size_t)bb * G.P + first,
                                  (uint32_t)n * 4, dfull);
                 }
-                if (br.round > 0 && !pf_wait(bar(kBEmpty + br.slot), br.phase ^ 1u, abort_flag, G.err)) break;
+                if (br.round > 0 && !pf_wait(bar(kStageDone + br.slot), br.phase ^ 1u, abort_flag, G.err)) break;
                 const uint32_t full = bar(kBFull + br.slot);
                 mbar_expect_tx(full, (uint32_t)n * 128);
                 tma_2d(sb0 + (uint32_t)br.slot * kPfBStage, &G.bmaps[(n >> 4) - 1], x, first, full);
@@ -343,134 +386,144 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
         }
     } else if (warp == kPfMmaWarp) {
         // ---------------- MMAs: four per stage into one of two block accumulators ----------------
+        // One loop iteration per block (4 stages): B slots 4 (blk & 1) + q, A buffer q.
         if (lane == 0 && total > 0) {
             // B descriptors: K-major, 128-byte swizzle, 8-row groups 1024 B apart
             const uint64_t bdesc0 = ((uint64_t)1 << 16) | ((uint64_t)64 << 32) | ((uint64_t)1 << 46) |
                                     ((uint64_t)2 << 61) | (uint64_t)((sb0 >> 4) & 0x3FFFu);
-            Ring<kPfRB> br;
-            int tile = 0, s = 0, q = 0, blk = 0;
+            const int nblk = total / 4;
+            int tile = 0, b = 0;
             uint32_t idesc = 0;
             int next_n = (pf_tile(G, 0).ntok + 15) & ~15;
-            for (int g = 0; g < total; ++g) {
-                if (s == 0) {
+            for (int blk = 0; blk < nblk; ++blk) {
+                if (b == 0) {
                     idesc = (1u << 4) | ((uint32_t)(next_n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
                     if (tile + 1 < my_tiles) next_n = (pf_tile(G, tile + 1).ntok + 15) & ~15;
                 }
-                if (!pf_wait(bar(kAFull + (g & 1)), (g >> 1) & 1, abort_flag, G.err)) break;
-                if (!pf_wait(bar(kBFull + br.slot), br.phase, abort_flag, G.err)) break;
-                const int a = blk & 1;
-                if (q == 0 && blk >= 2 && !pf_wait(bar(kAccEmpty + a), ((blk >> 1) & 1) ^ 1u, abort_flag, G.err)) break;
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint64_t bdesc = bdesc0 + (uint64_t)(br.slot * (kPfBStage >> 4));
-                const uint32_t da = tmem + kPfACol + (uint32_t)(g & 1) * 32, dd = tmem + (uint32_t)a * kPfMaxN;
+                const int a = blk & (kPfAcc - 1), half = blk & 1;
+                const uint32_t bph = (uint32_t)(blk >> 1) & 1u, aph = (uint32_t)blk & 1u;
+                if (blk >= kPfAcc && !pf_wait(bar(kAccEmpty + a), ((uint32_t)(blk / kPfAcc) & 1u) ^ 1u, abort_flag, G.err))
+                    break;
+                const uint64_t bdesc = bdesc0 + (uint64_t)(half * 4 * (kPfBStage >> 4));
+                const uint32_t dd = tmem + (uint32_t)a * kPfMaxN;
+                bool ok = true;
 #pragma unroll
-                for (int j = 0; j < kPfStageK / 16; ++j) {
-                    const uint32_t accum = (q > 0 || j > 0) ? 1u : 0u;
-                    asm volatile(
-                        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %3, 0;\n\t"
-                        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, p;\n\t}\n" ::"r"(dd),
-                        "r"(da + 8u * j), "l"(bdesc + 2u * j), "r"(accum), "r"(idesc)
-                        : "memory");
+                for (int q = 0; q < 4; ++q) {
+                    if (!pf_wait(bar(kAFull + q), aph, abort_flag, G.err) ||
+                        !pf_wait(bar(kBFull + half * 4 + q), bph, abort_flag, G.err)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                    for (int j = 0; j < kPfStageK / 16; ++j) {
+                        const uint64_t db = bdesc + (uint64_t)(q * (kPfBStage >> 4) + 2 * j);
+                        const uint32_t da = tmem + kPfACol + (uint32_t)(q * 32 + 8 * j);
+                        if (q == 0 && j == 0)
+                            umma_ts<false>(dd, da, db, idesc);
+                        else
+                            umma_ts<true>(dd, da, db, idesc);
+                    }
+                    umma_commit(bar(kStageDone + half * 4 + q));
                 }
-                umma_commit(bar(kBEmpty + br.slot));
-                umma_commit(bar(kAEmpty + (g & 1)));
-                if (q == 3) umma_commit(bar(kAccFull + a));
-                br.next();
-                if (++q == 4) {
-                    q = 0;
-                    ++blk;
-                }
-                if (++s == S) {
-                    s = 0;
+                if (!ok) break;
+                umma_commit(bar(kAccFull + a));
+                if (++b == nb) {
+                    b = 0;
                     ++tile;
                 }
             }
         }
-    } else {
-        // ---------------- decoders / epilogue (warps 0-7) ----------------
-        const uint32_t lb = (uint32_t)lane * 4u;
-        const int dr = 32 * (warp & 3) + lane, dj = warp >> 2;  // row, 32-value chunk of the stage
-        const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
-        const __half2 off2 = __float2half2_rn(1152.0f);
-        const int ecol0 = 64 * dj;                              // epilogue columns [ecol0, ecol0 + 64)
+    } else if (warp >= kPfEpiWarp0) {
+        // ---------------- epilogue (4 warps, one per lane quarter) ----------------
+        // Block sums D are scaled and added into running tile sums R kept in tensor memory;
+        // the last block of a tile writes 0.125 * R out instead.
+        const int quarter = warp - kPfEpiWarp0, row = 32 * quarter + lane;
+        const uint32_t tlane = (uint32_t)(32 * quarter) << 16;
         const __half* dwring = reinterpret_cast<const __half*>(sm + PfSmem::dw);
-        int te_i = -1, te_first = 0, te_ntok = 0, te_mt = 0;
-        float acc[64];
-#pragma unroll
-        for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
-
-        auto uwait = [&](int b, uint32_t parity) {  // warp-uniform bounded wait
+        auto uwait = [&](int b, uint32_t parity) {
             return __all_sync(0xffffffffu, pf_wait(bar(b), parity, abort_flag, G.err));
         };
-        auto half_block = [&](uint32_t taddr, const float* dv, float dw, float* a32) {
-            uint32_t r[32];
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                  "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-                  "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
-                  "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
-                  "=r"(r[30]), "=r"(r[31])
-                : "r"(taddr));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-                const float4 d4 = reinterpret_cast<const float4*>(dv)[j4];
-                a32[4 * j4 + 0] = __fmaf_rn(__fmul_rn(dw, d4.x), __uint_as_float(r[4 * j4 + 0]), a32[4 * j4 + 0]);
-                a32[4 * j4 + 1] = __fmaf_rn(__fmul_rn(dw, d4.y), __uint_as_float(r[4 * j4 + 1]), a32[4 * j4 + 1]);
-                a32[4 * j4 + 2] = __fmaf_rn(__fmul_rn(dw, d4.z), __uint_as_float(r[4 * j4 + 2]), a32[4 * j4 + 2]);
-                a32[4 * j4 + 3] = __fmaf_rn(__fmul_rn(dw, d4.w), __uint_as_float(r[4 * j4 + 3]), a32[4 * j4 + 3]);
+        Ring<kPfDwRing> dr;
+        int tile = 0, b = 0, first = 0, ntok = 0, mt = 0;
+        for (int e = 0; e < total / 4; ++e) {
+            if (b == 0) {
+                const PfTile t = pf_tile(G, tile);
+                first = t.first;
+                ntok = t.ntok;
+                mt = t.mt;
+                if (!uwait(kDxsFull + (tile & 1), (tile >> 1) & 1)) break;
             }
-        };
-        auto epilogue = [&](int e) -> bool {
-            const int i = e / nb, b = e - i * nb, a = e & 1;
-            if (i != te_i) {
-                te_i = i;
-                const PfTile t = pf_tile(G, i);
-                te_first = t.first;
-                te_ntok = t.ntok;
-                te_mt = t.mt;
-            }
-            if (!uwait(kDwFull + (e & 3), (e >> 2) & 1)) return false;
-            if (b == 0 && !uwait(kDxsFull + (i & 1), (i >> 1) & 1)) return false;
-            if (!uwait(kAccFull + a, (e >> 1) & 1)) return false;
-            const float dw = __half2float(dwring[(e & 3) * 128 + dr]);
+            if (!uwait(kDwFull + dr.slot, dr.phase)) break;
+            if (!uwait(kAccFull + (e & (kPfAcc - 1)), (uint32_t)(e / kPfAcc) & 1u)) break;
+            const float dw = __half2float(dwring[dr.slot * 128 + row]);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");  // the previous block's R stores
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const float* dv = reinterpret_cast<const float*>(sm + PfSmem::dxs) + ((i & 1) * kPfMaxNb + b) * kPfMaxN + ecol0;
-            const uint32_t taddr = tmem + tlane + (uint32_t)(a * kPfMaxN + ecol0);
-            if (ecol0 < te_ntok) half_block(taddr, dv, dw, acc);
-            if (ecol0 + 32 < te_ntok) half_block(taddr + 32, dv + 32, dw, acc + 32);
+            const float* dxs = reinterpret_cast<const float*>(sm + PfSmem::dxs) + ((tile & 1) * kPfMaxNb + b) * kPfMaxN;
+            const bool last = b == nb - 1;
+            for (int c0 = 0; c0 < ntok; c0 += 16) {
+                uint32_t d[16], r[16];
+                tmem_ld16(tmem + tlane + (uint32_t)((e & (kPfAcc - 1)) * kPfMaxN + c0), d);
+                if (b > 0) tmem_ld16(tmem + tlane + kPfRCol + (uint32_t)c0, r);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int j4 = 0; j4 < 4; ++j4) {
+                    const float4 d4 = reinterpret_cast<const float4*>(dxs + c0)[j4];
+                    const float sc[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int j = 4 * j4 + u;
+                        const float prev = b > 0 ? __uint_as_float(r[j]) : 0.0f;
+                        r[j] = __float_as_uint(__fmaf_rn(__fmul_rn(dw, sc[u]), __uint_as_float(d[j]), prev));
+                    }
+                }
+                if (!last) {
+                    tmem_st16(tmem + tlane + kPfRCol + (uint32_t)c0, r);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = c0 + j;
+                        if (n < ntok) {
+                            const float v = __fmul_rn(0.125f, __uint_as_float(r[j]));
+                            if (G.role == 0)
+                                G.out[((size_t)(first + n) * 2 + (row >> 6)) * G.nrows + mt * 64 + (row & 63)] = v;
+                            else
+                                G.out[(size_t)G.list[first + n] * G.nrows + mt * 128 + row] = v;
+                        }
+                    }
+                }
+            }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(bar(kAccEmpty + a));
-                mbar_arrive(bar(kDwEmpty + (e & 3)));
+                mbar_arrive(bar(kAccEmpty + (e & (kPfAcc - 1))));
+                mbar_arrive(bar(kDwEmpty + dr.slot));
+                if (last) mbar_arrive(bar(kDxsEmpty + (tile & 1)));
             }
-            if (b == nb - 1) {  // the tile is complete: store its rows, start the next one from zero
-#pragma unroll
-                for (int j = 0; j < 64; ++j) {
-                    const int n = ecol0 + j;
-                    if (n < te_ntok) {
-                        const float v = __fmul_rn(0.125f, acc[j]);
-                        if (G.role == 0)
-                            G.out[((size_t)(te_first + n) * 2 + (dr >> 6)) * G.nrows + te_mt * 64 + (dr & 63)] = v;
-                        else
-                            G.out[(size_t)G.list[te_first + n] * G.nrows + te_mt * 128 + dr] = v;
-                    }
-                    acc[j] = 0.0f;
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(kDxsEmpty + (i & 1)));
+            dr.next();
+            if (++b == nb) {
+                b = 0;
+                ++tile;
             }
-            return true;
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    } else {
+        // ---------------- decoders (warps 0-15): 16 weights of one row per stage ----------------
+        // The tensor-memory store of stage g overlaps the decode of stage g + 1.
+        const uint32_t lb = (uint32_t)lane * 4u;
+        const int dr = 32 * (warp & 3) + lane, dj = warp >> 2;  // row, 16-value part of the stage
+        const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
+        const __half2 off2 = __float2half2_rn(1152.0f);
+        auto uwait = [&](int b, uint32_t parity) {
+            return __all_sync(0xffffffffu, pf_wait(bar(b), parity, abort_flag, G.err));
         };
-
         Ring<kPfRA> rr;
-        bool live = true;
-        for (int g = 0; g < total && live; ++g) {
-            if (!uwait(kRawFull + rr.slot, rr.phase)) break;
-            const uint2 cw = *reinterpret_cast<const uint2*>(sm + PfSmem::raw + rr.slot * kPfRawStage + dr * 16 + dj * 8);
+        Ring<kPfRB> sd;  // stage g - 3 in the stage-done ring
+        uint32_t v[8];
+        auto decode = [&]() -> bool {  // the next stage's raw piece -> v
+            if (!uwait(kRawFull + rr.slot, rr.phase)) return false;
+            const uint2 cw =
+                *reinterpret_cast<const uint2*>(sm + PfSmem::raw + rr.slot * kPfRawStage + dr * 16 + (dj >> 1) * 8);
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kRawEmpty + rr.slot));
             rr.next();
@@ -478,29 +531,42 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
             const uint32_t sc = (((sw & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27;  // 2s + 1
             const __half2 s2 = __float2half2_rn((float)sc);
             const __half2 noff = __hneg2(__hmul2(off2, s2));
-            uint32_t v[16];
 #pragma unroll
-            for (int grp = 0; grp < 4; ++grp) {
-                const uint32_t selj = 0x5504u | ((uint32_t)grp << 4);
-                const uint32_t sel = tab32(kRowTabXXS + prmt2(gw, lb, selj)) | tab32(kRowTabXXS + 128 + prmt2(sw, lb, selj));
-                biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel), s2, noff, v[4 * grp], v[4 * grp + 1]);
-                biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel >> 16), s2, noff, v[4 * grp + 2], v[4 * grp + 3]);
+            for (int jj = 0; jj < 2; ++jj) {
+                const uint32_t grp = 2 * (dj & 1) + jj;
+                const uint32_t selj = 0x5504u | (grp << 4);
+                const uint32_t sel =
+                    tab32(kRowTabXXS + prmt2(gw, lb, selj)) | tab32(kRowTabXXS + 128 + prmt2(sw, lb, selj));
+                biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel), s2, noff, v[4 * jj], v[4 * jj + 1]);
+                biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel >> 16), s2, noff, v[4 * jj + 2], v[4 * jj + 3]);
             }
-            // A buffer g & 1 was last read by the MMAs of stage g - 2
-            if (g >= 2 && !uwait(kAEmpty + (g & 1), ((g >> 1) & 1) ^ 1u)) break;
-            asm volatile(
-                "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-                "%14, %15, %16};" ::"r"(tmem + tlane + kPfACol + (uint32_t)(g & 1) * 32 + (uint32_t)dj * 16),
-                "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-                "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-                : "memory");
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kAFull + (g & 1)));
-            if ((g & 3) == 1 && g >= 4) live = epilogue((g >> 2) - 1);
+            return true;
+        };
+        auto store = [&](int g) {
+            asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(
+                             tmem + tlane + kPfACol + (uint32_t)(g & (kPfABuf - 1)) * 32 + (uint32_t)dj * 8),
+                         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                         : "memory");
+        };
+        if (total > 0 && decode()) {
+            store(0);
+            for (int g = 0; g < total; ++g) {
+                const bool more = g + 1 < total;
+                if (more && !decode()) break;
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(kAFull + (g & (kPfABuf - 1))));
+                if (!more) break;
+                // A buffer (g + 1) % kPfABuf was last read by the MMAs of stage g + 1 - kPfABuf
+                if (g + 1 >= kPfABuf) {
+                    if (!uwait(kStageDone + sd.slot, sd.phase)) break;
+                    sd.next();
+                }
+                store(g + 1);
+            }
         }
-        if (live && !*abort_flag && total > 0) epilogue(total / 4 - 1);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
 
     __syncthreads();
