@@ -19,24 +19,24 @@
 // writes expert rows by slot for the combine.
 //
 // GEMM kernel: one CTA per SM, persistent over tiles (expert, 128 weight rows, up to 64
-// list entries), warp-specialised around one pipeline of 64-value K stages that runs
-// across tiles, synchronised by mbarriers only:
-//  * weight warp: bulk copies (cp.async.bulk) of the packed weight pieces of a stage
-//    (16 B per row, 2 KB) and of the rows' block scales into rings kPfRA stages deep;
-//  * B warp: the B operand of each stage by TMA (2-D tensor map over the list-order
-//    activations, 128-byte swizzle, box height = the tile's entries rounded up to 16) into
-//    a ring kPfRB stages deep, and each tile's activation scales;
-//  * MMA warp: per stage, four tcgen05.mma (A from tensor memory, B from shared memory)
-//    into one of kPfAcc block accumulators, and one commit that frees the stage's operands
-//    (one loop iteration per block, ring slots and accumulate flags known at compile time);
+// list entries), warp-specialised around one pipeline of 256-value K blocks (4 stages of 64)
+// that runs across tiles; roles hand blocks to each other through mbarriers, one wait and
+// one arrival per block:
+//  * weight warp: bulk copies (cp.async.bulk) of the packed weight pieces of a block
+//    (16 B per row and stage, 8 KB) and of the rows' block scales, two blocks ahead;
+//  * B warp: the B operand of a block by TMA (2-D tensor map over the list-order
+//    activations, 128-byte swizzle, box height = the tile's entries rounded up to 16), two
+//    blocks deep, and each tile's activation scales;
+//  * MMA warp: 16 tcgen05.mma per block (A from tensor memory, B from shared memory) into
+//    one of kPfAcc block accumulators, then one commit that frees the block's operands and
+//    one that hands the accumulator to the epilogue;
 //  * 16 decoder warps: each thread turns 16 weights of one row per stage into exact fp16
 //    integers and stores them to the A operand in tensor memory (tcgen05.st, row m in lane
-//    m, values k, k+1 in one column; kPfABuf buffers), the store of one stage overlapping
-//    the decode of the next;
+//    m, values k, k+1 in one column; two blocks of buffers);
 //  * 4 epilogue warps (one per tensor-memory lane quarter): per block, D * d_w * d_x added
 //    into running tile sums that also live in tensor memory; the tile's last block writes
 //    the rows out.
-// Control loops keep ring positions as counters (no divisions in the per-stage path).
+// Control loops keep ring positions as counters (no divisions in the per-block path).
 // Every wait is bounded: on time-out the CTA flags *err and an abort flag that ends every
 // loop, lets copies in flight land, waits (bounded) for its MMAs and frees its tensor memory.
 #include <cuda.h>
@@ -51,25 +51,24 @@ namespace clb {
 
 namespace {
 
-constexpr int kPfDecWarps = 16;               // warp w: TMEM lane quarter w & 3, 16-value part w >> 2 of the stage
+constexpr int kPfDecWarps = 16;               // warp w: TMEM lane quarter w & 3, 16-value part w >> 2 of a stage
 constexpr int kPfEpiWarps = 4;                // warp kPfDecWarps + r: lane quarter r
 constexpr int kPfEpiWarp0 = kPfDecWarps;
 constexpr int kPfProducerWarp = kPfDecWarps + kPfEpiWarps, kPfMmaWarp = kPfProducerWarp + 1, kPfBWarp = kPfProducerWarp + 2;
 constexpr int kPfThreads = 32 * (kPfDecWarps + kPfEpiWarps + 3);
 constexpr int kPfMaxN = 64;                   // list entries per tile (MMA N <= 64)
-constexpr int kPfStageK = 64;                 // K values per stage (4 MMAs of K = 16)
-constexpr int kPfRA = 8;                      // weight-piece ring (stages)
-constexpr int kPfRB = 8;                      // B operand ring (stages; two blocks)
+constexpr int kPfStageK = 64;                 // K values per stage (4 MMAs of K = 16); 4 stages per block
 constexpr int kPfRawStage = 128 * 16;         // one 16-byte piece per weight row
+constexpr int kPfRawBlock = 4 * kPfRawStage;  // 8 KB per block
 constexpr int kPfBStage = kPfMaxN * 128;      // 64 rows x 64 fp16, 128-byte swizzled
+constexpr int kPfBBlock = 4 * kPfBStage;
 constexpr int kPfMaxNb = 32;                  // K <= 8192
-constexpr int kPfAcc = 4;                     // block accumulators (64 columns each, from column 0)
-constexpr int kPfABuf = 4;                    // A operand buffers (32 columns each)
+constexpr int kPfAcc = 3;                     // block accumulators (64 columns each, from column 0)
 constexpr int kPfDwRing = 8;                  // row-scale ring (blocks)
 constexpr int kPfTmemCols = 512;
-constexpr uint32_t kPfRCol = kPfAcc * kPfMaxN;          // running tile sums
-constexpr uint32_t kPfACol = kPfRCol + kPfMaxN;         // A buffers
-static_assert(kPfACol + 32 * kPfABuf <= kPfTmemCols, "tensor memory budget");
+constexpr uint32_t kPfRCol = kPfAcc * kPfMaxN;          // running tile sums (64 columns)
+constexpr uint32_t kPfACol = 256;                       // A operand: 2 blocks x 4 stages x 32 columns
+static_assert(kPfRCol + kPfMaxN <= kPfACol && kPfACol + 8 * 32 <= kPfTmemCols, "tensor memory budget");
 constexpr uint32_t kPfSpin = 1u << 22;
 constexpr int kErrPrefillWait = 3;
 
@@ -77,24 +76,24 @@ constexpr int kErrPrefillWait = 3;
 constexpr uint32_t kPos2b = 0x00AB9988u;
 constexpr uint32_t kNeg2b = 0x00556778u;
 
-// mbarriers
+// mbarriers; operand rings hold two blocks, each synchronised once per block
 enum : int {
-    kRawFull = 0,
-    kRawEmpty = kRawFull + kPfRA,
-    kDwFull = kRawEmpty + kPfRA,
-    kDwEmpty = kDwFull + kPfDwRing,
-    kBFull = kDwEmpty + kPfDwRing,
-    kStageDone = kBFull + kPfRB,  // MMAs of the stage complete: its B slot and A buffer are free
-    kAFull = kStageDone + kPfRB,
-    kAccFull = kAFull + kPfABuf,
-    kAccEmpty = kAccFull + kPfAcc,
-    kDxsFull = kAccEmpty + kPfAcc,
-    kDxsEmpty = kDxsFull + 2,
+    kRawFull = 0,                      // [2] weight pieces of a block landed
+    kRawEmpty = kRawFull + 2,          // [2] decoded
+    kDwFull = kRawEmpty + 2,           // [kPfDwRing] row scales of a block landed
+    kDwEmpty = kDwFull + kPfDwRing,    // [kPfDwRing] read by the epilogue
+    kBFull = kDwEmpty + kPfDwRing,     // [2] B operand of a block landed
+    kAFull = kBFull + 2,               // [2] A operand of a block stored
+    kBlockDone = kAFull + 2,           // [2] MMAs of a block complete: its A and B buffers are free
+    kAccFull = kBlockDone + 2,         // [kPfAcc]
+    kAccEmpty = kAccFull + kPfAcc,     // [kPfAcc]
+    kDxsFull = kAccEmpty + kPfAcc,     // [2] a tile's activation scales landed
+    kDxsEmpty = kDxsFull + 2,          // [2]
     kDrain = kDxsEmpty + 2,
     kNumBars = kDrain + 1
 };
 __host__ __device__ constexpr uint32_t pf_bar_count(int i) {
-    return ((i >= kRawEmpty && i < kRawEmpty + kPfRA) || (i >= kAFull && i < kAFull + kPfABuf)) ? kPfDecWarps
+    return ((i >= kRawEmpty && i < kRawEmpty + 2) || (i >= kAFull && i < kAFull + 2)) ? kPfDecWarps
            : ((i >= kDwEmpty && i < kDwEmpty + kPfDwRing) || (i >= kAccEmpty && i < kAccEmpty + kPfAcc) ||
               (i >= kDxsEmpty && i < kDxsEmpty + 2))
                ? kPfEpiWarps
@@ -104,8 +103,8 @@ __host__ __device__ constexpr uint32_t pf_bar_count(int i) {
 struct PfSmem {
     // [0, 64K) IQ2_XXS tables; the B ring starts at the first 1024-byte boundary after them
     static constexpr uint32_t braw = 64 * 1024;                            // + alignment pad
-    static constexpr uint32_t raw = braw + 1024 + kPfRB * kPfBStage;       // weight pieces ring
-    static constexpr uint32_t dw = raw + kPfRA * kPfRawStage;              // [kPfDwRing][128] fp16 row scales
+    static constexpr uint32_t raw = braw + 1024 + 2 * kPfBBlock;           // weight pieces, 2 blocks
+    static constexpr uint32_t dw = raw + 2 * kPfRawBlock;                  // [kPfDwRing][128] fp16 row scales
     static constexpr uint32_t dxs = dw + kPfDwRing * 256;                  // [2][kPfMaxNb][kPfMaxN] floats
     static constexpr uint32_t bars = dxs + 2 * kPfMaxNb * kPfMaxN * 4;
     static constexpr uint32_t tslot = bars + kNumBars * 8;
@@ -286,18 +285,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + PfSmem::tslot);
 
+    const int nblk = total / 4;
     if (warp == kPfProducerWarp) {
-        // ---------------- weight pieces and row scales, kPfRA stages ahead ----------------
+        // ---------------- weight pieces and row scales, two blocks ahead ----------------
         if (lane == 0 && total > 0) {
-            Ring<kPfRA> rr;
+            Ring<2> rr;
             Ring<kPfDwRing> dr;
-            int tile = 0, s = 0;
+            int tile = 0, b = 0;
             bool ok = false;
             const uint8_t *pa0 = nullptr, *pa1 = nullptr;
             const uint16_t *pd0 = nullptr, *pd1 = nullptr;
             size_t plane = 0, dstride = 0;
-            for (int g = 0; g < total; ++g) {
-                if (s == 0) {  // tile setup
+            for (int blk = 0; blk < nblk; ++blk) {
+                if (b == 0) {  // tile setup
                     const PfTile t = pf_tile(G, tile);
                     const ExpertDesc& ex = G.desc[t.e];
                     const PackedMat& m0 = G.role == 0 ? ex.gate : ex.down;
@@ -314,52 +314,53 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
                     pd1 = m1.d + row0;
                 }
                 if (rr.round > 0 && !pf_wait(bar(kRawEmpty + rr.slot), rr.phase ^ 1u, abort_flag, G.err)) break;
-                const uint32_t full = bar(kRawFull + rr.slot), dst = sraw + (uint32_t)rr.slot * kPfRawStage;
+                const uint32_t full = bar(kRawFull + rr.slot), dst = sraw + (uint32_t)rr.slot * kPfRawBlock;
                 if (!ok) {
                     mbar_arrive(full);
                 } else {
-                    mbar_expect_tx(full, kPfRawStage);
-                    if (G.role == 0) {
-                        bulk_g2s(dst, pa0, kPfRawStage / 2, full);
-                        bulk_g2s(dst + kPfRawStage / 2, pa1, kPfRawStage / 2, full);
-                    } else {
-                        bulk_g2s(dst, pa0, kPfRawStage, full);
-                    }
-                }
-                pa0 += plane;
-                pa1 += plane;
-                rr.next();
-                if ((s & 3) == 0) {
-                    if (dr.round > 0 && !pf_wait(bar(kDwEmpty + dr.slot), dr.phase ^ 1u, abort_flag, G.err)) break;
-                    const uint32_t dfull = bar(kDwFull + dr.slot), ddst = sdw + (uint32_t)dr.slot * 256;
-                    if (!ok) {
-                        mbar_arrive(dfull);
-                    } else {
-                        mbar_expect_tx(dfull, 256);
+                    mbar_expect_tx(full, kPfRawBlock);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
                         if (G.role == 0) {
-                            bulk_g2s(ddst, pd0, 128, dfull);
-                            bulk_g2s(ddst + 128, pd1, 128, dfull);
+                            bulk_g2s(dst + q * kPfRawStage, pa0 + q * plane, kPfRawStage / 2, full);
+                            bulk_g2s(dst + q * kPfRawStage + kPfRawStage / 2, pa1 + q * plane, kPfRawStage / 2, full);
                         } else {
-                            bulk_g2s(ddst, pd0, 256, dfull);
+                            bulk_g2s(dst + q * kPfRawStage, pa0 + q * plane, kPfRawStage, full);
                         }
                     }
-                    pd0 += dstride;
-                    pd1 += dstride;
-                    dr.next();
                 }
-                if (++s == S) {
-                    s = 0;
+                pa0 += 4 * plane;
+                pa1 += 4 * plane;
+                rr.next();
+                if (dr.round > 0 && !pf_wait(bar(kDwEmpty + dr.slot), dr.phase ^ 1u, abort_flag, G.err)) break;
+                const uint32_t dfull = bar(kDwFull + dr.slot), ddst = sdw + (uint32_t)dr.slot * 256;
+                if (!ok) {
+                    mbar_arrive(dfull);
+                } else {
+                    mbar_expect_tx(dfull, 256);
+                    if (G.role == 0) {
+                        bulk_g2s(ddst, pd0, 128, dfull);
+                        bulk_g2s(ddst + 128, pd1, 128, dfull);
+                    } else {
+                        bulk_g2s(ddst, pd0, 256, dfull);
+                    }
+                }
+                pd0 += dstride;
+                pd1 += dstride;
+                dr.next();
+                if (++b == nb) {
+                    b = 0;
                     ++tile;
                 }
             }
         }
     } else if (warp == kPfBWarp) {
-        // ---------------- B operand (TMA) and the tiles' activation scales, kPfRB stages ahead ----------------
+        // ---------------- B operand (TMA, 4 stages per block) and the tiles' activation scales ----------------
         if (lane == 0 && total > 0) {
-            Ring<kPfRB> br;
-            int tile = 0, s = 0, first = 0, n = 16, x = 0;
-            for (int g = 0; g < total; ++g) {
-                if (s == 0) {
+            Ring<2> br;
+            int tile = 0, b = 0, first = 0, n = 16, x = 0;
+            for (int blk = 0; blk < nblk; ++blk) {
+                if (b == 0) {
                     const PfTile t = pf_tile(G, tile);
                     first = t.first;
                     n = (t.ntok + 15) & ~15;
@@ -372,26 +373,29 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
                         bulk_g2s(sdxs + (uint32_t)(xs * kPfMaxNb + bb) * (kPfMaxN * 4), G.actd + (size_t)bb * G.P + first,
                                  (uint32_t)n * 4, dfull);
                 }
-                if (br.round > 0 && !pf_wait(bar(kStageDone + br.slot), br.phase ^ 1u, abort_flag, G.err)) break;
+                if (br.round > 0 && !pf_wait(bar(kBlockDone + br.slot), br.phase ^ 1u, abort_flag, G.err)) break;
                 const uint32_t full = bar(kBFull + br.slot);
-                mbar_expect_tx(full, (uint32_t)n * 128);
-                tma_2d(sb0 + (uint32_t)br.slot * kPfBStage, &G.bmaps[(n >> 4) - 1], x, first, full);
-                x += kPfStageK;
+                mbar_expect_tx(full, (uint32_t)n * 128 * 4);
+                const CUtensorMap* map = &G.bmaps[(n >> 4) - 1];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    tma_2d(sb0 + (uint32_t)(br.slot * 4 + q) * kPfBStage, map, x + q * kPfStageK, first, full);
+                x += 4 * kPfStageK;
                 br.next();
-                if (++s == S) {
-                    s = 0;
+                if (++b == nb) {
+                    b = 0;
                     ++tile;
                 }
             }
         }
     } else if (warp == kPfMmaWarp) {
-        // ---------------- MMAs: four per stage into one of two block accumulators ----------------
-        // One loop iteration per block (4 stages): B slots 4 (blk & 1) + q, A buffer q.
+        // ---------------- MMAs: 16 per block (4 stages x 4) into one of kPfAcc accumulators ----------------
         if (lane == 0 && total > 0) {
             // B descriptors: K-major, 128-byte swizzle, 8-row groups 1024 B apart
             const uint64_t bdesc0 = ((uint64_t)1 << 16) | ((uint64_t)64 << 32) | ((uint64_t)1 << 46) |
                                     ((uint64_t)2 << 61) | (uint64_t)((sb0 >> 4) & 0x3FFFu);
-            const int nblk = total / 4;
+            Ring<2> ab;
+            Ring<kPfAcc> acc;
             int tile = 0, b = 0;
             uint32_t idesc = 0;
             int next_n = (pf_tile(G, 0).ntok + 15) & ~15;
@@ -400,34 +404,28 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
                     idesc = (1u << 4) | ((uint32_t)(next_n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
                     if (tile + 1 < my_tiles) next_n = (pf_tile(G, tile + 1).ntok + 15) & ~15;
                 }
-                const int a = blk & (kPfAcc - 1), half = blk & 1;
-                const uint32_t bph = (uint32_t)(blk >> 1) & 1u, aph = (uint32_t)blk & 1u;
-                if (blk >= kPfAcc && !pf_wait(bar(kAccEmpty + a), ((uint32_t)(blk / kPfAcc) & 1u) ^ 1u, abort_flag, G.err))
-                    break;
-                const uint64_t bdesc = bdesc0 + (uint64_t)(half * 4 * (kPfBStage >> 4));
-                const uint32_t dd = tmem + (uint32_t)a * kPfMaxN;
-                bool ok = true;
+                if (!pf_wait(bar(kAFull + ab.slot), ab.phase, abort_flag, G.err)) break;
+                if (!pf_wait(bar(kBFull + ab.slot), ab.phase, abort_flag, G.err)) break;
+                if (acc.round > 0 && !pf_wait(bar(kAccEmpty + acc.slot), acc.phase ^ 1u, abort_flag, G.err)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint64_t bdesc = bdesc0 + (uint64_t)(ab.slot * 4 * (kPfBStage >> 4));
+                const uint32_t dd = tmem + (uint32_t)acc.slot * kPfMaxN;
+                const uint32_t da = tmem + kPfACol + (uint32_t)ab.slot * 128;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    if (!pf_wait(bar(kAFull + q), aph, abort_flag, G.err) ||
-                        !pf_wait(bar(kBFull + half * 4 + q), bph, abort_flag, G.err)) {
-                        ok = false;
-                        break;
-                    }
-                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
                     for (int j = 0; j < kPfStageK / 16; ++j) {
                         const uint64_t db = bdesc + (uint64_t)(q * (kPfBStage >> 4) + 2 * j);
-                        const uint32_t da = tmem + kPfACol + (uint32_t)(q * 32 + 8 * j);
                         if (q == 0 && j == 0)
                             umma_ts<false>(dd, da, db, idesc);
                         else
-                            umma_ts<true>(dd, da, db, idesc);
+                            umma_ts<true>(dd, da + (uint32_t)(q * 32 + 8 * j), db, idesc);
                     }
-                    umma_commit(bar(kStageDone + half * 4 + q));
                 }
-                if (!ok) break;
-                umma_commit(bar(kAccFull + a));
+                umma_commit(bar(kBlockDone + ab.slot));
+                umma_commit(bar(kAccFull + acc.slot));
+                ab.next();
+                acc.next();
                 if (++b == nb) {
                     b = 0;
                     ++tile;
@@ -445,8 +443,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
             return __all_sync(0xffffffffu, pf_wait(bar(b), parity, abort_flag, G.err));
         };
         Ring<kPfDwRing> dr;
+        Ring<kPfAcc> acc;
         int tile = 0, b = 0, first = 0, ntok = 0, mt = 0;
-        for (int e = 0; e < total / 4; ++e) {
+        for (int e = 0; e < nblk; ++e) {
             if (b == 0) {
                 const PfTile t = pf_tile(G, tile);
                 first = t.first;
@@ -455,7 +454,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
                 if (!uwait(kDxsFull + (tile & 1), (tile >> 1) & 1)) break;
             }
             if (!uwait(kDwFull + dr.slot, dr.phase)) break;
-            if (!uwait(kAccFull + (e & (kPfAcc - 1)), (uint32_t)(e / kPfAcc) & 1u)) break;
+            if (!uwait(kAccFull + acc.slot, acc.phase)) break;
             const float dw = __half2float(dwring[dr.slot * 128 + row]);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");  // the previous block's R stores
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -463,7 +462,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
             const bool last = b == nb - 1;
             for (int c0 = 0; c0 < ntok; c0 += 16) {
                 uint32_t d[16], r[16];
-                tmem_ld16(tmem + tlane + (uint32_t)((e & (kPfAcc - 1)) * kPfMaxN + c0), d);
+                tmem_ld16(tmem + tlane + (uint32_t)(acc.slot * kPfMaxN + c0), d);
                 if (b > 0) tmem_ld16(tmem + tlane + kPfRCol + (uint32_t)c0, r);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
@@ -496,11 +495,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(bar(kAccEmpty + (e & (kPfAcc - 1))));
+                mbar_arrive(bar(kAccEmpty + acc.slot));
                 mbar_arrive(bar(kDwEmpty + dr.slot));
                 if (last) mbar_arrive(bar(kDxsEmpty + (tile & 1)));
             }
             dr.next();
+            acc.next();
             if (++b == nb) {
                 b = 0;
                 ++tile;
@@ -508,65 +508,52 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     } else {
-        // ---------------- decoders (warps 0-15): 16 weights of one row per stage ----------------
-        // The tensor-memory store of stage g overlaps the decode of stage g + 1.
+        // ---------------- decoders (warps 0-15): 16 weights of one row per stage, 4 stages per block ----------------
         const uint32_t lb = (uint32_t)lane * 4u;
-        const int dr = 32 * (warp & 3) + lane, dj = warp >> 2;  // row, 16-value part of the stage
+        const int dr = 32 * (warp & 3) + lane, dj = warp >> 2;  // row, 16-value part of a stage
         const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
         const __half2 off2 = __float2half2_rn(1152.0f);
         auto uwait = [&](int b, uint32_t parity) {
             return __all_sync(0xffffffffu, pf_wait(bar(b), parity, abort_flag, G.err));
         };
-        Ring<kPfRA> rr;
-        Ring<kPfRB> sd;  // stage g - 3 in the stage-done ring
-        uint32_t v[8];
-        auto decode = [&]() -> bool {  // the next stage's raw piece -> v
-            if (!uwait(kRawFull + rr.slot, rr.phase)) return false;
-            const uint2 cw =
-                *reinterpret_cast<const uint2*>(sm + PfSmem::raw + rr.slot * kPfRawStage + dr * 16 + (dj >> 1) * 8);
+        Ring<2> rr;
+        for (int blk = 0; blk < nblk; ++blk) {
+            if (!uwait(kRawFull + rr.slot, rr.phase)) break;
+            // this block's A buffers were last read by the MMAs of block blk - 2
+            if (rr.round > 0 && !uwait(kBlockDone + rr.slot, rr.phase ^ 1u)) break;
+            const uint8_t* raw = sm + PfSmem::raw + rr.slot * kPfRawBlock + dr * 16 + (dj >> 1) * 8;
+            uint2 cw[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) cw[q] = *reinterpret_cast<const uint2*>(raw + q * kPfRawStage);
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kRawEmpty + rr.slot));
-            rr.next();
-            const uint32_t gw = cw.x, sw = cw.y;
-            const uint32_t sc = (((sw & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27;  // 2s + 1
-            const __half2 s2 = __float2half2_rn((float)sc);
-            const __half2 noff = __hneg2(__hmul2(off2, s2));
 #pragma unroll
-            for (int jj = 0; jj < 2; ++jj) {
-                const uint32_t grp = 2 * (dj & 1) + jj;
-                const uint32_t selj = 0x5504u | (grp << 4);
-                const uint32_t sel =
-                    tab32(kRowTabXXS + prmt2(gw, lb, selj)) | tab32(kRowTabXXS + 128 + prmt2(sw, lb, selj));
-                biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel), s2, noff, v[4 * jj], v[4 * jj + 1]);
-                biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel >> 16), s2, noff, v[4 * jj + 2], v[4 * jj + 3]);
-            }
-            return true;
-        };
-        auto store = [&](int g) {
-            asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(
-                             tmem + tlane + kPfACol + (uint32_t)(g & (kPfABuf - 1)) * 32 + (uint32_t)dj * 8),
-                         "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-                         : "memory");
-        };
-        if (total > 0 && decode()) {
-            store(0);
-            for (int g = 0; g < total; ++g) {
-                const bool more = g + 1 < total;
-                if (more && !decode()) break;
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(kAFull + (g & (kPfABuf - 1))));
-                if (!more) break;
-                // A buffer (g + 1) % kPfABuf was last read by the MMAs of stage g + 1 - kPfABuf
-                if (g + 1 >= kPfABuf) {
-                    if (!uwait(kStageDone + sd.slot, sd.phase)) break;
-                    sd.next();
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t gw = cw[q].x, sw = cw[q].y;
+                const uint32_t sc = (((sw & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27;  // 2s + 1
+                const __half2 s2 = __float2half2_rn((float)sc);
+                const __half2 noff = __hneg2(__hmul2(off2, s2));
+                uint32_t v[8];
+#pragma unroll
+                for (int jj = 0; jj < 2; ++jj) {
+                    const uint32_t grp = 2 * (dj & 1) + jj;
+                    const uint32_t selj = 0x5504u | (grp << 4);
+                    const uint32_t sel =
+                        tab32(kRowTabXXS + prmt2(gw, lb, selj)) | tab32(kRowTabXXS + 128 + prmt2(sw, lb, selj));
+                    biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel), s2, noff, v[4 * jj], v[4 * jj + 1]);
+                    biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel >> 16), s2, noff, v[4 * jj + 2], v[4 * jj + 3]);
                 }
-                store(g + 1);
+                asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(
+                                 tmem + tlane + kPfACol + (uint32_t)(rr.slot * 4 + q) * 32 + (uint32_t)dj * 8),
+                             "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                             : "memory");
             }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kAFull + rr.slot));
+            rr.next();
         }
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     }
 
     __syncthreads();
