@@ -30,12 +30,13 @@
 //  * MMA warp: 16 tcgen05.mma per block (A from tensor memory, B from shared memory) into
 //    one of kPfAcc block accumulators, then one commit that frees the block's operands and
 //    one that hands the accumulator to the epilogue;
-//  * 16 decoder warps: each thread turns 16 weights of one row per stage into exact fp16
-//    integers and stores them to the A operand in tensor memory (tcgen05.st, row m in lane
-//    m, values k, k+1 in one column; two blocks of buffers);
-//  * 4 epilogue warps (one per tensor-memory lane quarter): per block, D * d_w * d_x added
-//    into running tile sums that also live in tensor memory; the tile's last block writes
-//    the rows out.
+//  * 8 decoder warps: each thread turns one 32-weight chunk of one row per stage into exact
+//    fp16 integers and stores them to the A operand in tensor memory (tcgen05.st, row m in
+//    lane m, values k, k+1 in one column; two blocks of buffers), two 32-column stores per
+//    block;
+//  * 8 epilogue warps (tensor-memory lane quarter x 32 columns): per block, D * d_w * d_x
+//    added into running tile sums that also live in tensor memory; the tile's last block
+//    writes the rows out.
 // Control loops keep ring positions as counters (no divisions in the per-block path).
 // Every wait is bounded: on time-out the CTA flags *err and an abort flag that ends every
 // loop, lets copies in flight land, waits (bounded) for its MMAs and frees its tensor memory.
@@ -51,8 +52,8 @@ namespace clb {
 
 namespace {
 
-constexpr int kPfDecWarps = 16;               // warp w: TMEM lane quarter w & 3, 16-value part w >> 2 of a stage
-constexpr int kPfEpiWarps = 4;                // warp kPfDecWarps + r: lane quarter r
+constexpr int kPfDecWarps = 8;                // warp w: TMEM lane quarter w & 3, 32-value chunk w >> 2 of a stage
+constexpr int kPfEpiWarps = 8;                // warp kPfDecWarps + w: lane quarter w & 3, 32 columns from 32 (w >> 2)
 constexpr int kPfEpiWarp0 = kPfDecWarps;
 constexpr int kPfProducerWarp = kPfDecWarps + kPfEpiWarps, kPfMmaWarp = kPfProducerWarp + 1, kPfBWarp = kPfProducerWarp + 2;
 constexpr int kPfThreads = 32 * (kPfDecWarps + kPfEpiWarps + 3);
@@ -67,7 +68,9 @@ constexpr int kPfAcc = 3;                     // block accumulators (64 columns 
 constexpr int kPfDwRing = 8;                  // row-scale ring (blocks)
 constexpr int kPfTmemCols = 512;
 constexpr uint32_t kPfRCol = kPfAcc * kPfMaxN;          // running tile sums (64 columns)
-constexpr uint32_t kPfACol = 256;                       // A operand: 2 blocks x 4 stages x 32 columns
+constexpr uint32_t kPfACol = 256;                       // A operand: 2 blocks x 128 columns
+// A operand of a block: the 16-value slice j (0-3) of stage q (0-3) sits at columns 32 j + 8 q, so
+// the four stages of one slice are 32 contiguous columns (one tcgen05.st per decoder thread).
 static_assert(kPfRCol + kPfMaxN <= kPfACol && kPfACol + 8 * 32 <= kPfTmemCols, "tensor memory budget");
 constexpr uint32_t kPfSpin = 1u << 22;
 constexpr int kErrPrefillWait = 3;
@@ -177,19 +180,24 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const void* map, int x, int
         "l"(map), "r"(x), "r"(y), "r"(bar)
         : "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-            taddr),
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
         "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
 
@@ -419,7 +427,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
                         if (q == 0 && j == 0)
                             umma_ts<false>(dd, da, db, idesc);
                         else
-                            umma_ts<true>(dd, da + (uint32_t)(q * 32 + 8 * j), db, idesc);
+                            umma_ts<true>(dd, da + (uint32_t)(j * 32 + 8 * q), db, idesc);
                     }
                 }
                 umma_commit(bar(kBlockDone + ab.slot));
@@ -433,10 +441,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
             }
         }
     } else if (warp >= kPfEpiWarp0) {
-        // ---------------- epilogue (4 warps, one per lane quarter) ----------------
+        // ---------------- epilogue (8 warps: lane quarter, 32-column half) ----------------
         // Block sums D are scaled and added into running tile sums R kept in tensor memory;
         // the last block of a tile writes 0.125 * R out instead.
-        const int quarter = warp - kPfEpiWarp0, row = 32 * quarter + lane;
+        const int ew = warp - kPfEpiWarp0, quarter = ew & 3, c0 = 32 * (ew >> 2), row = 32 * quarter + lane;
         const uint32_t tlane = (uint32_t)(32 * quarter) << 16;
         const __half* dwring = reinterpret_cast<const __half*>(sm + PfSmem::dw);
         auto uwait = [&](int b, uint32_t parity) {
@@ -455,19 +463,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
             }
             if (!uwait(kDwFull + dr.slot, dr.phase)) break;
             if (!uwait(kAccFull + acc.slot, acc.phase)) break;
-            const float dw = __half2float(dwring[dr.slot * 128 + row]);
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");  // the previous block's R stores
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const float* dxs = reinterpret_cast<const float*>(sm + PfSmem::dxs) + ((tile & 1) * kPfMaxNb + b) * kPfMaxN;
             const bool last = b == nb - 1;
-            for (int c0 = 0; c0 < ntok; c0 += 16) {
-                uint32_t d[16], r[16];
-                tmem_ld16(tmem + tlane + (uint32_t)(acc.slot * kPfMaxN + c0), d);
-                if (b > 0) tmem_ld16(tmem + tlane + kPfRCol + (uint32_t)c0, r);
+            if (c0 < ntok) {
+                const float dw = __half2float(dwring[dr.slot * 128 + row]);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");  // the previous block's R stores
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const float* dxs =
+                    reinterpret_cast<const float*>(sm + PfSmem::dxs) + ((tile & 1) * kPfMaxNb + b) * kPfMaxN + c0;
+                uint32_t d[32], r[32];
+                tmem_ld32(tmem + tlane + (uint32_t)(acc.slot * kPfMaxN + c0), d);
+                if (b > 0) tmem_ld32(tmem + tlane + kPfRCol + (uint32_t)c0, r);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                for (int j4 = 0; j4 < 4; ++j4) {
-                    const float4 d4 = reinterpret_cast<const float4*>(dxs + c0)[j4];
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 d4 = reinterpret_cast<const float4*>(dxs)[j4];
                     const float sc[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
@@ -477,10 +486,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
                     }
                 }
                 if (!last) {
-                    tmem_st16(tmem + tlane + kPfRCol + (uint32_t)c0, r);
+                    tmem_st32(tmem + tlane + kPfRCol + (uint32_t)c0, r);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
+                    for (int j = 0; j < 32; ++j) {
                         const int n = c0 + j;
                         if (n < ntok) {
                             const float v = __fmul_rn(0.125f, __uint_as_float(r[j]));
@@ -508,9 +517,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     } else {
-        // ---------------- decoders (warps 0-15): 16 weights of one row per stage, 4 stages per block ----------------
+        // ---------------- decoders (warps 0-7): one 32-value chunk of one row per stage ----------------
+        // Per block and slice (16 values of the chunk): decode the slice of the 4 stages, then
+        // one 32-column tensor-memory store.
         const uint32_t lb = (uint32_t)lane * 4u;
-        const int dr = 32 * (warp & 3) + lane, dj = warp >> 2;  // row, 16-value part of a stage
+        const int dr = 32 * (warp & 3) + lane, dc = warp >> 2;  // row, chunk of a stage
         const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
         const __half2 off2 = __float2half2_rn(1152.0f);
         auto uwait = [&](int b, uint32_t parity) {
@@ -519,34 +530,39 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
         Ring<2> rr;
         for (int blk = 0; blk < nblk; ++blk) {
             if (!uwait(kRawFull + rr.slot, rr.phase)) break;
-            // this block's A buffers were last read by the MMAs of block blk - 2
-            if (rr.round > 0 && !uwait(kBlockDone + rr.slot, rr.phase ^ 1u)) break;
-            const uint8_t* raw = sm + PfSmem::raw + rr.slot * kPfRawBlock + dr * 16 + (dj >> 1) * 8;
+            const uint8_t* raw = sm + PfSmem::raw + rr.slot * kPfRawBlock + dr * 16 + dc * 8;
             uint2 cw[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) cw[q] = *reinterpret_cast<const uint2*>(raw + q * kPfRawStage);
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kRawEmpty + rr.slot));
+            __half2 s2[4], noff[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const uint32_t gw = cw[q].x, sw = cw[q].y;
-                const uint32_t sc = (((sw & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27;  // 2s + 1
-                const __half2 s2 = __float2half2_rn((float)sc);
-                const __half2 noff = __hneg2(__hmul2(off2, s2));
-                uint32_t v[8];
+                const uint32_t sc = (((cw[q].y & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27;  // 2s + 1
+                s2[q] = __float2half2_rn((float)sc);
+                noff[q] = __hneg2(__hmul2(off2, s2[q]));
+            }
+            // this block's A buffers were last read by the MMAs of block blk - 2
+            if (rr.round > 0 && !uwait(kBlockDone + rr.slot, rr.phase ^ 1u)) break;
 #pragma unroll
-                for (int jj = 0; jj < 2; ++jj) {
-                    const uint32_t grp = 2 * (dj & 1) + jj;
-                    const uint32_t selj = 0x5504u | (grp << 4);
-                    const uint32_t sel =
-                        tab32(kRowTabXXS + prmt2(gw, lb, selj)) | tab32(kRowTabXXS + 128 + prmt2(sw, lb, selj));
-                    biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel), s2, noff, v[4 * jj], v[4 * jj + 1]);
-                    biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel >> 16), s2, noff, v[4 * jj + 2], v[4 * jj + 3]);
+            for (int jj = 0; jj < 2; ++jj) {
+                uint32_t v[32];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint32_t grp = 2 * jj + h;
+                        const uint32_t selj = 0x5504u | (grp << 4);
+                        const uint32_t sel = tab32(kRowTabXXS + prmt2(cw[q].x, lb, selj)) |
+                                             tab32(kRowTabXXS + 128 + prmt2(cw[q].y, lb, selj));
+                        biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel), s2[q], noff[q], v[8 * q + 4 * h],
+                                        v[8 * q + 4 * h + 1]);
+                        biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel >> 16), s2[q], noff[q], v[8 * q + 4 * h + 2],
+                                        v[8 * q + 4 * h + 3]);
+                    }
                 }
-                asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(
-                                 tmem + tlane + kPfACol + (uint32_t)(rr.slot * 4 + q) * 32 + (uint32_t)dj * 8),
-                             "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-                             : "memory");
+                tmem_st32(tmem + tlane + kPfACol + (uint32_t)rr.slot * 128 + (uint32_t)(2 * dc + jj) * 32, v);
             }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
