@@ -171,6 +171,174 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+PF_TOKENS = 2048
+PF_METRIC = "routed-expert prefill tok/s (one layer, 2048 tokens)"
+PF_WORKLOAD = "BASELINE config 4: batched prefill through one MoE layer, 2048 tokens, 384 IQ2_XXS experts, top-6"
+
+
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    return 1590.0, "fallback 1590 TFLOP/s"
+
+
+def prefill_cpu_baseline(tokens=2, threads=0):
+    """Reference CPU lane on `tokens` tokens of the config-4 layer (one token = 6 experts + combine)."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib
+    ref = oracle_lib.reference()
+    if ref is None:
+        return None
+    orc = oracle_lib.Oracle()
+    rng = np.random.default_rng(98)
+    times, cores = [], None
+    for s in range(tokens + 1):  # first token warms the team and page cache
+        ids, w = orc.route_sigmoid(rng.standard_normal(EXPERTS).astype(np.float32), PICKS)
+        x = rng.standard_normal(DIM).astype(np.float32)
+        mats = [(orc.synth_matrix(16, SEED, 0, int(e), 0, FF, DIM), orc.synth_matrix(16, SEED, 0, int(e), 1, FF, DIM),
+                 orc.synth_matrix(16, SEED, 0, int(e), 2, DIM, FF)) for e in ids]
+        t0 = time.perf_counter()
+        rows = np.stack([ref.expert(16, g, u, d, x, DIM, FF, 0.0, threads)[1] for g, u, d in mats])
+        ref.combine(ids, w, rows)
+        if s > 0:
+            times.append(time.perf_counter() - t0)
+        cores = ref.L.ref_team_threads(threads)
+    per_tok = statistics.median(times)
+    return {"value": 1.0 / per_tok, "unit": "tok/s", "cores": int(cores), "kind": "reference",
+            "sample": f"{tokens} token(s) of config 4 (6 IQ2_XXS experts each, weights generated in RAM), median "
+                      f"{per_tok * 1e3:.1f} ms per token; crosslane q8k_core.hpp arithmetic, persistent 64-row-job "
+                      f"team (the CPU lane has no batched path: tokens run one after another)"}
+
+
+def run_prefill(args, rank, world, local):
+    """Config 4: T tokens through one IQ2_XXS layer per step; N>1 runs independent replicas."""
+    import torch
+    import torch.distributed as dist
+
+    import crosslane_b200 as cb
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        res = prefill_cpu_baseline(tokens=max(1, min(args.steps, 4)))
+        if res is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref.so was not built"}))
+            return
+        print(json.dumps({"metric": PF_METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": world,
+                          "steps": args.steps, "warmup": args.warmup, "ms_per_step": PF_TOKENS * 1e3 / res["value"],
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xIQ/fp32",
+                          "data": "synthetic", "config": {"workload": PF_WORKLOAD, "tokens": PF_TOKENS},
+                          "impl": "reference", "cpu_baseline": res,
+                          "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    T, k = PF_TOKENS, PICKS
+    bank = cb.ExpertBank(n_layers=1, n_experts=args.experts, dim=DIM, ff=FF, max_picks=k, device=local)
+    bank.fill_synthetic(SEED, 0)
+    stream = torch.cuda.ExternalStream(bank.stream)
+    rng = np.random.default_rng(2000 + rank)
+    n_in = 4  # distinct batches cycled through the steps
+    xs = rng.standard_normal((n_in, T, DIM)).astype(np.float32)
+    ids = np.zeros((n_in, T, k), np.int32)
+    ws = np.zeros((n_in, T, k), np.float32)
+    for i in range(n_in):
+        lg = rng.standard_normal((T, args.experts)).astype(np.float32)
+        for t in range(T):
+            ids[i, t], ws[i, t] = cb.route_host(0, lg[t], k)
+    d_x = torch.from_numpy(xs).cuda()
+    d_ids = torch.from_numpy(ids).cuda()
+    d_w = torch.from_numpy(ws).cuda()
+    d_out = torch.empty((T, DIM), dtype=torch.float32, device="cuda")
+    d_ws = torch.empty(bank.prefill_workspace_bytes(T, k), dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+
+    def step(i):
+        j = i % n_in
+        bank.prefill_layer_device(0, d_ids[j], d_w[j], d_x[j], d_out, d_ws)
+
+    for i in range(args.warmup):
+        step(i)
+    bank.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    bank.synchronize()
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * T * args.steps / (ms / 1e3)
+    # GEMM kernels alone (gate/up and down), for the tensor-pipe figure
+    gemm_ms = 0.0
+    for mask in (2, 8):
+        ev0.record(stream)
+        for _ in range(5):
+            bank.prefill_phases_device(0, d_ids[0], d_w[0], d_x[0], d_out, d_ws, mask)
+        ev1.record(stream)
+        ev1.synchronize()
+        gemm_ms += ev0.elapsed_time(ev1) / 5
+    # e2e: host buffers through clb_prefill_layer (copies in the timed region)
+    e2e_steps = 2 if args.quick else max(3, min(args.steps, 10))
+    bank.prefill_layer(0, ids[0], ws[0], xs[0])
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        bank.prefill_layer(0, ids[i % n_in], ws[i % n_in], xs[i % n_in])
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    flops = 2.0 * T * k * 3 * DIM * FF  # 811.7 GFLOP per step
+    peak_tf, peak_kind = tensor_peak()
+    hbm, hbm_kind = peaks()
+    tflops = flops / (gemm_ms / 1e3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
+        cpu = prefill_cpu_baseline(tokens=2)
+    line = {
+        "metric": PF_METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 integers x fp16 integers -> fp32 (IQ2_XXS x Q8_K)", "data": "synthetic",
+        "config": {"workload": PF_WORKLOAD, "tokens": T, "experts": args.experts, "dim": DIM, "ff": FF, "picks": k,
+                   "routing": "top-6 by sigmoid of N(0,1) logits, renormalised",
+                   "parallelism": f"replica x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2: 3.27 GB of expert weights per step"},
+        "e2e": {"value": round(world * T / e2e_s, 1), "unit": "tok/s", "h2d_bytes_per_step": T * DIM * 4 + T * k * 8,
+                "d2h_bytes_per_step": T * DIM * 4},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": round(tflops / peak_tf, 4), "traffic": None, "kernel": "clb::k_prefill_gemm (both roles)",
+                     "peak_source": peak_kind, "algorithmic_flops_per_step": flops,
+                     "gemm_ms_per_step": round(gemm_ms, 4),
+                     "hbm_frac_of_step": round(bank.weight_bytes / (ms_per_step / 1e3) / 1e9 / hbm, 4),
+                     "hbm_peak_source": hbm_kind},
+        "cpu_baseline": cpu,
+        "clocks": clocks.summary(),
+        "gpu_launches": 7 * args.steps,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    bank.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -187,12 +355,19 @@ def main():
                     help="with N>1: independent full-bank replicas per GPU instead of expert-ID sharding")
     ap.add_argument("--exact-order", action="store_true",
                     help="reference summation order (CLB_BANK_EXACT_ORDER): bit-identical to the CPU lane")
+    ap.add_argument("--prefill", action="store_true",
+                    help="BASELINE config 4 instead: 2048 tokens through one IQ2_XXS layer per step (own JSON line)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.prefill:
+        if args.steps == 200:
+            args.steps = 20
+        return run_prefill(args, rank, world, local)
 
     if args.impl == "reference":
         return run_reference(args, rank, world)

@@ -16,7 +16,9 @@
 // expert's run padded to a multiple of 16 entries; activations are gathered into list
 // order once (fp16 Q8_K values [list][K], scales [K/256][list]), so the token rows of a
 // tile are contiguous. Gate/up outputs and Q8_K(h) stay in list order; the down GEMM
-// writes expert rows by slot for the combine.
+// writes expert rows by slot for the combine. Padding entries are never written: a tile
+// reads them into MMA columns (tokens) whose results it never stores, and the columns of
+// an MMA do not mix.
 //
 // GEMM kernel: one CTA per SM, persistent over tiles (expert, 128 weight rows, up to 64
 // list entries), warp-specialised around one pipeline of 256-value K blocks (4 stages of 64)
@@ -38,8 +40,9 @@
 //    added into running tile sums that also live in tensor memory; the tile's last block
 //    writes the rows out.
 // Control loops keep ring positions as counters (no divisions in the per-block path).
-// Every wait is bounded: on time-out the CTA flags *err and an abort flag that ends every
-// loop, lets copies in flight land, waits (bounded) for its MMAs and frees its tensor memory.
+// Waits sleep in mbarrier.try_wait (suspend hint) rather than spin, and are bounded in time:
+// on time-out the CTA flags *err and an abort flag that ends every loop, lets copies in
+// flight land, waits (bounded) for its MMAs and frees its tensor memory.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -72,7 +75,9 @@ constexpr uint32_t kPfACol = 256;                       // A operand: 2 blocks x
 // A operand of a block: the 16-value slice j (0-3) of stage q (0-3) sits at columns 32 j + 8 q, so
 // the four stages of one slice are 32 contiguous columns (one tcgen05.st per decoder thread).
 static_assert(kPfRCol + kPfMaxN <= kPfACol && kPfACol + 8 * 32 <= kPfTmemCols, "tensor memory budget");
-constexpr uint32_t kPfSpin = 1u << 22;
+constexpr uint32_t kPfSpin = 1u << 22;        // drain wait polls
+constexpr uint32_t kPfSuspendNs = 20000;      // try_wait suspend hint
+constexpr uint64_t kPfTimeoutNs = 1000000000; // 1 s: a pipeline wait longer than this is an error
 constexpr int kErrPrefillWait = 3;
 
 // Magnitudes biased by +128 so that 0x64XX = 1024 + XX as fp16: +8, +25, +43 and -8, -25, -43.
@@ -136,11 +141,30 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
         : "memory");
     return done != 0;
 }
-// Bounded wait; gives up early once another thread has raised the abort flag.
+__device__ __forceinline__ uint64_t pf_now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// try_wait with a suspend-time hint: the thread sleeps until the phase completes or the hint
+// elapses instead of spinning (spinning warps would take issue slots from the decoders).
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, P1;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(kPfSuspendNs)
+        : "memory");
+    return done != 0;
+}
+// Bounded wait (kPfTimeoutNs); gives up early once another thread has raised the abort flag.
 __device__ __noinline__ bool pf_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
-    for (uint32_t it = 0; it < kPfSpin; ++it) {
-        if (mbar_try(bar, parity)) return true;
-        if ((it & 255u) == 255u && *abort_flag) return false;
+    const uint64_t t0 = pf_now_ns();
+    for (;;) {
+        if (mbar_try_sleep(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (pf_now_ns() - t0 > kPfTimeoutNs) break;
     }
     atomicExch(err, kErrPrefillWait);
     *abort_flag = 1;
@@ -675,8 +699,8 @@ __global__ void __launch_bounds__(256) k_prefill_quant(const float* __restrict__
     quant_block_fp16(v, qs + o, d + blk, q16 + o);
 }
 
-// Token rows of Q8_K(x) into list order: xg16[p] = q16[token of list[p]], dxg[b][p] its scales
-// (zeros for padding entries). One warp per (entry, 256-value block).
+// Token rows of Q8_K(x) into list order: xg16[p] = q16[token of list[p]], dxg[b][p] its scales.
+// One warp per (entry, 256-value block).
 __global__ void __launch_bounds__(256) k_prefill_gather(const int* __restrict__ list, int P, int k, int cols,
                                                         const __half* __restrict__ q16, const float* __restrict__ d,
                                                         __half* __restrict__ xg16, float* __restrict__ dxg) {
@@ -684,19 +708,15 @@ __global__ void __launch_bounds__(256) k_prefill_gather(const int* __restrict__ 
     const int blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (blk >= P * nbr) return;
     const int p = blk / nbr, b = blk % nbr, sl = list[p];
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    float dv = 0.0f;
-    if (sl >= 0) {
-        const int t = sl / k;
-        v = *reinterpret_cast<const uint4*>(q16 + (size_t)t * cols + b * 256 + lane * 8);
-        dv = d[(size_t)t * nbr + b];
-    }
-    *reinterpret_cast<uint4*>(xg16 + (size_t)p * cols + b * 256 + lane * 8) = v;
-    if (lane == 0) dxg[(size_t)b * P + p] = dv;
+    if (sl < 0) return;  // padding: the GEMM reads these rows into columns it never stores
+    const int t = sl / k;
+    *reinterpret_cast<uint4*>(xg16 + (size_t)p * cols + b * 256 + lane * 8) =
+        *reinterpret_cast<const uint4*>(q16 + (size_t)t * cols + b * 256 + lane * 8);
+    if (lane == 0) dxg[(size_t)b * P + p] = d[(size_t)t * nbr + b];
 }
 
 // SwiGLU of the gate/up rows (list order) and Q8_K of h: qh16[p] fp16 values, dhg[b][p]
-// scales; padding entries get zeros. One warp per (entry, 256-value block).
+// scales. One warp per (entry, 256-value block).
 __global__ void __launch_bounds__(256) k_prefill_act(const int* __restrict__ list, int P, int ff, float limit,
                                                      const float* __restrict__ gu, int8_t* __restrict__ qh,
                                                      __half* __restrict__ qh16, float* __restrict__ dhg) {
@@ -705,11 +725,7 @@ __global__ void __launch_bounds__(256) k_prefill_act(const int* __restrict__ lis
     if (blk >= P * nbr) return;
     const int p = blk / nbr, b = blk % nbr;
     const size_t o = (size_t)p * ff + b * 256;
-    if (list[p] < 0) {
-        *reinterpret_cast<uint4*>(qh16 + o + lane * 8) = make_uint4(0u, 0u, 0u, 0u);
-        if (lane == 0) dhg[(size_t)b * P + p] = 0.0f;
-        return;
-    }
+    if (list[p] < 0) return;  // padding (see k_prefill_gather)
     const float* g = gu + (size_t)p * 2 * ff + b * 256 + lane * 8;
     const float* u = g + ff;
     float v[8];
@@ -719,25 +735,50 @@ __global__ void __launch_bounds__(256) k_prefill_act(const int* __restrict__ lis
 }
 
 // out[t] = fma over the token's picks in ascending expert id of (w, expert row), then
-// + resid when given (runtime.cpp:184-187).
-__global__ void k_prefill_combine(const float* __restrict__ y, const int* __restrict__ ids, const float* __restrict__ w,
-                                  int k, int dim, const float* __restrict__ resid, float* __restrict__ out) {
-    const int t = blockIdx.y;
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= dim) return;
-    const int* id = ids + (size_t)t * k;
-    float acc = 0.0f;
-    int prev = -1;
-    for (int o = 0; o < k; ++o) {
-        int best = -1;
-        for (int p = 0; p < k; ++p)
-            if (id[p] > prev && (best < 0 || id[p] < id[best])) best = p;
-        if (best < 0) break;
-        prev = id[best];
-        acc = __fmaf_rn(w[(size_t)t * k + best], y[((size_t)t * k + best) * dim + c], acc);
+// + resid when given (runtime.cpp:184-187). One CTA per token, four columns per thread.
+__global__ void __launch_bounds__(256) k_prefill_combine(const float* __restrict__ y, const int* __restrict__ ids,
+                                                         const float* __restrict__ w, int k, int dim,
+                                                         const float* __restrict__ resid, float* __restrict__ out) {
+    __shared__ int order[kMaxPicks];
+    __shared__ float wo[kMaxPicks];
+    __shared__ int npk;
+    const int t = blockIdx.x;
+    if (threadIdx.x == 0) {
+        const int* id = ids + (size_t)t * k;
+        int prev = -1, n = 0;
+        for (int o = 0; o < k; ++o) {
+            int best = -1;
+            for (int p = 0; p < k; ++p)
+                if (id[p] > prev && (best < 0 || id[p] < id[best])) best = p;
+            if (best < 0) break;
+            prev = id[best];
+            order[n] = best;
+            wo[n++] = w[(size_t)t * k + best];
+        }
+        npk = n;
     }
-    if (resid) acc = __fadd_rn(resid[(size_t)t * dim + c], acc);
-    out[(size_t)t * dim + c] = acc;
+    __syncthreads();
+    const int n = npk, d4 = dim >> 2;
+    const float4* y4 = reinterpret_cast<const float4*>(y) + (size_t)t * k * d4;
+    for (int c = threadIdx.x; c < d4; c += blockDim.x) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int o = 0; o < n; ++o) {
+            const float4 v = y4[(size_t)order[o] * d4 + c];
+            const float wt = wo[o];
+            acc.x = __fmaf_rn(wt, v.x, acc.x);
+            acc.y = __fmaf_rn(wt, v.y, acc.y);
+            acc.z = __fmaf_rn(wt, v.z, acc.z);
+            acc.w = __fmaf_rn(wt, v.w, acc.w);
+        }
+        if (resid) {
+            const float4 r = reinterpret_cast<const float4*>(resid)[(size_t)t * d4 + c];
+            acc.x = __fadd_rn(r.x, acc.x);
+            acc.y = __fadd_rn(r.y, acc.y);
+            acc.z = __fadd_rn(r.z, acc.z);
+            acc.w = __fadd_rn(r.w, acc.w);
+        }
+        reinterpret_cast<float4*>(out)[(size_t)t * d4 + c] = acc;
+    }
 }
 
 namespace {
@@ -881,7 +922,7 @@ cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const 
         g.out = ws.y;
         k_prefill_gemm<<<sms, kPfThreads, PfSmem::total, s>>>(g);
     }
-    if (phase_mask & 16) k_prefill_combine<<<dim3((dim + 255) / 256, T), 256, 0, s>>>(ws.y, ids, w, k, dim, resid, out);
+    if (phase_mask & 16) k_prefill_combine<<<T, 256, 0, s>>>(ws.y, ids, w, k, dim, resid, out);
     return cudaGetLastError();
 }
 
