@@ -31,9 +31,13 @@ constexpr int kErrBarrier = 2;                     // err flag value of a timed-
 // ordered before it by the preceding __syncthreads, become visible first) and polls
 // with acquire loads. Bounded: after kBarrierSpinLimit polls the CTA sets *err and
 // every thread of it gets false, so the kernel can return instead of hanging.
-__device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err) {
+// `overlap` runs on the threads other than thread 0 while thread 0 waits (work that needs
+// no other CTA's results, e.g. staging the next layer's routing).
+template <class F>
+__device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err, F&& overlap) {
     __syncthreads();
     int ok = 1;
+    if (threadIdx.x != 0) overlap();
     if (threadIdx.x == 0) {
         const unsigned target = epoch * gridDim.x;
         asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(count), "r"(1u) : "memory");
@@ -49,6 +53,9 @@ __device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err) {
         }
     }
     return __syncthreads_and(ok) != 0;
+}
+__device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err) {
+    return grid_barrier(count, epoch, err, [] {});
 }
 
 // After a layer's down phase (all local CTAs past the grid barrier, their peer stores
@@ -148,7 +155,7 @@ struct StackSmem {
         xd = o;    o = up16(o + (size_t)(dim >> 8) * 4);
         hq = o;    o = up16(o + (size_t)k * (ff >> 8) * kActStride);  // fast order: every pick
         hd = o;    o = up16(o + (size_t)k * (ff >> 8) * 4);
-        desc = o;  o = up16(o + (size_t)k * sizeof(ExpertDesc));
+        desc = o;  o = up16(o + (size_t)2 * k * sizeof(ExpertDesc));  // this and the next layer
         ids = o;   o = up16(o + (size_t)2 * kMaxPicks * 4);  // this and the previous layer
         w = o;     o = up16(o + (size_t)2 * kMaxPicks * 4);
         order = o; o = up16(o + (size_t)2 * kMaxPicks * 4);
@@ -207,36 +214,45 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
     fill_row_tables(P.tables, xch_all);
     for (int i = tid; i < dim; i += NT) hs[i] = __ldcg(P.h_in + i);
 
+    // Routing of layer lj into slot lj & 1, by warp 1: ids and weights, the ascending-id order
+    // of the picks, the picks whose expert this GPU holds (in pick order, count last) and
+    // their descriptors. Layer 0 before the loop; layer l + 1 while the last grid barrier of
+    // layer l is waited for, so the loads are off the critical path.
+    auto load_routing = [&](int lj) {
+        if (warp != 1) return;
+        const int sl = lj & 1;
+        int e = -1;
+        if (lane < k) {
+            e = __ldcg(P.route_ids + (size_t)lj * k + lane);
+            sid[sl * kMaxPicks + lane] = e;
+            sw[sl * kMaxPicks + lane] = __ldcg(P.route_w + (size_t)lj * k + lane);
+        }
+        int rank = 0;
+        for (int p = 0; p < k; ++p) rank += __shfl_sync(0xffffffffu, e, p) < e;
+        if (lane < k) sord[sl * kMaxPicks + rank] = lane;
+        const bool mine = lane < k && e >= sh.own_begin && e < sh.own_end;
+        const uint32_t m = __ballot_sync(0xffffffffu, mine);
+        if (mine) sown[sl * (kMaxPicks + 1) + __popc(m & ((1u << lane) - 1u))] = lane;
+        if (lane == 0) sown[sl * (kMaxPicks + 1) + kMaxPicks] = __popc(m);
+        __syncwarp();
+        constexpr int words = (int)(sizeof(ExpertDesc) / 4);
+        for (int i = lane; i < k * words; i += 32) {
+            const int p = i / words, wd = i - p * words;
+            const uint32_t* src =
+                reinterpret_cast<const uint32_t*>(P.desc + (size_t)(P.first + lj) * P.E + sid[sl * kMaxPicks + p]);
+            reinterpret_cast<uint32_t*>(dsc + sl * k + p)[wd] = __ldcg(src + wd);
+        }
+    };
+    if (P.nl > 0) load_routing(0);
+    __syncthreads();
+
     for (int li = 0; li <= P.nl; ++li) {
         const int cur = li & 1, prev = cur ^ 1;
         bool stored_peer = false;  // this thread stored expert rows into a peer's slot
-        // routing of this layer, and the ascending-id order of its picks
-        if (li < P.nl && tid < k) {
-            sid[cur * kMaxPicks + tid] = P.route_ids[(size_t)li * k + tid];
-            sw[cur * kMaxPicks + tid] = P.route_w[(size_t)li * k + tid];
-        }
-        __syncthreads();
-        if (li < P.nl && tid < k) {
-            const int me = sid[cur * kMaxPicks + tid];
-            int rank = 0;
-            for (int p = 0; p < k; ++p) rank += sid[cur * kMaxPicks + p] < me;
-            sord[cur * kMaxPicks + rank] = tid;
-        }
-        if (li < P.nl && warp == 0) {  // picks whose expert this GPU holds, in pick order
-            const int e = lane < k ? sid[cur * kMaxPicks + lane] : -1;
-            const bool mine = lane < k && e >= sh.own_begin && e < sh.own_end;
-            const uint32_t m = __ballot_sync(0xffffffffu, mine);
-            if (mine) sown[cur * (kMaxPicks + 1) + __popc(m & ((1u << lane) - 1u))] = lane;
-            if (lane == 0) sown[cur * (kMaxPicks + 1) + kMaxPicks] = __popc(m);
-        }
-        if (li < P.nl)
-            for (int i = tid; i < k * (int)(sizeof(ExpertDesc) / 4); i += NT) {
-                const int p = i / (int)(sizeof(ExpertDesc) / 4), wd = i % (int)(sizeof(ExpertDesc) / 4);
-                const uint32_t* src = reinterpret_cast<const uint32_t*>(
-                    P.desc + (size_t)(P.first + li) * P.E + sid[cur * kMaxPicks + p]);
-                reinterpret_cast<uint32_t*>(dsc + p)[wd] = src[wd];
-            }
-        __syncthreads();
+        const ExpertDesc* dl = dsc + cur * k;  // this layer's descriptors
+        auto stage_next = [&] {
+            if (li + 1 < P.nl) load_routing(li + 1);
+        };
 
         // 1. h += combine of the previous layer (ascending expert id), in every CTA: four
         //    rows per thread and two such quads at a time, the rows of up to 3 picks of both
@@ -355,7 +371,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                 float y = 0.0f;
                 if (rg < nrg) {
                     const int pick = own[rg / rgpp], row = (rg % rgpp) * 32 + lane;
-                    const PackedMat& m = mat ? dsc[pick].up : dsc[pick].gate;
+                    const PackedMat& m = mat ? dl[pick].up : dl[pick].gate;
                     if (m.body != nullptr && m.k == dim && m.n == ff) y = lane_row_partial_any(m, row, b0, b1, xq, xd);
                     else if (lane == 0) atomicExch(P.err, 1);
                 }
@@ -417,7 +433,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                     float y = 0.0f;
                     if (slot < PPR && pr < npair) {
                         const int pick = own[pr / rgd], row = (pr % rgd) * 32 + lane;
-                        const PackedMat& m = dsc[pick].down;
+                        const PackedMat& m = dl[pick].down;
                         if (m.body != nullptr && m.k == ff && m.n == dim)
                             y = lane_row_partial_any(m, row, d0, d1, hq + (size_t)pick * nbh * kActStride, hd + pick * nbh);
                         else if (lane == 0) atomicExch(P.err, 1);
@@ -448,7 +464,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             for (int it = gw; it < items; it += W) {
                 const int pick = own[it / (2 * groups)], rem = it % (2 * groups);
                 const int group = rem >> 1, mat = rem & 1;
-                const PackedMat& m = mat ? dsc[pick].up : dsc[pick].gate;
+                const PackedMat& m = mat ? dl[pick].up : dl[pick].gate;
                 const int row = group * rpw + lane / 4;
                 float y = 0.0f;
                 if (m.body != nullptr && m.k == dim && m.n == ff) y = quad_row_dot_any<false>(m, row, xq, xd, xch);
@@ -473,7 +489,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                 warp_quant_regs(v, hq + (size_t)hb * kActStride, hd + hb);
             }
             __syncthreads();
-            const PackedMat& m = dsc[my_pick].down;
+            const PackedMat& m = dl[my_pick].down;
             const int groups_d = dim >> 5;
             const bool ok = m.body != nullptr && m.k == ff && m.n == dim;
             if (kown > 0 && !ok && tid == 0) atomicExch(P.err, 1);
@@ -488,7 +504,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             }
         }
         if (stored_peer) __threadfence_system();  // this thread's peer stores before the barrier
-        if (!grid_barrier(P.bar, 2 * li + 2, P.err)) return;
+        if (!grid_barrier(P.bar, 2 * li + 2, P.err, stage_next)) return;
         if (sh.world > 1 && !exchange_rows(sh, li, P.err)) return;
     }
     // h after the last layer: each CTA writes its slice
