@@ -69,6 +69,9 @@ SIGNATURES = {
     "clb_bank_stack_persistent": (_I, [_P]),
     "clb_bank_exchange_handle": (_I, [_P, _P, _PE]),
     "clb_bank_connect": (_I, [_P, _I, _I, _P, _PE]),
+    "clb_placement_parse": (_I, [C.c_char_p, _SZ, _I, _I, _P, C.POINTER(C.c_uint64), _PE]),
+    "clb_bank_apply_placement": (_I, [_P, _P, _I, _PE]),
+    "clb_bank_placed": (_I, [_P, _U32, _I]),
     "clb_bank_contains": (_I, [_P, _U32, _I]),
     "clb_bank_compute": (_I, [_P, _U32, _I, _P, _P, _PE]),
     "clb_bank_compute_many": (_I, [_P, _U32, _P, _I, _P, _P, _PE]),

@@ -127,6 +127,18 @@ class ExpertBank:
         check(lib.clb_bank_compute_many(self._h, layer, _ptr(ids), len(ids), _ptr(x), _ptr(y), C.byref(err)), err)
         return y
 
+    # -- frozen warm placement (crosslane_b200.placement) --
+    def apply_placement(self, lanes, lane_id: int = 3) -> None:
+        """Hold exactly the experts `lanes` [layers][experts] assigns to `lane_id` (3 = CUDA,
+        or 1 = the GPU-lane slot); before any weights are loaded."""
+        lanes = np.ascontiguousarray(lanes, dtype=np.int32)
+        assert lanes.shape == (self.n_layers, self.n_experts)
+        err = ErrorV1()
+        check(lib.clb_bank_apply_placement(self._h, _ptr(lanes), lane_id, C.byref(err)), err)
+
+    def placed(self, layer: int, expert: int) -> bool:
+        return bool(lib.clb_bank_placed(self._h, layer, expert))
+
     # -- layer / stack --
     def layer_execute(self, layer: int, ids, w, x, shared=None) -> np.ndarray:
         ids, w, x = _i32(ids), _f32(w), _f32(x)

@@ -4,9 +4,12 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cerrno>
+#include <cctype>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <exception>
 #include <map>
@@ -144,6 +147,7 @@ struct clb_bank {
     uint64_t weight_bytes = 0;
     std::vector<clb::ExpertDesc> desc;  // [layer][expert]
     std::vector<uint8_t> resident;
+    std::vector<uint8_t> placed;  // [layer][expert]: this bank is to hold it (owned range, or a placement)
     clb::ExpertDesc* d_desc = nullptr;
     uint16_t* d_scales = nullptr;
 
@@ -455,6 +459,9 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         ensure_device_ready(cfg.device, bank->stream);
         bank->desc.assign(bank->L() * bank->E(), clb::ExpertDesc{});
         bank->resident.assign(bank->L() * bank->E(), 0);
+        bank->placed.assign(bank->L() * bank->E(), 0);
+        for (size_t l = 0; l < bank->L(); ++l)
+            for (int e = bank->cfg.expert_begin; e < bank->cfg.expert_end; ++e) bank->placed[l * bank->E() + (size_t)e] = 1;
         bank->d_desc = bank->dev_alloc<clb::ExpertDesc>(bank->L() * bank->E());
         const size_t dim = (size_t)cfg.dim, ff = (size_t)cfg.ff, k = (size_t)cfg.max_picks;
         bank->d_x = bank->dev_alloc<float>(dim);
@@ -515,6 +522,71 @@ void clb_bank_destroy(clb_bank* bank) {
 }
 
 uint64_t clb_bank_weight_bytes(const clb_bank* bank) { return bank ? bank->weight_bytes : 0; }
+
+// ---- frozen warm placement (STRATA_WARM_PLACEMENT_V1, frozen_placement.hpp:5-16) ----
+int32_t clb_placement_parse(const char* text, size_t len, int32_t n_layers, int32_t n_experts, int32_t* lanes,
+                            uint64_t* tag, clb_error_v1* err) {
+    if (!text || !lanes || n_layers <= 0 || n_experts <= 0) return fail(err, CLB_E_INVALID, "null placement/output");
+    return guarded(err, [&] {
+        const char* p = text;
+        const char* end = text + len;
+        auto word = [&](std::string& w) {
+            while (p < end && std::isspace((unsigned char)*p)) ++p;
+            const char* b = p;
+            while (p < end && !std::isspace((unsigned char)*p)) ++p;
+            w.assign(b, (size_t)(p - b));
+            return !w.empty();
+        };
+        auto number = [&](uint64_t& v) {
+            std::string w;
+            if (!word(w) || w.size() > 20) return false;
+            for (char c : w)
+                if (c < '0' || c > '9') return false;
+            errno = 0;
+            v = std::strtoull(w.c_str(), nullptr, 10);
+            return errno == 0;
+        };
+        std::string version;
+        uint64_t nl = 0, ne = 0, t = 0;
+        require(word(version) && version == "STRATA_WARM_PLACEMENT_V1" && number(nl) && number(ne) && number(t) &&
+                    nl == (uint64_t)n_layers && ne == (uint64_t)n_experts,
+                CLB_E_INVALID, "warm placement header/profile mismatch");
+        for (int32_t l = 0; l < n_layers; ++l)
+            for (int32_t e = 0; e < n_experts; ++e) {
+                uint64_t rl = 0, re = 0, lane = 0;
+                require(number(rl) && number(re) && number(lane) && rl == (uint64_t)l && re == (uint64_t)e &&
+                            lane <= (uint64_t)CLB_LANE_CUDA,
+                        CLB_E_INVALID, "warm placement missing/duplicate/unsorted row at (%d, %d)", l, e);
+                lanes[(size_t)l * (size_t)n_experts + (size_t)e] = (int32_t)lane;
+            }
+        std::string extra;
+        require(!word(extra), CLB_E_INVALID, "extra/invalid warm placement data");
+        if (tag) *tag = t;
+    });
+}
+
+int32_t clb_bank_apply_placement(clb_bank* bank, const int32_t* lanes, int32_t lane_id, clb_error_v1* err) {
+    if (!bank || !lanes) return fail(err, CLB_E_INVALID, "null bank/placement");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        bank->check_usable();
+        require(lane_id >= 1 && lane_id <= CLB_LANE_CUDA, CLB_E_INVALID, "lane id %d is not a GPU lane", lane_id);
+        require(bank->weight_bytes == 0, CLB_E_STATE, "placement must be applied before any weights are loaded");
+        for (size_t l = 0; l < bank->L(); ++l)
+            for (size_t e = 0; e < bank->E(); ++e) {
+                const int32_t lane = lanes[l * bank->E() + e];
+                require(lane >= 0 && lane <= CLB_LANE_CUDA, CLB_E_INVALID, "lane %d out of range", lane);
+                require(lane != lane_id || bank->owns((int)e), CLB_E_INVALID,
+                        "expert (%zu, %zu) is placed on this lane but outside the bank's owned range", l, e);
+                bank->placed[l * bank->E() + e] = lane == lane_id ? 1 : 0;
+            }
+    });
+}
+
+int32_t clb_bank_placed(const clb_bank* bank, uint32_t layer, int32_t expert) {
+    if (!bank || layer >= (uint32_t)bank->cfg.n_layers || expert < 0 || expert >= bank->cfg.n_experts) return 0;
+    return bank->placed[(size_t)layer * bank->E() + (size_t)expert] ? 1 : 0;
+}
 
 int32_t clb_bank_contains(const clb_bank* bank, uint32_t layer, int32_t expert) {
     if (!bank || layer >= (uint32_t)bank->cfg.n_layers || expert < 0 || expert >= bank->cfg.n_experts) return 0;
@@ -593,16 +665,19 @@ int32_t clb_bank_fill_synthetic(clb_bank* bank, uint64_t seed, int32_t policy, c
                 size_t slab = 0;
                 std::vector<size_t> offs;
                 for (int e = c.expert_begin; e < c.expert_end; ++e) {
+                    if (!bank->placed[(size_t)layer * bank->E() + (size_t)e]) continue;
                     const int t = clb_expert_type(policy, seed, layer, (uint32_t)e);
                     for (int role = 0; role < 3; ++role) {
                         offs.push_back(slab);
                         slab += clb_packed_layout(t, role == 2 ? c.dim : c.ff, role == 2 ? c.ff : c.dim).total;
                     }
                 }
+                if (slab == 0) continue;  // nothing placed in this layer
                 uint8_t* base = bank->dev_alloc<uint8_t>(slab);
                 bank->weight_bytes += slab;
                 size_t i = 0;
                 for (int e = c.expert_begin; e < c.expert_end; ++e) {
+                    if (!bank->placed[(size_t)layer * bank->E() + (size_t)e]) continue;
                     const int t = clb_expert_type(policy, seed, layer, (uint32_t)e);
                     for (int role = 0; role < 3; ++role, ++i) {
                         const int n = role == 2 ? c.dim : c.ff, k = role == 2 ? c.ff : c.dim;
@@ -631,6 +706,8 @@ int32_t clb_bank_load_matrix(clb_bank* bank, uint32_t layer, int32_t expert, int
         require(layer < (uint32_t)c.n_layers && expert >= 0 && expert < c.n_experts && role >= 0 && role <= 2,
                 CLB_E_INVALID, "matrix address out of range");
         require(bank->owns(expert), CLB_E_INVALID, "expert %d outside this bank's owned range", expert);
+        require(bank->placed[(size_t)layer * bank->E() + (size_t)expert], CLB_E_INVALID,
+                "expert (%u, %d) is not placed on this bank", layer, expert);
         require(clb_type_supported(type), CLB_E_UNSUPPORTED, "quant type %d has no kernel", type);
         const int n = role == 2 ? c.dim : c.ff, k = role == 2 ? c.ff : c.dim;
         require(ggml && bytes == (size_t)n * (k / 256) * clb_block_bytes(type), CLB_E_INVALID,

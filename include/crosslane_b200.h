@@ -125,7 +125,8 @@ typedef struct clb_bank_config_v1 {
 int32_t clb_bank_create(const clb_bank_config_v1* cfg, clb_bank** out, clb_error_v1* err);
 void clb_bank_destroy(clb_bank* bank);
 
-/* Allocates and fills every owned matrix with the counter-based synthetic weights
+/* Allocates and fills every placed matrix (the owned range, or the experts a placement
+ * gave this bank: clb_bank_apply_placement) with the counter-based synthetic weights
  * (seed, layer, expert, role, block) -> bytes. type_policy: 0 all IQ2_XXS,
  * 1 experts 0-127 IQ2_XXS / 128-255 IQ2_XS / 256+ IQ1_M, 2 per (layer, expert) from
  * the seed, 3 all IQ2_XS, 4 all IQ1_M. */
@@ -156,6 +157,31 @@ int32_t clb_bank_exchange_handle(clb_bank* bank, void* handle_out, clb_error_v1*
 /* Opens the peers' regions: handles = world x 64 bytes, indexed by rank (own entry
  * ignored). world in [2, 8]; needs the persistent stack kernel. */
 int32_t clb_bank_connect(clb_bank* bank, int32_t rank, int32_t world, const void* handles, clb_error_v1* err);
+
+/* ---- frozen warm placement ----
+ * crosslane freezes which lane serves each (layer, expert) in a text document
+ * (frozen_placement.hpp:5-16): "STRATA_WARM_PLACEMENT_V1 <layers> <experts> <profile tag>"
+ * followed by one "<layer> <expert> <lane>" row for every pair in order. Lanes 0 (CPU),
+ * 1 (HIP) and 2 (SYCL) are the reference's; CLB_LANE_CUDA (3) names this lane, which a
+ * document may also give lane 1 (the GPU-lane slot). */
+#define CLB_LANE_CPU 0
+#define CLB_LANE_HIP 1
+#define CLB_LANE_SYCL 2
+#define CLB_LANE_CUDA 3
+/* Parses a placement document (no GPU involved): lanes[layers * experts] receive the lane of
+ * each (layer, expert), *tag (may be NULL) the profile tag. The header must name
+ * n_layers x n_experts; rows must be complete, sorted, unique, lanes in [0, 3], nothing
+ * after the last row (the reference's checks); otherwise CLB_E_INVALID with the reason. */
+int32_t clb_placement_parse(const char* text, size_t len, int32_t n_layers, int32_t n_experts, int32_t* lanes,
+                            uint64_t* tag, clb_error_v1* err);
+/* Restricts the bank to the experts that lanes[layers * experts] assigns to lane_id (1 or 3
+ * for this lane): later fills and matrix loads cover exactly those (within the owned
+ * range), and clb_bank_contains answers for them, so warm_execute sends every other pick to
+ * its other lane. Only before any weights are loaded (else CLB_E_STATE). Replaces the HIP
+ * half of apply_frozen_warm_placement (frozen_placement.hpp:5-37). */
+int32_t clb_bank_apply_placement(clb_bank* bank, const int32_t* lanes, int32_t lane_id, clb_error_v1* err);
+/* 1 if (layer, expert) is placed on this bank (resident or to be loaded), else 0. */
+int32_t clb_bank_placed(const clb_bank* bank, uint32_t layer, int32_t expert);
 
 /* 1 if (layer, expert) is resident in this bank, else 0. Const, allocation free.
  * Replaces WarmRedirect::warm_contains (engine/strata/warm/runtime.hpp:14). */
