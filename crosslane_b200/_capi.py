@@ -72,6 +72,14 @@ SIGNATURES = {
     "clb_placement_parse": (_I, [C.c_char_p, _SZ, _I, _I, _P, C.POINTER(C.c_uint64), _PE]),
     "clb_bank_apply_placement": (_I, [_P, _P, _I, _PE]),
     "clb_bank_placed": (_I, [_P, _U32, _I]),
+    "clb_strata_pack_open": (_I, [C.c_char_p, C.POINTER(_P), _PE]),
+    "clb_strata_pack_close": (None, [_P]),
+    "clb_strata_pack_meta": (_I, [_P, C.c_char_p, C.c_char_p, _SZ]),
+    "clb_strata_pack_tensor": (_I, [_P, C.c_char_p, C.c_char_p, _SZ, C.POINTER(C.c_uint64), C.POINTER(C.c_int64), _I,
+                                    C.POINTER(_I)]),
+    "clb_strata_pack_read": (_I, [_P, C.c_char_p, C.c_uint64, _P, C.c_uint64, _PE]),
+    "clb_bank_load_strata_pack": (_I, [_P, _P, _U32, _PE]),
+    "clb_bank_geometry": (_I, [_P, C.POINTER(_I), C.POINTER(_I), C.POINTER(_I), C.POINTER(_I)]),
     "clb_bank_contains": (_I, [_P, _U32, _I]),
     "clb_bank_compute": (_I, [_P, _U32, _I, _P, _P, _PE]),
     "clb_bank_compute_many": (_I, [_P, _U32, _P, _I, _P, _P, _PE]),

@@ -136,6 +136,12 @@ class ExpertBank:
         err = ErrorV1()
         check(lib.clb_bank_apply_placement(self._h, _ptr(lanes), lane_id, C.byref(err)), err)
 
+    def load_strata_pack(self, pack, first_layer: int = 0) -> None:
+        """Repack every matrix placed on this bank from a crosslane_b200.strata_pack.StrataPack
+        (bank layer l <- pack layer first_layer + l)."""
+        err = ErrorV1()
+        check(lib.clb_bank_load_strata_pack(self._h, pack.handle, first_layer, C.byref(err)), err)
+
     def placed(self, layer: int, expert: int) -> bool:
         return bool(lib.clb_bank_placed(self._h, layer, expert))
 

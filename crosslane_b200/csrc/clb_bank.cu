@@ -22,56 +22,13 @@
 #include <vector>
 
 #include "../../include/crosslane_b200.h"
+#include "clb_host.h"
 #include "clb_kernels.h"
+#include "clb_pack_io.h"
 #include "clb_pack.h"
 #include "scale_table.h"
 
 namespace {
-
-struct Error : std::runtime_error {
-    int code;
-    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
-};
-
-void require(bool ok, int code, const char* fmt, ...) {
-    if (ok) return;
-    char buf[480];
-    va_list ap;
-    va_start(ap, fmt);
-    std::vsnprintf(buf, sizeof buf, fmt, ap);
-    va_end(ap);
-    throw Error(code, buf);
-}
-
-void cuda_check(cudaError_t e, const char* what) {
-    if (e != cudaSuccess) throw Error(CLB_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
-}
-
-int fail(clb_error_v1* err, int code, const char* msg) {
-    if (err) {
-        err->code = code;
-        std::snprintf(err->message, sizeof err->message, "%s", msg);
-    }
-    return code;
-}
-
-template <class F>
-int guarded(clb_error_v1* err, F&& f) {
-    try {
-        f();
-        if (err) {
-            err->code = CLB_OK;
-            err->message[0] = 0;
-        }
-        return CLB_OK;
-    } catch (const Error& e) {
-        return fail(err, e.code, e.what());
-    } catch (const std::bad_alloc&) {
-        return fail(err, CLB_E_NOMEM, "host allocation failed");
-    } catch (const std::exception& e) {
-        return fail(err, CLB_E_INVALID, e.what());
-    }
-}
 
 struct DeviceGuard {
     int prev = -1;
@@ -441,7 +398,7 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
                     cfg.ff <= 16384,
                 CLB_E_UNSUPPORTED, "dim and ff must be positive multiples of 256 (dim <= 32768, ff <= 16384)");
         require(cfg.max_picks >= 1 && cfg.max_picks <= clb::kMaxPicks && cfg.max_picks <= cfg.n_experts,
-                CLB_E_INVALID, "max_picks must be in [1, 16]");
+                CLB_E_INVALID, "max_picks must be in [1, min(16, n_experts)]");
         require(std::isfinite(cfg.limit) && cfg.limit >= 0, CLB_E_INVALID, "SwiGLU limit must be finite and >= 0");
         require((cfg.flags & ~(CLB_BANK_EXACT_ORDER | CLB_BANK_PER_LAYER_KERNELS)) == 0, CLB_E_INVALID,
                 "unknown bank flags 0x%x", cfg.flags);
@@ -696,50 +653,113 @@ int32_t clb_bank_fill_synthetic(clb_bank* bank, uint64_t seed, int32_t policy, c
     });
 }
 
+static void load_matrix_locked(clb_bank* bank, uint32_t layer, int32_t expert, int32_t role, int32_t type,
+                               const void* ggml, size_t bytes, bool upload) {
+    bank->check_usable();
+    const auto& c = bank->cfg;
+    require(layer < (uint32_t)c.n_layers && expert >= 0 && expert < c.n_experts && role >= 0 && role <= 2,
+            CLB_E_INVALID, "matrix address out of range");
+    require(bank->owns(expert), CLB_E_INVALID, "expert %d outside this bank's owned range", expert);
+    require(bank->placed[(size_t)layer * bank->E() + (size_t)expert], CLB_E_INVALID,
+            "expert (%u, %d) is not placed on this bank", layer, expert);
+    require(clb_type_supported(type), CLB_E_UNSUPPORTED, "quant type %d has no kernel", type);
+    const int n = role == 2 ? c.dim : c.ff, k = role == 2 ? c.ff : c.dim;
+    require(ggml && bytes == (size_t)n * (k / 256) * clb_block_bytes(type), CLB_E_INVALID,
+            "matrix byte extent %zu does not match [%d, %d] of type %d", bytes, n, k, type);
+    auto& d = bank->desc[(size_t)layer * bank->E() + (size_t)expert];
+    const PackedMat& cur = role == 0 ? d.gate : role == 1 ? d.up : d.down;
+    require(cur.body == nullptr, CLB_E_INVALID, "matrix already loaded");
+    DeviceGuard g(c.device);
+    bank->device_step([&] {
+        const PackedLayout l = clb_packed_layout(type, n, k);
+        uint8_t* packed = bank->dev_alloc<uint8_t>(l.total);
+        void* staging = nullptr;
+        cuda_check(cudaMalloc(&staging, bytes), "staging alloc");
+        int bad = 0;
+        cudaError_t e = cudaMemcpyAsync(staging, ggml, bytes, cudaMemcpyHostToDevice, bank->stream);
+        if (e == cudaSuccess) e = cudaMemsetAsync(bank->d_err, 0, sizeof(int), bank->stream);
+        if (e == cudaSuccess)
+            e = clb::launch_pack(static_cast<const uint8_t*>(staging), packed, l, type, n, k, bank->d_err,
+                                 bank->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(&bad, bank->d_err, sizeof(int), cudaMemcpyDeviceToHost, bank->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(bank->stream);
+        cudaFree(staging);
+        cuda_check(e, "matrix upload/pack");
+        if (bad) {
+            cuda_check(cudaMemsetAsync(bank->d_err, 0, sizeof(int), bank->stream), "flag reset");
+            throw Error(CLB_E_NONFINITE, "non-finite fp16 super-scale in matrix");
+        }
+        bank->weight_bytes += l.total;
+        bank->set_matrix(layer, expert, role, type, packed);
+        bank->refresh_resident(layer, expert);
+        if (upload) bank->upload_desc();
+    });
+}
+
 int32_t clb_bank_load_matrix(clb_bank* bank, uint32_t layer, int32_t expert, int32_t role, int32_t type,
                              const void* ggml, size_t bytes, clb_error_v1* err) {
     if (!bank) return fail(err, CLB_E_INVALID, "null bank");
     std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] { load_matrix_locked(bank, layer, expert, role, type, ggml, bytes, true); });
+}
+
+int32_t clb_bank_geometry(const clb_bank* bank, int32_t* n_layers, int32_t* n_experts, int32_t* dim, int32_t* ff) {
+    if (!bank) return CLB_E_INVALID;
+    if (n_layers) *n_layers = bank->cfg.n_layers;
+    if (n_experts) *n_experts = bank->cfg.n_experts;
+    if (dim) *dim = bank->cfg.dim;
+    if (ff) *ff = bank->cfg.ff;
+    return CLB_OK;
+}
+
+int32_t clb_bank_load_strata_pack(clb_bank* bank, const clb_strata_pack* pack, uint32_t first_layer, clb_error_v1* err) {
+    if (!bank || !pack) return fail(err, CLB_E_INVALID, "null bank/pack");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
     return guarded(err, [&] {
         bank->check_usable();
         const auto& c = bank->cfg;
-        require(layer < (uint32_t)c.n_layers && expert >= 0 && expert < c.n_experts && role >= 0 && role <= 2,
-                CLB_E_INVALID, "matrix address out of range");
-        require(bank->owns(expert), CLB_E_INVALID, "expert %d outside this bank's owned range", expert);
-        require(bank->placed[(size_t)layer * bank->E() + (size_t)expert], CLB_E_INVALID,
-                "expert (%u, %d) is not placed on this bank", layer, expert);
-        require(clb_type_supported(type), CLB_E_UNSUPPORTED, "quant type %d has no kernel", type);
-        const int n = role == 2 ? c.dim : c.ff, k = role == 2 ? c.ff : c.dim;
-        require(ggml && bytes == (size_t)n * (k / 256) * clb_block_bytes(type), CLB_E_INVALID,
-                "matrix byte extent %zu does not match [%d, %d] of type %d", bytes, n, k, type);
-        auto& d = bank->desc[(size_t)layer * bank->E() + (size_t)expert];
-        const PackedMat& cur = role == 0 ? d.gate : role == 1 ? d.up : d.down;
-        require(cur.body == nullptr, CLB_E_INVALID, "matrix already loaded");
-        DeviceGuard g(c.device);
-        bank->device_step([&] {
-            const PackedLayout l = clb_packed_layout(type, n, k);
-            uint8_t* packed = bank->dev_alloc<uint8_t>(l.total);
-            void* staging = nullptr;
-            cuda_check(cudaMalloc(&staging, bytes), "staging alloc");
-            int bad = 0;
-            cudaError_t e = cudaMemcpyAsync(staging, ggml, bytes, cudaMemcpyHostToDevice, bank->stream);
-            if (e == cudaSuccess) e = cudaMemsetAsync(bank->d_err, 0, sizeof(int), bank->stream);
-            if (e == cudaSuccess)
-                e = clb::launch_pack(static_cast<const uint8_t*>(staging), packed, l, type, n, k, bank->d_err,
-                                     bank->stream);
-            if (e == cudaSuccess) e = cudaMemcpyAsync(&bad, bank->d_err, sizeof(int), cudaMemcpyDeviceToHost, bank->stream);
-            if (e == cudaSuccess) e = cudaStreamSynchronize(bank->stream);
-            cudaFree(staging);
-            cuda_check(e, "matrix upload/pack");
-            if (bad) {
-                cuda_check(cudaMemsetAsync(bank->d_err, 0, sizeof(int), bank->stream), "flag reset");
-                throw Error(CLB_E_NONFINITE, "non-finite fp16 super-scale in matrix");
+        auto geo = [&](const char* key, long want) {
+            const std::string v = clb::pack_meta(pack, key);
+            require(v.empty() || std::strtol(v.c_str(), nullptr, 10) == want, CLB_E_INVALID,
+                    "pack %s = %s, the bank has %ld", key, v.c_str(), want);
+        };
+        geo("hidden_size", c.dim);
+        geo("moe_intermediate_size", c.ff);
+        geo("n_routed_experts", c.n_experts);
+        const std::string nh = clb::pack_meta(pack, "num_hidden_layers");
+        require(nh.empty() || (long)first_layer + c.n_layers <= std::strtol(nh.c_str(), nullptr, 10), CLB_E_INVALID,
+                "pack has %s layers, the bank spans %u..%u", nh.c_str(), first_layer, first_layer + c.n_layers - 1);
+        const std::string lim = clb::pack_meta(pack, "swiglu_limit");
+        require(lim.empty() || std::strtof(lim.c_str(), nullptr) == c.limit, CLB_E_INVALID,
+                "pack swiglu_limit %s differs from the bank's %g", lim.c_str(), (double)c.limit);
+        static const char* roles[3] = {"w1", "w3", "w2"};  // gate, up, down (cpu_lane.hpp:36)
+        std::vector<uint8_t> buf;
+        size_t loaded = 0;
+        for (int l = 0; l < c.n_layers; ++l)
+            for (int e = 0; e < c.n_experts; ++e) {
+                if (!bank->placed[(size_t)l * bank->E() + (size_t)e]) continue;
+                for (int role = 0; role < 3; ++role) {
+                    const std::string name = "layers." + std::to_string(first_layer + (uint32_t)l) + ".ffn.experts." +
+                                             std::to_string(e) + "." + roles[role] + ".weight";
+                    const clb::PackTensor* t = clb::pack_find(pack, name);
+                    require(t != nullptr, CLB_E_INVALID, "missing tensor %s", name.c_str());
+                    const int type = clb::pack_expert_type(t->dtype);
+                    require(type != 0, CLB_E_UNSUPPORTED, "%s: unadmitted dtype %s", name.c_str(), t->dtype.c_str());
+                    const long n = role == 2 ? c.dim : c.ff, k = role == 2 ? c.ff : c.dim;
+                    require(t->shape.size() < 2 || (t->shape[0] == n && t->shape[1] == k), CLB_E_INVALID,
+                            "%s: shape %lld x %lld, expected %ld x %ld", name.c_str(),
+                            (long long)(t->shape.size() ? t->shape[0] : 0), (long long)(t->shape.size() > 1 ? t->shape[1] : 0),
+                            n, k);
+                    buf.resize((size_t)t->bytes);
+                    clb::pack_read(pack, *t, 0, buf.data(), t->bytes);
+                    load_matrix_locked(bank, (uint32_t)l, e, role, type, buf.data(), buf.size(), false);
+                    ++loaded;
+                }
             }
-            bank->weight_bytes += l.total;
-            bank->set_matrix(layer, expert, role, type, packed);
-            bank->refresh_resident(layer, expert);
-            bank->upload_desc();
-        });
+        if (loaded) {
+            DeviceGuard g(c.device);
+            bank->device_step([&] { bank->upload_desc(); });
+        }
     });
 }
 

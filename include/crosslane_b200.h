@@ -137,6 +137,35 @@ int32_t clb_bank_fill_synthetic(clb_bank* bank, uint64_t seed, int32_t type_poli
 int32_t clb_bank_load_matrix(clb_bank* bank, uint32_t layer, int32_t expert, int32_t role, int32_t type,
                              const void* ggml, size_t bytes, clb_error_v1* err);
 
+/* ---- Strata pack ingestion (crosslane's index over the model's GGUF shards) ----
+ * A pack is <dir>/ds4.txt ("key value" lines: model_dir, format, geometry) and
+ * <dir>/tensors.txt ("file <i> <shard>", "t <name> <dtype> <file> <offset> <bytes> <shape...>")
+ * (weight_source.hpp:1-5; pack_source.cpp:144-185); a relative model_dir is taken
+ * relative to <dir>. Expert matrices are layers.<l>.ffn.experts.<e>.w{1,3,2}.weight (gate,
+ * up, down) in ggml block bytes. No GPU is involved in opening or reading a pack. */
+typedef struct clb_strata_pack clb_strata_pack;
+/* Opens a pack: the reference's checks (model_dir present, format "gguf", well-formed and
+ * unique tensor lines, no shard gap, every extent inside its shard). */
+int32_t clb_strata_pack_open(const char* dir, clb_strata_pack** out, clb_error_v1* err);
+void clb_strata_pack_close(clb_strata_pack* pack);
+/* ds4.txt value of `key` into value[cap] (NUL-terminated); CLB_E_INVALID if absent / too long. */
+int32_t clb_strata_pack_meta(const clb_strata_pack* pack, const char* key, char* value, size_t cap);
+/* dtype (as tensors.txt spells it), byte size and shape of tensor `name`; CLB_E_INVALID if absent. */
+int32_t clb_strata_pack_tensor(const clb_strata_pack* pack, const char* name, char* dtype, size_t dtype_cap, uint64_t* bytes,
+                        int64_t* shape, int32_t shape_cap, int32_t* ndim);
+/* bytes of tensor `name` from byte `offset` into dst (pread semantics, thread-safe). */
+int32_t clb_strata_pack_read(const clb_strata_pack* pack, const char* name, uint64_t offset, void* dst, uint64_t bytes,
+                      clb_error_v1* err);
+/* Loads every matrix placed on the bank (owned range or placement) from the pack's layers
+ * first_layer .. first_layer + n_layers - 1 (bank layer l <- pack layer first_layer + l),
+ * repacking them into the HBM layout. Checks the pack's hidden_size, moe_intermediate_size,
+ * n_routed_experts, num_hidden_layers and swiglu_limit against the bank, each expert dtype
+ * (IQ2_XXS / IQ2_XS / IQ1_M, else CLB_E_UNSUPPORTED) and shape. Replaces the file half of
+ * HipResidentBank::load (hip_resident_bank.hpp:97-136) over crosslane's WeightSource. */
+int32_t clb_bank_load_strata_pack(clb_bank* bank, const clb_strata_pack* pack, uint32_t first_layer, clb_error_v1* err);
+/* The bank's geometry. */
+int32_t clb_bank_geometry(const clb_bank* bank, int32_t* n_layers, int32_t* n_experts, int32_t* dim, int32_t* ff);
+
 /* Device bytes held by expert matrices (sum of packed sizes). */
 uint64_t clb_bank_weight_bytes(const clb_bank* bank);
 /* 1 when stack decode runs as the persistent kernel, 0 for the per-layer kernels
