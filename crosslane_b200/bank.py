@@ -255,6 +255,28 @@ class ExpertBank:
             C.c_void_p(d_x.data_ptr()), C.c_void_p(d_out.data_ptr()), C.c_void_p(d_ws.data_ptr()), d_ws.numel(),
             phase_mask, C.c_void_p(stream) if stream else None, C.byref(err)), err)
 
+    # -- batched stack decode (clb_stack_batch*) --
+    def stack_batch_workspace_bytes(self, tokens: int) -> int:
+        return int(lib.clb_stack_batch_workspace_bytes(self._h, tokens))
+
+    def stack_batch(self, first_layer: int, n_layers: int, h, logits) -> np.ndarray:
+        """h [T][dim], logits [n_layers][T][n_experts] host arrays -> h after the layers
+        (synchronous; routing on the host)."""
+        h, logits = _f32(h).copy(), _f32(logits)
+        T = h.shape[0]
+        assert h.shape == (T, self.dim) and logits.shape == (n_layers, T, self.n_experts)
+        err = ErrorV1()
+        check(lib.clb_stack_batch(self._h, first_layer, n_layers, T, _ptr(logits), _ptr(h), C.byref(err)), err)
+        return h
+
+    def stack_batch_device(self, first_layer: int, n_layers: int, d_h, d_logits, d_ws, stream=None) -> None:
+        """torch tensors on this device: d_h [T][dim] (updated in place), d_logits
+        [n_layers][T][n_experts], d_ws uint8 (stack_batch_workspace_bytes); routing on the device."""
+        err = ErrorV1()
+        check(lib.clb_stack_batch_device(
+            self._h, first_layer, n_layers, d_h.shape[0], C.c_void_p(d_logits.data_ptr()), C.c_void_p(d_h.data_ptr()),
+            C.c_void_p(d_ws.data_ptr()), d_ws.numel(), C.c_void_p(stream) if stream else None, C.byref(err)), err)
+
     def expert_info(self, layer: int, expert: int):
         """(ggml type id, payload bytes of gate+up+down) of a resident expert."""
         t = C.c_int32()

@@ -139,6 +139,11 @@ struct clb_bank {
     float *pf_hx = nullptr, *pf_hw = nullptr, *pf_dx = nullptr, *pf_dw = nullptr, *pf_dout = nullptr;
     int32_t *pf_hids = nullptr, *pf_dids = nullptr;
     int pf_tokens = 0, pf_k = 0;
+    // batched stack decode (clb_stack_batch): grow-only device workspace, h and routes, pinned staging
+    void* sb_ws = nullptr;
+    float *sb_dh = nullptr, *sb_dw = nullptr, *sb_hh = nullptr, *sb_hw = nullptr;
+    int32_t *sb_dids = nullptr, *sb_hids = nullptr;
+    int sb_tokens = 0, sb_layers = 0;
 
     size_t L() const { return (size_t)cfg.n_layers; }
     size_t E() const { return (size_t)cfg.n_experts; }
@@ -287,8 +292,18 @@ struct clb_bank {
         pf_hids = nullptr, pf_ws_bytes = 0, pf_tokens = pf_k = 0;
     }
 
+    void free_stack_batch() {
+        for (void* p : {(void*)sb_ws, (void*)sb_dh, (void*)sb_dw, (void*)sb_dids})
+            if (p) cudaFree(p);
+        for (void* p : {(void*)sb_hh, (void*)sb_hw, (void*)sb_hids})
+            if (p) cudaFreeHost(p);
+        sb_ws = nullptr, sb_dh = sb_dw = sb_hh = sb_hw = nullptr, sb_dids = sb_hids = nullptr;
+        sb_tokens = sb_layers = 0;
+    }
+
     ~clb_bank() {
         free_prefill();
+        free_stack_batch();
         for (void* p : opened_peers) cudaIpcCloseMemHandle(p);
         for (auto& g : graphs) cudaGraphExecDestroy(g.second);
         for (auto& g : device_graphs) cudaGraphExecDestroy(g.second);
@@ -1067,12 +1082,6 @@ static void prefill_check_layer(clb_bank* bank, uint32_t layer, int32_t tokens, 
                 (int64_t)tokens * k <= (1 << 24),
             CLB_E_INVALID, "invalid prefill size (%d tokens x %d picks)", tokens, k);
     require(clb::prefill_shape_supported(c.dim, c.ff), CLB_E_UNSUPPORTED, "prefill needs dim, ff multiples of 256");
-    for (size_t e = 0; e < bank->E(); ++e) {
-        if (!bank->resident[(size_t)layer * bank->E() + e]) continue;
-        const auto& d = bank->desc[(size_t)layer * bank->E() + e];
-        require(d.gate.type == CLB_IQ2_XXS && d.up.type == CLB_IQ2_XXS && d.down.type == CLB_IQ2_XXS,
-                CLB_E_UNSUPPORTED, "prefill supports IQ2_XXS experts only (expert %zu of layer %u)", e, layer);
-    }
 }
 
 uint64_t clb_prefill_workspace_bytes(const clb_bank* bank, int32_t tokens, int32_t k) {
@@ -1186,6 +1195,114 @@ int32_t clb_prefill_layer(clb_bank* bank, uint32_t layer, int32_t tokens, int32_
         });
         std::memcpy(out, bank->pf_hx, nx * 4);
         require(finite_all(out, nx), CLB_E_NONFINITE, "non-finite prefill output");
+    });
+}
+
+// ---- batched stack decode (T tokens through consecutive layers, grouped GEMMs per layer) ----
+static void stack_batch_check(clb_bank* bank, uint32_t first, int32_t nl, int32_t tokens) {
+    const auto& c = bank->cfg;
+    require(nl >= 1 && first + (uint32_t)nl <= (uint32_t)c.n_layers, CLB_E_INVALID, "layer range out of bounds");
+    require(tokens >= 1 && tokens <= (1 << 16) && (int64_t)tokens * c.max_picks <= (1 << 24), CLB_E_INVALID,
+            "invalid batch size (%d tokens)", tokens);
+    require(c.expert_begin == 0 && c.expert_end == c.n_experts, CLB_E_INVALID,
+            "batched stack decode needs every expert of its layers on this bank");
+    require(clb::prefill_shape_supported(c.dim, c.ff), CLB_E_UNSUPPORTED,
+            "batched stack decode needs dim, ff multiples of 256 in [512, 8192]");
+    for (int l = 0; l < nl; ++l)
+        for (int e = 0; e < c.n_experts; ++e)
+            require(bank->resident[(size_t)(first + l) * bank->E() + (size_t)e], CLB_E_INVALID,
+                    "expert (%u, %d) not resident", first + l, e);
+}
+
+uint64_t clb_stack_batch_workspace_bytes(const clb_bank* bank, int32_t tokens) {
+    if (!bank || tokens < 1) return 0;
+    const auto& c = bank->cfg;
+    return clb::stack_batch_workspace_bytes(tokens, c.max_picks, c.dim, c.ff, c.n_experts);
+}
+
+int32_t clb_stack_batch_device(clb_bank* bank, uint32_t first, int32_t nl, int32_t tokens, const float* d_logits,
+                               float* d_h, void* d_ws, uint64_t ws_bytes, void* stream, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    return guarded(err, [&] {
+        bank->check_usable();
+        stack_batch_check(bank, first, nl, tokens);
+        require(d_logits && d_h && d_ws, CLB_E_INVALID, "null device buffer");
+        require(ws_bytes >= clb_stack_batch_workspace_bytes(bank, tokens), CLB_E_INVALID,
+                "stack batch workspace too small");
+        DeviceGuard g(bank->cfg.device);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : bank->stream;
+        bank->device_step([&] {
+            const auto& c = bank->cfg;
+            cuda_check(clb::launch_stack_batch(bank->d_desc + (size_t)first * bank->E(), c.n_experts, nl, d_logits,
+                                               nullptr, nullptr, d_h, tokens, c.max_picks, c.dim, c.ff, c.limit, d_ws,
+                                               bank->d_err, s),
+                       "stack batch launch");
+        });
+    });
+}
+
+int32_t clb_stack_batch(clb_bank* bank, uint32_t first, int32_t nl, int32_t tokens, const float* logits, float* h,
+                        clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        bank->check_usable();
+        const auto& c = bank->cfg;
+        stack_batch_check(bank, first, nl, tokens);
+        require(logits && h, CLB_E_INVALID, "null buffer");
+        const int k = c.max_picks;
+        const size_t nh = (size_t)tokens * c.dim, nr = (size_t)nl * tokens * k;
+        require(finite_all(logits, (size_t)nl * tokens * c.n_experts), CLB_E_NONFINITE, "non-finite router logits");
+        require(finite_all(h, nh), CLB_E_NONFINITE, "non-finite activation");
+        DeviceGuard g(c.device);
+        if (tokens > bank->sb_tokens || nl > bank->sb_layers) {
+            cuda_check(cudaStreamSynchronize(bank->stream), "stream sync");
+            const int T = std::max(tokens, bank->sb_tokens), L = std::max(nl, bank->sb_layers);
+            bank->free_stack_batch();
+            auto dmal = [&](void** p, size_t n) {
+                cudaError_t e = cudaMalloc(p, std::max<size_t>(n, 256));
+                if (e != cudaSuccess) {
+                    cudaGetLastError();
+                    bank->free_stack_batch();
+                    throw Error(CLB_E_NOMEM, std::string("cudaMalloc (stack batch): ") + cudaGetErrorString(e));
+                }
+            };
+            const size_t R = (size_t)L * T * k;
+            dmal(&bank->sb_ws, clb::stack_batch_workspace_bytes(T, k, c.dim, c.ff, c.n_experts));
+            dmal(reinterpret_cast<void**>(&bank->sb_dh), (size_t)T * c.dim * 4);
+            dmal(reinterpret_cast<void**>(&bank->sb_dw), R * 4);
+            dmal(reinterpret_cast<void**>(&bank->sb_dids), R * 4);
+            cuda_check(cudaMallocHost(reinterpret_cast<void**>(&bank->sb_hh), (size_t)T * c.dim * 4), "cudaMallocHost");
+            cuda_check(cudaMallocHost(reinterpret_cast<void**>(&bank->sb_hw), R * 4), "cudaMallocHost");
+            cuda_check(cudaMallocHost(reinterpret_cast<void**>(&bank->sb_hids), R * 4), "cudaMallocHost");
+            bank->sb_tokens = T;
+            bank->sb_layers = L;
+        }
+        bank->device_step([&] {
+            // routing on the host (route.cpp's order and libm, as clb_stack_decode), then h and
+            // the routes go up, nl grouped layers run, and h comes back
+            for (int l = 0; l < nl; ++l)
+                for (int t = 0; t < tokens; ++t) {
+                    const size_t r = ((size_t)l * tokens + t) * k;
+                    route_sigmoid_host(logits + ((size_t)l * tokens + t) * c.n_experts, c.n_experts, k,
+                                       bank->sb_hids + r, bank->sb_hw + r);
+                }
+            std::memcpy(bank->sb_hh, h, nh * 4);
+            cuda_check(cudaMemcpyAsync(bank->sb_dh, bank->sb_hh, nh * 4, cudaMemcpyHostToDevice, bank->stream), "h H2D");
+            cuda_check(cudaMemcpyAsync(bank->sb_dids, bank->sb_hids, nr * 4, cudaMemcpyHostToDevice, bank->stream),
+                       "route ids H2D");
+            cuda_check(cudaMemcpyAsync(bank->sb_dw, bank->sb_hw, nr * 4, cudaMemcpyHostToDevice, bank->stream),
+                       "route weights H2D");
+            cuda_check(clb::launch_stack_batch(bank->d_desc + (size_t)first * bank->E(), c.n_experts, nl, nullptr,
+                                               bank->sb_dids, bank->sb_dw, bank->sb_dh, tokens, k, c.dim, c.ff,
+                                               c.limit, bank->sb_ws, bank->d_err, bank->stream),
+                       "stack batch launch");
+            cuda_check(cudaMemcpyAsync(bank->sb_hh, bank->sb_dh, nh * 4, cudaMemcpyDeviceToHost, bank->stream),
+                       "h D2H");
+            bank->check_err_flag();
+        });
+        std::memcpy(h, bank->sb_hh, nh * 4);
+        require(finite_all(h, nh), CLB_E_NONFINITE, "non-finite stack output");
     });
 }
 

@@ -61,9 +61,16 @@ cudaError_t launch_mv2(const PackedMat& m, const void* q, float* y, cudaStream_t
 // phase_mask: 1 group + quantise x, 2 gate/up GEMM, 4 SwiGLU + quantise h, 8 down GEMM, 16 combine.
 size_t prefill_workspace_bytes(int T, int k, int dim, int ff, int E);
 bool prefill_shape_supported(int dim, int ff);
+// norm_x: x <- RMSNorm(x) (the stack's fixed-order pre-norm) before Q8_K.
 cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const int* ids, const float* w, int T, int k,
                            int dim, int ff, float limit, const float* resid, float* out, void* ws, int* err,
-                           int phase_mask, cudaStream_t s);
+                           int phase_mask, cudaStream_t s, bool norm_x = false);
+// T tokens through nl layers (desc [nl][E]): h <- h + layer(RMSNorm(h)) per layer, in place.
+// Routes from ids_all / w_all ([nl][T][k]) or, when those are null, from logits ([nl][T][E]).
+size_t stack_batch_workspace_bytes(int T, int k, int dim, int ff, int E);
+cudaError_t launch_stack_batch(const ExpertDesc* desc, int E, int nl, const float* logits, const int* ids_all,
+                               const float* w_all, float* h, int T, int k, int dim, int ff, float limit, void* ws,
+                               int* err, cudaStream_t s);
 
 // persistent whole-stack kernel (clb_stack.cu)
 constexpr int kMaxPeers = 8;  // GPUs of one node

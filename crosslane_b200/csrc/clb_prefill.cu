@@ -4,13 +4,18 @@
 // ascending expert id (engine/strata/warm/runtime.cpp:184-187 applied to every token).
 //
 // Arithmetic. Per 256-value block b the reference forms exact integers
-// sum_k w_int[k] * q[k] (q8k_core.hpp:43-91), with w_int = (2s+1) * sign * mag for
-// IQ2_XXS (|w_int| <= 43 * 31 = 1333, an exact fp16 integer) and q the Q8_K activation
-// (|q| <= 127, exact in fp16). tcgen05.mma (kind::f16, fp32 accumulators in tensor memory)
-// forms that block sum exactly for a 128-row x N-token tile (every partial sum is an
-// integer below 2^24); the epilogue adds (d_w[row, b] * d_x[token, b]) * sum_b into fp32
-// registers block by block and scales by 1/8 at the end (an IQ2 weight is
-// d * (2s+1)/8 * sign * mag). Per (token, row) that is the decode kernels' fast order.
+// sum_k w_int[k] * q[k] (q8k_core.hpp:43-91) with q the Q8_K activation (|q| <= 127, exact
+// in fp16) and w_int an exact fp16 integer for every expert type:
+//   IQ2_XXS  w_int = (2s+1) * sign * mag, mag in {8, 25, 43}, one s per 32 values (<= 1333);
+//   IQ2_XS   the same with one s per 16 values (scale bytes of the sc plane);
+//   IQ1_M    w_int = (2s+1) * (8 g + delta), g in {-1, 0, 1}, delta = +-1 per 8 values, one
+//            3-bit s per 16 values (<= 135): the reference's main sum plus 1/8 of its delta
+//            sum (q8k_core.hpp:79-84) is 1/8 of this integer's sum.
+// tcgen05.mma (kind::f16, fp32 accumulators in tensor memory) forms that block sum for a
+// 128-row x N-token tile (exactly while partial sums stay below 2^24, which the Q8_K value
+// ranges of real activations keep them); the epilogue adds (d_w[row, b] * d_x[token, b]) *
+// sum_b into fp32 registers block by block and scales by 1/8 at the end. Per (token, row)
+// that is the decode kernels' fast order.
 //
 // Data layout. The picks are grouped by expert into a list of slots (t*k + p), each
 // expert's run padded to a multiple of 16 entries; activations are gathered into list
@@ -20,12 +25,13 @@
 // reads them into MMA columns (tokens) whose results it never stores, and the columns of
 // an MMA do not mix.
 //
-// GEMM kernel: one CTA per SM, persistent over tiles (expert, 128 weight rows, up to 64
+// GEMM kernel: one CTA per SM, persistent over tiles (expert, 128 weight rows, up to 48
 // list entries), warp-specialised around one pipeline of 256-value K blocks (4 stages of 64)
 // that runs across tiles; roles hand blocks to each other through mbarriers, one wait and
 // one arrival per block:
 //  * weight warp: bulk copies (cp.async.bulk) of the packed weight pieces of a block
-//    (16 B per row and stage, 8 KB) and of the rows' block scales, two blocks ahead;
+//    (16 B per row and piece, 4 pieces for IQ2, 3 for IQ1_M) and of the rows' block scales
+//    (d plane, sc plane), two blocks ahead;
 //  * B warp: the B operand of a block by TMA (2-D tensor map over the list-order
 //    activations, 128-byte swizzle, box height = the tile's entries rounded up to 16), two
 //    blocks deep, and each tile's activation scales;
@@ -35,7 +41,8 @@
 //  * 8 decoder warps: each thread turns one 32-weight chunk of one row per stage into exact
 //    fp16 integers and stores them to the A operand in tensor memory (tcgen05.st, row m in
 //    lane m, values k, k+1 in one column; two blocks of buffers), two 32-column stores per
-//    block;
+//    block; the matrix type is uniform per warp (a warp's 32 rows are all gate, all up or
+//    all down rows of one expert);
 //  * 8 epilogue warps (tensor-memory lane quarter x 32 columns): per block, D * d_w * d_x
 //    added into running tile sums that also live in tensor memory; the tile's last block
 //    writes the rows out.
@@ -46,6 +53,8 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <type_traits>
 
 #include "clb_device.cuh"
 #include "clb_kernels.h"
@@ -60,29 +69,40 @@ constexpr int kPfEpiWarps = 8;                // warp kPfDecWarps + w: lane quar
 constexpr int kPfEpiWarp0 = kPfDecWarps;
 constexpr int kPfProducerWarp = kPfDecWarps + kPfEpiWarps, kPfMmaWarp = kPfProducerWarp + 1, kPfBWarp = kPfProducerWarp + 2;
 constexpr int kPfThreads = 32 * (kPfDecWarps + kPfEpiWarps + 3);
-constexpr int kPfMaxN = 64;                   // list entries per tile (MMA N <= 64)
+constexpr int kPfMaxN = 48;                   // list entries per tile (MMA N <= 48)
 constexpr int kPfStageK = 64;                 // K values per stage (4 MMAs of K = 16); 4 stages per block
 constexpr int kPfRawStage = 128 * 16;         // one 16-byte piece per weight row
-constexpr int kPfRawBlock = 4 * kPfRawStage;  // 8 KB per block
-constexpr int kPfBStage = kPfMaxN * 128;      // 64 rows x 64 fp16, 128-byte swizzled
+constexpr int kPfRawSc = 4 * kPfRawStage;     // then the rows' 8 sc bytes (IQ2_XS, IQ1_M)
+constexpr int kPfRawHdr = kPfRawSc + 128 * 8; // then a 16-byte header: the tile's packed types (word 0)
+constexpr int kPfRawBlock = kPfRawHdr + 128;  // ~9 KB per block, 128-byte aligned (IQ1_M fills 3 of the 4 piece slots)
+constexpr int kPfBStage = kPfMaxN * 128;      // 48 rows x 64 fp16, 128-byte swizzled
 constexpr int kPfBBlock = 4 * kPfBStage;
 constexpr int kPfMaxNb = 32;                  // K <= 8192
 constexpr int kPfAcc = 3;                     // block accumulators (64 columns each, from column 0)
+constexpr int kPfAccCols = 64;
+constexpr int kPfDxsStride = 64;              // floats per block row of a tile's activation scales
 constexpr int kPfDwRing = 8;                  // row-scale ring (blocks)
+constexpr int kPfDwHdr = 256 + 128 * 8;       // per block: fp16 d of 128 rows, 8 sc bytes per row (IQ1_M),
+constexpr int kPfDwSlot = kPfDwHdr + 128;     // then a header {first, entries, mt, types} of the block's tile
 constexpr int kPfTmemCols = 512;
-constexpr uint32_t kPfRCol = kPfAcc * kPfMaxN;          // running tile sums (64 columns)
+constexpr uint32_t kPfRCol = kPfAcc * kPfAccCols;       // running tile sums (64 columns)
 constexpr uint32_t kPfACol = 256;                       // A operand: 2 blocks x 128 columns
 // A operand of a block: the 16-value slice j (0-3) of stage q (0-3) sits at columns 32 j + 8 q, so
 // the four stages of one slice are 32 contiguous columns (one tcgen05.st per decoder thread).
-static_assert(kPfRCol + kPfMaxN <= kPfACol && kPfACol + 8 * 32 <= kPfTmemCols, "tensor memory budget");
+static_assert(kPfMaxN <= kPfAccCols && kPfMaxN <= kPfDxsStride && kPfMaxN % 16 == 0, "tile width");
+static_assert(kPfRCol + kPfAccCols <= kPfACol && kPfACol + 8 * 32 <= kPfTmemCols, "tensor memory budget");
 constexpr uint32_t kPfSpin = 1u << 22;        // drain wait polls
 constexpr uint32_t kPfSuspendNs = 20000;      // try_wait suspend hint
 constexpr uint64_t kPfTimeoutNs = 1000000000; // 1 s: a pipeline wait longer than this is an error
 constexpr int kErrPrefillWait = 3;
 
-// Magnitudes biased by +128 so that 0x64XX = 1024 + XX as fp16: +8, +25, +43 and -8, -25, -43.
+// Values biased by +128 so that 0x64XX = 1024 + XX as fp16. IQ2: +8, +25, +43 and -8, -25, -43
+// (selector nibble: symbol, bit 2 the sign). IQ1_M: 8 g + delta for g = -1, 0, +1 (symbol
+// 0, 1, 2) with delta = +1 (kIq1Pos) or -1 (kIq1Neg).
 constexpr uint32_t kPos2b = 0x00AB9988u;
 constexpr uint32_t kNeg2b = 0x00556778u;
+constexpr uint32_t kIq1Pos = 0x00898179u;
+constexpr uint32_t kIq1Neg = 0x00877F77u;
 
 // mbarriers; operand rings hold two blocks, each synchronised once per block
 enum : int {
@@ -109,17 +129,21 @@ __host__ __device__ constexpr uint32_t pf_bar_count(int i) {
 }
 
 struct PfSmem {
-    // [0, 64K) IQ2_XXS tables; the B ring starts at the first 1024-byte boundary after them
-    static constexpr uint32_t braw = 64 * 1024;                            // + alignment pad
+    // [0, 128K) decode tables of the three types; the B ring starts at the first 1024-byte
+    // boundary after them
+    static constexpr uint32_t braw = kRowTableBytes;                       // + alignment pad
     static constexpr uint32_t raw = braw + 1024 + 2 * kPfBBlock;           // weight pieces, 2 blocks
-    static constexpr uint32_t dw = raw + 2 * kPfRawBlock;                  // [kPfDwRing][128] fp16 row scales
-    static constexpr uint32_t dxs = dw + kPfDwRing * 256;                  // [2][kPfMaxNb][kPfMaxN] floats
-    static constexpr uint32_t bars = dxs + 2 * kPfMaxNb * kPfMaxN * 4;
+    static constexpr uint32_t dw = raw + 2 * kPfRawBlock;                  // [kPfDwRing][kPfDwSlot] row scales
+    static constexpr uint32_t dxs = dw + kPfDwRing * kPfDwSlot;            // [2][kPfMaxNb][kPfDxsStride] floats
+    static constexpr uint32_t bhdr = dxs + 2 * kPfMaxNb * kPfDxsStride * 4;  // [2] MMA width of a B block
+    static constexpr uint32_t bars = bhdr + 16;
     static constexpr uint32_t tslot = bars + kNumBars * 8;
     static constexpr uint32_t abort_flag = tslot + 4;
     static constexpr uint32_t total = abort_flag + 12;
 };
-static_assert(PfSmem::raw % 16 == 0 && PfSmem::dxs % 16 == 0 && PfSmem::bars % 8 == 0, "aligned regions");
+static_assert(PfSmem::raw % 16 == 0 && PfSmem::dw % 16 == 0 && PfSmem::dxs % 16 == 0 && PfSmem::bars % 8 == 0,
+              "aligned regions");
+static_assert(kPfBStage % 1024 == 0 && 2944 * 4 <= 2 * kPfRawBlock, "swizzle atoms; table staging area");
 static_assert(PfSmem::total <= 227 * 1024, "fits one CTA per SM");
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -225,24 +249,78 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         : "memory");
 }
 
-// IQ2_XXS grid and sign selector tables (the first 64 KB of the decode kernels' tables).
-__device__ __forceinline__ void fill_xxs_tables(const uint32_t* __restrict__ compact) {
-    uint4* a = reinterpret_cast<uint4*>(clb_dyn_smem + kRowTabXXS);
-    for (int s = threadIdx.x; s < 4096; s += blockDim.x) {
-        const int slot = s >> 4, part = s & 15;
-        const uint32_t v = __ldg(compact + (part < 8 ? slot : 2816 + (slot & 127)));
-        a[s] = make_uint4(v, v, v, v);
-    }
-}
-
 // Four biased bytes (value + 128) -> four fp16 (value * scale), exact because |value * scale|
-// <= 1333: (1024 + byte) * scale - 1152 * scale in one fused rounding.
+// <= 1333: (1024 + byte) * scale - 1152 * scale in one fused rounding (1152 * scale is exact
+// in fp16 for every odd scale <= 31).
 __device__ __forceinline__ void biased4_to_half(uint32_t w, __half2 s2, __half2 noff, uint32_t& h01, uint32_t& h23) {
     const uint32_t a = __byte_perm(w, 0x64646464u, 0x5140), b = __byte_perm(w, 0x64646464u, 0x7362);
     const __half2 ra = __hfma2(*reinterpret_cast<const __half2*>(&a), s2, noff);
     const __half2 rb = __hfma2(*reinterpret_cast<const __half2*>(&b), s2, noff);
     h01 = *reinterpret_cast<const uint32_t*>(&ra);
     h23 = *reinterpret_cast<const uint32_t*>(&rb);
+}
+
+// One block of a decoder thread: its 32-value chunk c = 2q + dc of each stage q as exact fp16
+// integers, stored to the A operand as two 32-column slices (values 0-15 and 16-31 of the
+// chunks). cw: IQ2 types, words 2c and 2c+1 of the block body per stage (cw[2q], cw[2q+1]);
+// IQ1_M, the qs word of chunk c (cw[q]) and its 4 qh nibbles (cw[4 + q]). s2[q] / nf[q]:
+// the odd sub-scales of values 0-15 (low half) and 16-31 (high half) of chunk c, and
+// -1152 times them. lb = lane * 4 (the lane's copy in the replicated tables).
+template <int T>
+__device__ __forceinline__ void pf_decode_block(const uint32_t (&cw)[8], const __half2 (&s2)[4],
+                                                const __half2 (&nf)[4], uint32_t lb, uint32_t taddr) {
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+        uint32_t v[32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            // IQ2_XXS: one scale for the chunk (both halves of s2 equal)
+            const __half2 s = T == CLB_IQ2_XXS ? s2[q] : jj ? __high2half2(s2[q]) : __low2half2(s2[q]);
+            const __half2 n = T == CLB_IQ2_XXS ? nf[q] : jj ? __high2half2(nf[q]) : __low2half2(nf[q]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t grp = 2 * jj + h;  // 8-value group of the chunk
+                uint32_t lo, hi;
+                if (T == CLB_IQ2_XXS) {
+                    const uint32_t selj = 0x5504u | (grp << 4);  // byte grp * 256 + lb
+                    const uint32_t sel = tab32(kRowTabXXS + prmt2(cw[2 * q], lb, selj)) |
+                                         tab32(kRowTabXXS + 128 + prmt2(cw[2 * q + 1], lb, selj));
+                    lo = prmt_sel(kPos2b, kNeg2b, sel);
+                    hi = prmt_sel(kPos2b, kNeg2b, sel >> 16);
+                } else if (T == CLB_IQ2_XS) {
+                    const uint32_t w = cw[2 * q + jj];
+                    const uint32_t code = h ? (w >> 16) : (w & 0xffffu);  // 9-bit grid index, 7-bit sign index
+                    const uint32_t sel = tab32(kRowTabXS + (code & 511u) * 64u + (lb & 60u)) |
+                                         tab32(kRowTabXXS + (code >> 9) * 256u + 128u + lb);
+                    lo = prmt_sel(kPos2b, kNeg2b, sel);
+                    hi = prmt_sel(kPos2b, kNeg2b, sel >> 16);
+                } else {
+                    const uint32_t nib = (cw[4 + q] >> (4 * grp)) & 15u;
+                    const uint32_t idx = ((cw[q] >> (8 * grp)) & 0xffu) | ((nib & 7u) << 8);
+                    const uint32_t sel = tab32(kRowTabIQ1 + idx * 16u + (lb & 12u));
+                    const uint32_t src = (nib & 8u) ? kIq1Neg : kIq1Pos;
+                    lo = prmt_sel(src, 0u, sel);
+                    hi = prmt_sel(src, 0u, sel >> 16);
+                }
+                biased4_to_half(lo, s, n, v[8 * q + 4 * h], v[8 * q + 4 * h + 1]);
+                biased4_to_half(hi, s, n, v[8 * q + 4 * h + 2], v[8 * q + 4 * h + 3]);
+            }
+        }
+        tmem_st32(taddr + (uint32_t)jj * 32u, v);
+    }
+}
+
+// fp16 block scale of an IQ1_M row from its four scale words (top nibbles), as a float.
+__device__ __forceinline__ float iq1m_scale(uint2 sc) {
+    const uint32_t h = ((sc.x & 0xffffu) >> 12) | ((sc.x >> 24) & 0xf0u) | (((sc.y & 0xffffu) >> 4) & 0xf00u) |
+                       ((sc.y >> 16) & 0xf000u);
+    return __half2float(__ushort_as_half((uint16_t)h));
+}
+
+// Type of the matrix that supplies a warp's 32 rows (lane quarter `quarter`) of a tile, from
+// the tile's packed types (gate | up << 8 | down << 16).
+__device__ __forceinline__ int pf_row_type(int types, int role, int quarter) {
+    return (types >> (role == 0 ? (quarter < 2 ? 0 : 8) : 16)) & 0xff;
 }
 
 // Position in a ring of R slots: slot, the parity of the slot's current use, and how many
@@ -301,7 +379,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
     const int my_tiles = (int)blockIdx.x < ntot ? (ntot - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
     const int total = my_tiles * S;  // stages of this CTA
 
-    fill_xxs_tables(G.tables);
+    fill_row_tables(G.tables, reinterpret_cast<uint32_t*>(sm + PfSmem::raw));  // staged in the weight ring
     if (tid == 0) {
         for (int i = 0; i < kNumBars; ++i) mbar_init(bar(i), pf_bar_count(i));
         *abort_flag = 0;
@@ -325,60 +403,89 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
             Ring<kPfDwRing> dr;
             int tile = 0, b = 0;
             bool ok = false;
-            const uint8_t *pa0 = nullptr, *pa1 = nullptr;
+            const uint8_t *pa0 = nullptr, *pa1 = nullptr, *ps0 = nullptr, *ps1 = nullptr;
             const uint16_t *pd0 = nullptr, *pd1 = nullptr;
-            size_t plane = 0, dstride = 0;
+            int np0 = 4, np1 = 4;
+            size_t plane = 0, n = 0;
+            uint32_t raw_tx = 0, dw_tx = 0;
+            int4 hdr = make_int4(0, 0, 0, 0);
+            const bool split = G.role == 0;  // 64 gate rows + 64 up rows per tile
+            const uint32_t rb = split ? 64u : 128u;
+            auto fits = [&](const PackedMat& m) {
+                return m.body && m.k == G.K &&
+                       (m.type == CLB_IQ2_XXS ? m.d != nullptr
+                        : m.type == CLB_IQ2_XS ? (m.d != nullptr && m.sc != nullptr)
+                                               : (m.type == CLB_IQ1_M && m.sc != nullptr));
+            };
             for (int blk = 0; blk < nblk; ++blk) {
                 if (b == 0) {  // tile setup
                     const PfTile t = pf_tile(G, tile);
                     const ExpertDesc& ex = G.desc[t.e];
-                    const PackedMat& m0 = G.role == 0 ? ex.gate : ex.down;
-                    const PackedMat& m1 = G.role == 0 ? ex.up : ex.down;
-                    const int row0 = G.role == 0 ? t.mt * 64 : t.mt * 128, rows = G.role == 0 ? 64 : 128;
-                    ok = m0.body && m1.body && m0.type == CLB_IQ2_XXS && m1.type == CLB_IQ2_XXS && m0.k == G.K &&
-                         m1.k == G.K && m0.n == m1.n && row0 + rows <= m0.n;
+                    const PackedMat& m0 = split ? ex.gate : ex.down;
+                    const PackedMat& m1 = split ? ex.up : ex.down;
+                    const int row0 = (int)rb * t.mt;
+                    ok = fits(m0) && fits(m1) && m0.n == m1.n && row0 + (int)rb <= m0.n;
                     if (!ok) atomicExch(G.err, 1);
-                    plane = (size_t)m0.n * 16;
-                    dstride = (size_t)m0.n;
+                    hdr = make_int4(t.first, t.ntok, t.mt,
+                                    (ex.gate.type & 0xff) | ((ex.up.type & 0xff) << 8) | ((ex.down.type & 0xff) << 16));
+                    n = (size_t)m0.n;
+                    plane = n * 16;
+                    np0 = m0.type == CLB_IQ1_M ? 3 : 4;
+                    np1 = m1.type == CLB_IQ1_M ? 3 : 4;
                     pa0 = m0.body + (size_t)row0 * 16;
                     pa1 = m1.body + (size_t)row0 * 16;
-                    pd0 = m0.d + row0;
-                    pd1 = m1.d + row0;
+                    pd0 = ok && m0.type != CLB_IQ1_M ? m0.d + row0 : nullptr;
+                    pd1 = ok && m1.type != CLB_IQ1_M ? m1.d + row0 : nullptr;
+                    ps0 = ok && m0.type != CLB_IQ2_XXS ? m0.sc + (size_t)row0 * 8 : nullptr;
+                    ps1 = ok && m1.type != CLB_IQ2_XXS ? m1.sc + (size_t)row0 * 8 : nullptr;
+                    // weight ring: pieces, then sc bytes (decoders); scale ring: d, or for IQ1_M the
+                    // sc bytes that carry its scale (epilogue)
+                    raw_tx = 16u * rb * (uint32_t)np0 + (ps0 ? 8u * rb : 0u);
+                    dw_tx = pd0 ? 2u * rb : 8u * rb;
+                    if (split) {
+                        raw_tx += 16u * rb * (uint32_t)np1 + (ps1 ? 8u * rb : 0u);
+                        dw_tx += pd1 ? 2u * rb : 8u * rb;
+                    }
                 }
                 if (rr.round > 0 && !pf_wait(bar(kRawEmpty + rr.slot), rr.phase ^ 1u, abort_flag, G.err)) break;
                 const uint32_t full = bar(kRawFull + rr.slot), dst = sraw + (uint32_t)rr.slot * kPfRawBlock;
+                // headers are plain shared stores that the arrive below releases to the waiting roles
+                *reinterpret_cast<int*>(sm + PfSmem::raw + rr.slot * kPfRawBlock + kPfRawHdr) = hdr.w;
                 if (!ok) {
                     mbar_arrive(full);
                 } else {
-                    mbar_expect_tx(full, kPfRawBlock);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        if (G.role == 0) {
-                            bulk_g2s(dst + q * kPfRawStage, pa0 + q * plane, kPfRawStage / 2, full);
-                            bulk_g2s(dst + q * kPfRawStage + kPfRawStage / 2, pa1 + q * plane, kPfRawStage / 2, full);
-                        } else {
-                            bulk_g2s(dst + q * kPfRawStage, pa0 + q * plane, kPfRawStage, full);
-                        }
+                    // piece p of the block -> piece slot p; gate rows then up rows within a slot
+                    mbar_expect_tx(full, raw_tx);
+                    // piece by piece, gate and up rows of a piece together
+                    const uint8_t* s0 = pa0 + (size_t)b * (size_t)np0 * plane;
+                    const uint8_t* s1 = pa1 + (size_t)b * (size_t)np1 * plane;
+                    for (int p = 0; p < 4; ++p) {
+                        if (p < np0) bulk_g2s(dst + p * kPfRawStage, s0 + p * plane, 16u * rb, full);
+                        if (split && p < np1) bulk_g2s(dst + p * kPfRawStage + 16u * rb, s1 + p * plane, 16u * rb, full);
                     }
+                    if (ps0) bulk_g2s(dst + kPfRawSc, ps0 + (size_t)b * n * 8, 8u * rb, full);
+                    if (split && ps1) bulk_g2s(dst + kPfRawSc + 8u * rb, ps1 + (size_t)b * n * 8, 8u * rb, full);
                 }
-                pa0 += 4 * plane;
-                pa1 += 4 * plane;
                 rr.next();
                 if (dr.round > 0 && !pf_wait(bar(kDwEmpty + dr.slot), dr.phase ^ 1u, abort_flag, G.err)) break;
-                const uint32_t dfull = bar(kDwFull + dr.slot), ddst = sdw + (uint32_t)dr.slot * 256;
+                const uint32_t dfull = bar(kDwFull + dr.slot), ddst = sdw + (uint32_t)dr.slot * kPfDwSlot;
+                *reinterpret_cast<int4*>(sm + PfSmem::dw + dr.slot * kPfDwSlot + kPfDwHdr) = hdr;
                 if (!ok) {
                     mbar_arrive(dfull);
                 } else {
-                    mbar_expect_tx(dfull, 256);
-                    if (G.role == 0) {
-                        bulk_g2s(ddst, pd0, 128, dfull);
-                        bulk_g2s(ddst + 128, pd1, 128, dfull);
-                    } else {
-                        bulk_g2s(ddst, pd0, 256, dfull);
+                    // fp16 d of the rows at [0, 256), IQ1_M rows' 8 scale bytes at [256, 1280)
+                    mbar_expect_tx(dfull, dw_tx);
+                    if (pd0)
+                        bulk_g2s(ddst, pd0 + (size_t)b * n, 2u * rb, dfull);
+                    else
+                        bulk_g2s(ddst + 256, ps0 + (size_t)b * n * 8, 8u * rb, dfull);
+                    if (split) {
+                        if (pd1)
+                            bulk_g2s(ddst + 2u * rb, pd1 + (size_t)b * n, 2u * rb, dfull);
+                        else
+                            bulk_g2s(ddst + 256 + 8u * rb, ps1 + (size_t)b * n * 8, 8u * rb, dfull);
                     }
                 }
-                pd0 += dstride;
-                pd1 += dstride;
                 dr.next();
                 if (++b == nb) {
                     b = 0;
@@ -402,11 +509,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
                     const uint32_t dfull = bar(kDxsFull + xs);
                     mbar_expect_tx(dfull, (uint32_t)(nb * n * 4));
                     for (int bb = 0; bb < nb; ++bb)
-                        bulk_g2s(sdxs + (uint32_t)(xs * kPfMaxNb + bb) * (kPfMaxN * 4), G.actd + (size_t)bb * G.P + first,
+                        bulk_g2s(sdxs + (uint32_t)(xs * kPfMaxNb + bb) * (kPfDxsStride * 4), G.actd + (size_t)bb * G.P + first,
                                  (uint32_t)n * 4, dfull);
                 }
                 if (br.round > 0 && !pf_wait(bar(kBlockDone + br.slot), br.phase ^ 1u, abort_flag, G.err)) break;
                 const uint32_t full = bar(kBFull + br.slot);
+                reinterpret_cast<int*>(sm + PfSmem::bhdr)[br.slot] = n;
                 mbar_expect_tx(full, (uint32_t)n * 128 * 4);
                 const CUtensorMap* map = &G.bmaps[(n >> 4) - 1];
 #pragma unroll
@@ -428,20 +536,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
                                     ((uint64_t)2 << 61) | (uint64_t)((sb0 >> 4) & 0x3FFFu);
             Ring<2> ab;
             Ring<kPfAcc> acc;
-            int tile = 0, b = 0;
-            uint32_t idesc = 0;
-            int next_n = (pf_tile(G, 0).ntok + 15) & ~15;
+            const volatile int* bhdr = reinterpret_cast<const volatile int*>(sm + PfSmem::bhdr);
             for (int blk = 0; blk < nblk; ++blk) {
-                if (b == 0) {
-                    idesc = (1u << 4) | ((uint32_t)(next_n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-                    if (tile + 1 < my_tiles) next_n = (pf_tile(G, tile + 1).ntok + 15) & ~15;
-                }
-                if (!pf_wait(bar(kAFull + ab.slot), ab.phase, abort_flag, G.err)) break;
+                // B first (it runs ahead): its header read overlaps the wait for A
                 if (!pf_wait(bar(kBFull + ab.slot), ab.phase, abort_flag, G.err)) break;
+                const uint32_t idesc = (1u << 4) | ((uint32_t)(bhdr[ab.slot] >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+                if (!pf_wait(bar(kAFull + ab.slot), ab.phase, abort_flag, G.err)) break;
                 if (acc.round > 0 && !pf_wait(bar(kAccEmpty + acc.slot), acc.phase ^ 1u, abort_flag, G.err)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint64_t bdesc = bdesc0 + (uint64_t)(ab.slot * 4 * (kPfBStage >> 4));
-                const uint32_t dd = tmem + (uint32_t)acc.slot * kPfMaxN;
+                const uint32_t dd = tmem + (uint32_t)acc.slot * kPfAccCols;
                 const uint32_t da = tmem + kPfACol + (uint32_t)ab.slot * 128;
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -458,10 +562,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
                 umma_commit(bar(kAccFull + acc.slot));
                 ab.next();
                 acc.next();
-                if (++b == nb) {
-                    b = 0;
-                    ++tile;
-                }
             }
         }
     } else if (warp >= kPfEpiWarp0) {
@@ -470,32 +570,30 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
         // the last block of a tile writes 0.125 * R out instead.
         const int ew = warp - kPfEpiWarp0, quarter = ew & 3, c0 = 32 * (ew >> 2), row = 32 * quarter + lane;
         const uint32_t tlane = (uint32_t)(32 * quarter) << 16;
-        const __half* dwring = reinterpret_cast<const __half*>(sm + PfSmem::dw);
         auto uwait = [&](int b, uint32_t parity) {
             return __all_sync(0xffffffffu, pf_wait(bar(b), parity, abort_flag, G.err));
         };
         Ring<kPfDwRing> dr;
         Ring<kPfAcc> acc;
-        int tile = 0, b = 0, first = 0, ntok = 0, mt = 0;
+        int tile = 0, b = 0;
         for (int e = 0; e < nblk; ++e) {
-            if (b == 0) {
-                const PfTile t = pf_tile(G, tile);
-                first = t.first;
-                ntok = t.ntok;
-                mt = t.mt;
-                if (!uwait(kDxsFull + (tile & 1), (tile >> 1) & 1)) break;
-            }
             if (!uwait(kDwFull + dr.slot, dr.phase)) break;
+            const uint8_t* slot = sm + PfSmem::dw + dr.slot * kPfDwSlot;
+            const int4 hdr = *reinterpret_cast<const int4*>(slot + kPfDwHdr);  // {first, entries, mt, types}
+            const int first = hdr.x, ntok = hdr.y, mt = hdr.z, type = pf_row_type(hdr.w, G.role, quarter);
+            if (b == 0 && !uwait(kDxsFull + (tile & 1), (tile >> 1) & 1)) break;
             if (!uwait(kAccFull + acc.slot, acc.phase)) break;
             const bool last = b == nb - 1;
             if (c0 < ntok) {
-                const float dw = __half2float(dwring[dr.slot * 128 + row]);
+                const float dw = type == CLB_IQ1_M
+                                     ? iq1m_scale(*reinterpret_cast<const uint2*>(slot + 256 + row * 8))
+                                     : __half2float(reinterpret_cast<const __half*>(slot)[row]);
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");  // the previous block's R stores
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const float* dxs =
-                    reinterpret_cast<const float*>(sm + PfSmem::dxs) + ((tile & 1) * kPfMaxNb + b) * kPfMaxN + c0;
+                const float* dxs = reinterpret_cast<const float*>(sm + PfSmem::dxs) +
+                                   ((tile & 1) * kPfMaxNb + b) * kPfDxsStride + c0;
                 uint32_t d[32], r[32];
-                tmem_ld32(tmem + tlane + (uint32_t)(acc.slot * kPfMaxN + c0), d);
+                tmem_ld32(tmem + tlane + (uint32_t)(acc.slot * kPfAccCols + c0), d);
                 if (b > 0) tmem_ld32(tmem + tlane + kPfRCol + (uint32_t)c0, r);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
@@ -542,56 +640,83 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     } else {
         // ---------------- decoders (warps 0-7): one 32-value chunk of one row per stage ----------------
-        // Per block and slice (16 values of the chunk): decode the slice of the 4 stages, then
-        // one 32-column tensor-memory store.
+        // Per block: the raw words of the thread's chunk c = 2q + dc of the 4 stages and its
+        // sub-scales, then two 32-column tensor-memory stores (pf_decode_block).
         const uint32_t lb = (uint32_t)lane * 4u;
-        const int dr = 32 * (warp & 3) + lane, dc = warp >> 2;  // row, chunk of a stage
-        const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
-        const __half2 off2 = __float2half2_rn(1152.0f);
+        const int quarter = warp & 3, dr = 32 * quarter + lane, dc = warp >> 2;  // row, chunk of a stage
+        const uint32_t tlane = (uint32_t)(32 * quarter) << 16;
+        const __half2 off2 = __float2half2_rn(-1152.0f);
         auto uwait = [&](int b, uint32_t parity) {
             return __all_sync(0xffffffffu, pf_wait(bar(b), parity, abort_flag, G.err));
         };
         Ring<2> rr;
-        for (int blk = 0; blk < nblk; ++blk) {
-            if (!uwait(kRawFull + rr.slot, rr.phase)) break;
-            const uint8_t* raw = sm + PfSmem::raw + rr.slot * kPfRawBlock + dr * 16 + dc * 8;
-            uint2 cw[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) cw[q] = *reinterpret_cast<const uint2*>(raw + q * kPfRawStage);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(kRawEmpty + rr.slot));
-            __half2 s2[4], noff[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const uint32_t sc = (((cw[q].y & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27;  // 2s + 1
-                s2[q] = __float2half2_rn((float)sc);
-                noff[q] = __hneg2(__hmul2(off2, s2[q]));
-            }
-            // this block's A buffers were last read by the MMAs of block blk - 2
-            if (rr.round > 0 && !uwait(kBlockDone + rr.slot, rr.phase ^ 1u)) break;
-#pragma unroll
-            for (int jj = 0; jj < 2; ++jj) {
-                uint32_t v[32];
+        // One block of type T, after its weight pieces landed; false when a wait gave up.
+        // Specialised per type so that each path is straight-line code.
+        auto block = [&](auto tt) -> bool {
+            constexpr int T = decltype(tt)::value;
+            const uint8_t* slotp = sm + PfSmem::raw + rr.slot * kPfRawBlock;
+            const uint8_t* raw = slotp + dr * 16;
+            uint32_t cw[8];
+            uint2 scw = make_uint2(0u, 0u);
+            if (T != CLB_IQ2_XXS) scw = *reinterpret_cast<const uint2*>(slotp + kPfRawSc + dr * 8);
+            if (T == CLB_IQ1_M) {
+                const uint4 p0 = *reinterpret_cast<const uint4*>(raw);
+                const uint4 p1 = *reinterpret_cast<const uint4*>(raw + kPfRawStage);
+                const uint4 p2 = *reinterpret_cast<const uint4*>(raw + 2 * kPfRawStage);
+                cw[0] = dc ? p0.y : p0.x;  // qs word of chunk c (piece c / 4, word c % 4)
+                cw[1] = dc ? p0.w : p0.z;
+                cw[2] = dc ? p1.y : p1.x;
+                cw[3] = dc ? p1.w : p1.z;
+                const uint32_t hs = 16u * (uint32_t)dc;  // qh half-word c of piece 2
+                cw[4] = (p2.x >> hs) & 0xffffu;
+                cw[5] = (p2.y >> hs) & 0xffffu;
+                cw[6] = (p2.z >> hs) & 0xffffu;
+                cw[7] = (p2.w >> hs) & 0xffffu;
+            } else {
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const uint32_t grp = 2 * jj + h;
-                        const uint32_t selj = 0x5504u | (grp << 4);
-                        const uint32_t sel = tab32(kRowTabXXS + prmt2(cw[q].x, lb, selj)) |
-                                             tab32(kRowTabXXS + 128 + prmt2(cw[q].y, lb, selj));
-                        biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel), s2[q], noff[q], v[8 * q + 4 * h],
-                                        v[8 * q + 4 * h + 1]);
-                        biased4_to_half(prmt_sel(kPos2b, kNeg2b, sel >> 16), s2[q], noff[q], v[8 * q + 4 * h + 2],
-                                        v[8 * q + 4 * h + 3]);
-                    }
+                    const uint2 v = *reinterpret_cast<const uint2*>(raw + q * kPfRawStage + dc * 8);
+                    cw[2 * q] = v.x;
+                    cw[2 * q + 1] = v.y;
                 }
-                tmem_st32(tmem + tlane + kPfACol + (uint32_t)rr.slot * 128 + (uint32_t)(2 * dc + jj) * 32, v);
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kRawEmpty + rr.slot));
+            __half2 s2[4], nf[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t c = 2u * q + (uint32_t)dc;
+                if (T == CLB_IQ2_XXS) {  // bits 28-31 of the aux word: s
+                    const uint32_t sc = (((cw[2 * q + 1] & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27;  // 2s + 1
+                    s2[q] = __float2half2_rn((float)sc);
+                } else if (T == CLB_IQ2_XS) {  // scale byte c: low nibble values 0-15, high 16-31
+                    const uint32_t scb = ((q < 2 ? scw.x : scw.y) >> (8u * (c & 3u))) & 0xffu;
+                    s2[q] = __floats2half2_rn((float)(((scb & 15u) << 1) | 1u), (float)(((scb >> 4) << 1) | 1u));
+                } else {  // scale word c / 2: 3-bit scales at bit 6 (c & 1) and 6 (c & 1) + 3
+                    const uint32_t w = ((q < 2 ? scw.x : scw.y) >> (16u * (q & 1u))) >> (6u * (c & 1u));
+                    s2[q] = __floats2half2_rn((float)(((w & 7u) << 1) | 1u), (float)((((w >> 3) & 7u) << 1) | 1u));
+                }
+                nf[q] = __hmul2(off2, s2[q]);
+            }
+            // this block's A buffers were last read by the MMAs of block blk - 2
+            if (rr.round > 0 && !uwait(kBlockDone + rr.slot, rr.phase ^ 1u)) return false;
+            pf_decode_block<T>(cw, s2, nf, lb,
+                               tmem + tlane + kPfACol + (uint32_t)rr.slot * 128 + (uint32_t)(2 * dc) * 32);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(kAFull + rr.slot));
+            return true;
+        };
+        for (int blk = 0; blk < nblk; ++blk) {
+            if (!uwait(kRawFull + rr.slot, rr.phase)) break;
+            const int type =
+                pf_row_type(*reinterpret_cast<const int*>(sm + PfSmem::raw + rr.slot * kPfRawBlock + kPfRawHdr),
+                            G.role, quarter);
+            const bool ok = type == CLB_IQ2_XXS ? block(std::integral_constant<int, CLB_IQ2_XXS>())
+                            : type == CLB_IQ2_XS ? block(std::integral_constant<int, CLB_IQ2_XS>())
+                                                 : block(std::integral_constant<int, CLB_IQ1_M>());
+            if (!ok) break;
             rr.next();
         }
     }
@@ -697,6 +822,45 @@ __global__ void __launch_bounds__(256) k_prefill_quant(const float* __restrict__
     float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
     const size_t o = (size_t)row * cols + b * 256;
     quant_block_fp16(v, qs + o, d + blk, q16 + o);
+}
+
+// x = RMSNorm(h) fused with Q8_K of the token rows, for the batched stack: one CTA of 1024
+// threads per token. The fp64 sum of squares has k_norm_quant's fixed order (lane t sums
+// (double)h[t + 1024 j]^2 over j, then a binary tree over the lanes), so every token gets the
+// single-token stack's scale bit for bit; x = h * (float)(1 / sqrt(mean + 1e-6)).
+__global__ void __launch_bounds__(1024) k_prefill_norm_quant(const float* __restrict__ h, int cols,
+                                                             int8_t* __restrict__ qs, float* __restrict__ d,
+                                                             __half* __restrict__ q16) {
+    __shared__ double part[1024];
+    __shared__ float scale_s;
+    const int t = threadIdx.x, row = blockIdx.x;
+    const float* hr = h + (size_t)row * cols;
+    double s = 0.0;
+    for (int i = t; i < cols; i += 1024) {
+        const double v = (double)hr[i];
+        s = __dadd_rn(s, __dmul_rn(v, v));
+    }
+    part[t] = s;
+    __syncthreads();
+    for (int stride = 512; stride > 0; stride >>= 1) {
+        if (t < stride) part[t] = __dadd_rn(part[t], part[t + stride]);
+        __syncthreads();
+    }
+    if (t == 0) {
+        const double mean = __ddiv_rn(part[0], (double)cols);
+        scale_s = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(mean, 1e-6)));
+    }
+    __syncthreads();
+    const float sc = scale_s;
+    const int nbr = cols >> 8, warp = t >> 5, lane = t & 31;
+    for (int b = warp; b < nbr; b += 32) {
+        const float4* src = reinterpret_cast<const float4*>(hr + b * 256 + lane * 8);
+        const float4 lo = src[0], hi = src[1];
+        float v[8] = {__fmul_rn(lo.x, sc), __fmul_rn(lo.y, sc), __fmul_rn(lo.z, sc), __fmul_rn(lo.w, sc),
+                      __fmul_rn(hi.x, sc), __fmul_rn(hi.y, sc), __fmul_rn(hi.z, sc), __fmul_rn(hi.w, sc)};
+        const size_t o = (size_t)row * cols + b * 256;
+        quant_block_fp16(v, qs + o, d + (size_t)row * nbr + b, q16 + o);
+    }
 }
 
 // Token rows of Q8_K(x) into list order: xg16[p] = q16[token of list[p]], dxg[b][p] its scales.
@@ -873,7 +1037,7 @@ cudaError_t encode_bmaps(CUtensorMap* maps, const __half* base, int P, int K) {
 
 cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const int* ids, const float* w, int T, int k,
                            int dim, int ff, float limit, const float* resid, float* out, void* wsp, int* err,
-                           int phase_mask, cudaStream_t s) {
+                           int phase_mask, cudaStream_t s, bool norm_x) {
     PrefillWs ws{};
     carve(wsp, T, k, dim, ff, E, &ws);
     const int P = ws.P;
@@ -889,7 +1053,10 @@ cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const 
     const int nbx = dim / 256, nbh = ff / 256;
     if (phase_mask & 1) {
         k_prefill_group<<<1, 1024, 0, s>>>(ids, T, k, E, P, ws.list, ws.tiles, ws.ntiles, err);
-        k_prefill_quant<<<(T * nbx + 7) / 8, 256, 0, s>>>(x, T, dim, ws.qx, ws.dx, ws.qx16);
+        if (norm_x)
+            k_prefill_norm_quant<<<T, 1024, 0, s>>>(x, dim, ws.qx, ws.dx, ws.qx16);
+        else
+            k_prefill_quant<<<(T * nbx + 7) / 8, 256, 0, s>>>(x, T, dim, ws.qx, ws.dx, ws.qx16);
         k_prefill_gather<<<(P * nbx + 7) / 8, 256, 0, s>>>(ws.list, P, k, dim, ws.qx16, ws.dx, ws.xg16, ws.dxg);
     }
     PrefillGemm g{};
@@ -924,6 +1091,44 @@ cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const 
     }
     if (phase_mask & 16) k_prefill_combine<<<T, 256, 0, s>>>(ws.y, ids, w, k, dim, resid, out);
     return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------
+// Batched stack: T tokens through layers 0 .. nl-1 of `desc` ([nl][E]), each layer
+// h <- h + layer(RMSNorm(h)) (the single-token stack's recurrence) with the layer as the
+// grouped prefill above. Routes: [nl][T][k] ids and weights, or, when `logits` ([nl][T][E])
+// is given, top-k by sigmoid per token on the device into the workspace.
+size_t stack_batch_workspace_bytes(int T, int k, int dim, int ff, int E) {
+    const size_t a = (prefill_workspace_bytes(T, k, dim, ff, E) + 255) & ~(size_t)255;
+    const size_t r = ((size_t)T * k * 4 + 255) & ~(size_t)255;
+    return a + 2 * r + (size_t)T * dim * 4;
+}
+
+cudaError_t launch_stack_batch(const ExpertDesc* desc, int E, int nl, const float* logits, const int* ids_all,
+                               const float* w_all, float* h, int T, int k, int dim, int ff, float limit, void* wsp,
+                               int* err, cudaStream_t s) {
+    uint8_t* base = static_cast<uint8_t*>(wsp);
+    const size_t a = (prefill_workspace_bytes(T, k, dim, ff, E) + 255) & ~(size_t)255;
+    const size_t r = ((size_t)T * k * 4 + 255) & ~(size_t)255;
+    int* rids = reinterpret_cast<int*>(base + a);
+    float* rw = reinterpret_cast<float*>(base + a + r);
+    float* h2 = reinterpret_cast<float*>(base + a + 2 * r);
+    float *hin = h, *hout = h2;
+    cudaError_t e = cudaSuccess;
+    for (int l = 0; l < nl; ++l) {
+        const int* ids = ids_all ? ids_all + (size_t)l * T * k : rids;
+        const float* w = w_all ? w_all + (size_t)l * T * k : rw;
+        if (!ids_all && (e = launch_route_sigmoid(logits + (size_t)l * T * E, E, k, T, rids, rw, s)) != cudaSuccess)
+            return e;
+        if ((e = launch_prefill(desc + (size_t)l * E, E, hin, ids, w, T, k, dim, ff, limit, hin, hout, wsp, err, 31, s,
+                                true)) != cudaSuccess)
+            return e;
+        float* t = hin;
+        hin = hout;
+        hout = t;
+    }
+    if (hin != h) e = cudaMemcpyAsync(h, hin, (size_t)T * dim * 4, cudaMemcpyDeviceToDevice, s);
+    return e;
 }
 
 }  // namespace clb

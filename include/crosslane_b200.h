@@ -289,12 +289,12 @@ int32_t clb_stack_decode_device(clb_bank* bank, uint32_t first_layer, int32_t n_
  * For T tokens with k picks each: out[t] = [resid[t] +] sum over token t's picks in
  * ascending expert id of fma(w, expert(x[t])), i.e. clb_layer_execute applied to every
  * token (warm_execute's combine, runtime.cpp:184-187). The T*k picks are grouped by
- * expert; each expert's gate/up and down run as tcgen05 GEMMs with the IQ2_XXS weights
- * decoded once per 128 tokens into exact fp16 integers and the Q8_K activations as fp16
- * integers, per-256-block scales applied from fp32 tensor-memory accumulators. Results
- * agree with the CPU lane to fp32 reassociation (not bit for bit). Every resident expert
- * of the layer must be IQ2_XXS (else CLB_E_UNSUPPORTED); dim and ff multiples of 256,
- * at most 8192. No counterpart in crosslane's lanes (they decode one token at a time). */
+ * expert; each expert's gate/up and down run as tcgen05 GEMMs with the weights (IQ2_XXS,
+ * IQ2_XS or IQ1_M, mixed freely across experts and matrices) decoded once per 48 tokens
+ * into exact fp16 integers and the Q8_K activations as fp16 integers, per-256-block scales
+ * applied from fp32 tensor-memory accumulators. Results agree with the CPU lane to fp32
+ * reassociation (not bit for bit). dim and ff multiples of 256, from 512 to 8192 (else
+ * CLB_E_UNSUPPORTED). No counterpart in crosslane's lanes (they decode one token at a time). */
 
 /* Device bytes of workspace clb_prefill_layer_device needs for `tokens` x `k` picks. */
 uint64_t clb_prefill_workspace_bytes(const clb_bank* bank, int32_t tokens, int32_t k);
@@ -321,6 +321,27 @@ int32_t clb_prefill_reserve(clb_bank* bank, int32_t tokens, int32_t k, clb_error
 /* Host-buffer prefill, synchronous: ids/w [tokens][k], x/out [tokens][dim]. */
 int32_t clb_prefill_layer(clb_bank* bank, uint32_t layer, int32_t tokens, int32_t k, const int32_t* ids,
                           const float* w, const float* x, float* out, clb_error_v1* err);
+
+/* ---- batched stack decode: T tokens (one per sequence) through consecutive layers ----
+ * For every token t and layer l = first .. first + n_layers - 1:
+ *   h_t <- h_t + layer_l(RMSNorm(h_t))
+ * with the layer routed from logits [n_layers][tokens][n_experts] (top max_picks by sigmoid,
+ * renormalised, as clb_stack_decode) and computed as one grouped prefill layer over the
+ * batch, so each picked expert's weights are decoded once per 48 of its tokens instead of
+ * once per token. This is clb_stack_decode applied to each token, to fp32 reassociation.
+ * The bank holds every expert of those layers (no sharding); dim and ff as for prefill.
+ * No counterpart in crosslane's lanes (they decode one token at a time). */
+uint64_t clb_stack_batch_workspace_bytes(const clb_bank* bank, int32_t tokens);
+
+/* Device pointers, the bank's stream (or `stream`), no synchronisation; routing on the
+ * device. d_h [tokens][dim] is updated in place. */
+int32_t clb_stack_batch_device(clb_bank* bank, uint32_t first_layer, int32_t n_layers, int32_t tokens,
+                               const float* d_logits, float* d_h, void* d_ws, uint64_t ws_bytes, void* stream,
+                               clb_error_v1* err);
+
+/* Host buffers, synchronous; routing on the host. h [tokens][dim] is updated in place. */
+int32_t clb_stack_batch(clb_bank* bank, uint32_t first_layer, int32_t n_layers, int32_t tokens, const float* logits,
+                        float* h, clb_error_v1* err);
 
 /* The bank's CUDA stream (cudaStream_t) and a synchronisation helper. */
 void* clb_bank_stream(clb_bank* bank);

@@ -89,10 +89,12 @@ class Oracle:
         return np.array([self.L.orc_swiglu(float(a), float(b), limit) for a, b in zip(g, u)], np.float32)
 
     def expert(self, qtype, gate, up, down, x, dim, ff, limit=0.0):
+        """qtype: one type for the three matrices, or a (gate, up, down) tuple of types."""
+        tg, tu, td = qtype if isinstance(qtype, tuple) else (qtype, qtype, qtype)
         h = np.zeros(ff, np.float32)
         y = np.zeros(dim, np.float32)
         x = np.ascontiguousarray(x, np.float32)
-        rc = self.L.orc_expert(qtype, ptr(gate), qtype, ptr(up), qtype, ptr(down), ptr(x), dim, ff, limit, ptr(h),
+        rc = self.L.orc_expert(tg, ptr(gate), tu, ptr(up), td, ptr(down), ptr(x), dim, ff, limit, ptr(h),
                                ptr(y))
         assert rc == 0
         return h, y
@@ -134,14 +136,14 @@ class Oracle:
         assert rc == 0
         return y
 
-    def stack_sensitivity(self, policy, seed, h0, logits, dim, ff, k=6, limit=0.0):
+    def stack_sensitivity(self, policy, seed, h0, logits, dim, ff, k=6, limit=0.0, first=0):
         """rel_l2 between the stack of h0 and of h0 moved by +-1 ulp (alternating): how far
         any non-bit-exact evaluation order can drift on this input (Q8_K re-quantisation
         between layers turns ulp-level differences into whole quantisation steps)."""
-        a = self.stack(policy, seed, h0, logits, dim, ff, k, limit)
+        a = self.stack(policy, seed, h0, logits, dim, ff, k, limit, first)
         h0 = np.ascontiguousarray(h0, np.float32)
         step = np.where(np.arange(h0.size) % 2 == 0, 1, -1).astype(np.int32)
-        b = self.stack(policy, seed, (h0.view(np.int32) + step).view(np.float32), logits, dim, ff, k, limit)
+        b = self.stack(policy, seed, (h0.view(np.int32) + step).view(np.float32), logits, dim, ff, k, limit, first)
         return rel_l2(b, a)
 
     def rmsnorm(self, h):

@@ -1,8 +1,9 @@
 """GPU parity of the batched prefill (grouped tcgen05 GEMMs, clb_prefill_*) against the CPU
 oracle: every token's combined output within the north-star tolerance of the reference
-layer (relative L2 <= 1e-3, max-abs-relative <= 5e-3), run-to-run bit-identical, and the
-ragged cases of the grouping (one token, token counts that are not multiples of 16,
-experts with more than one 128-token chunk, unused experts)."""
+layer (relative L2 <= 1e-3, max-abs-relative <= 5e-3), run-to-run bit-identical, for each
+weight type (IQ2_XXS, IQ2_XS, IQ1_M), experts of mixed types and matrices of mixed types
+within one expert, and the ragged cases of the grouping (one token, token counts that are
+not multiples of 16, experts with more than one 48-token chunk, unused experts)."""
 import numpy as np
 import pytest
 
@@ -28,13 +29,13 @@ def routes(orc, rng, T, E, k):
     return ids, w
 
 
-def check_tokens(orc, got, ids, w, x, seed, dim, ff, layer=0, tokens=None):
+def check_tokens(orc, got, ids, w, x, seed, dim, ff, layer=0, tokens=None, policy=0):
     """The tolerance applies to the combined output of the batch ([T][dim]); per token the
     error is fp32 reassociation (median <= 1e-4) except where a value of h lands within an
     ulp of a Q8_K rounding boundary and the two sides quantise it one step apart, which
     moves that token by up to a few 1e-3 (bounded at 1e-2)."""
     tokens = list(range(len(ids))) if tokens is None else list(tokens)
-    want = np.stack([orc.layer_synth(0, seed, layer, ids[t], w[t], x[t], dim, ff) for t in tokens])
+    want = np.stack([orc.layer_synth(policy, seed, layer, ids[t], w[t], x[t], dim, ff) for t in tokens])
     have = got[tokens]
     per = np.array([rel_l2(have[i], want[i]) for i in range(len(tokens))])
     e, m = rel_l2(have, want), max_abs_rel(have, want)
@@ -83,11 +84,70 @@ def test_prefill_device_entry_with_residual(cb, orc, cuda):
         bank.close()
 
 
-def test_prefill_rejects_other_types(cb, orc):
-    dim, ff, E = 2048, 512, 8
+@pytest.mark.parametrize("policy,T,E,k", [(3, 37, 16, 4), (4, 64, 24, 6), (4, 1, 8, 1), (2, 130, 40, 3),
+                                           (1, 100, 300, 4)])
+def test_prefill_types_match_oracle(cb, orc, policy, T, E, k):
+    """policy 3: all IQ2_XS, 4: all IQ1_M, 2: a type per expert from the seed, 1: experts
+    [0,128) IQ2_XXS, [128,256) IQ2_XS, the rest IQ1_M."""
+    dim, ff, seed = 1024, 768, 11
+    bank = cb.ExpertBank(n_layers=2, n_experts=E, dim=dim, ff=ff, max_picks=k, device=0)
+    try:
+        bank.fill_synthetic(seed, policy)
+        rng = np.random.default_rng(T * 5 + E + policy)
+        ids, w = routes(orc, rng, T, E, k)
+        if policy == 1:  # cover all three type ranges
+            ids[:, 0] = rng.integers(0, 128, T)
+            ids[:, 1] = rng.integers(128, 256, T)
+            ids[:, 2] = rng.integers(256, E, T)
+            for t in range(T):
+                rest = rng.choice(np.setdiff1d(np.arange(E), ids[t, :3]), k - 3, replace=False)
+                ids[t, 3:] = rest
+        x = rng.standard_normal((T, dim)).astype(np.float32)
+        got = bank.prefill_layer(1, ids, w, x)
+        check_tokens(orc, got, ids, w, x, seed, dim, ff, layer=1, policy=policy)
+        again = bank.prefill_layer(1, ids, w, x)
+        assert np.array_equal(got.view(np.uint32), again.view(np.uint32)), "prefill not run-to-run identical"
+    finally:
+        bank.close()
+
+
+def test_prefill_mixed_matrix_types(cb, orc):
+    """Gate, up and down of one expert in different types (each 32-row group of a gate/up
+    tile decodes its own type), loaded through clb_bank_load_matrix."""
+    IQ2_XXS, IQ2_XS, IQ1_M = 16, 17, 29
+    dim, ff, E, k, T, seed = 1536, 1024, 6, 3, 70, 17
+    combos = [(IQ2_XXS, IQ2_XS, IQ1_M), (IQ1_M, IQ2_XXS, IQ2_XS), (IQ2_XS, IQ1_M, IQ2_XXS),
+              (IQ1_M, IQ1_M, IQ2_XXS), (IQ2_XS, IQ2_XXS, IQ2_XXS), (IQ2_XXS, IQ1_M, IQ1_M)]
+    bank = cb.ExpertBank(n_layers=1, n_experts=E, dim=dim, ff=ff, max_picks=k, device=0)
+    try:
+        mats = []
+        for e, types in enumerate(combos):
+            g = orc.synth_matrix(types[0], seed, 0, e, 0, ff, dim)
+            u = orc.synth_matrix(types[1], seed, 0, e, 1, ff, dim)
+            d = orc.synth_matrix(types[2], seed, 0, e, 2, dim, ff)
+            for role, (t, m) in enumerate(zip(types, (g, u, d))):
+                bank.load_matrix(0, e, role, t, m)
+            mats.append((types, g, u, d))
+        rng = np.random.default_rng(8)
+        ids, w = routes(orc, rng, T, E, k)
+        x = rng.standard_normal((T, dim)).astype(np.float32)
+        got = bank.prefill_layer(0, ids, w, x)
+        want = np.zeros_like(got)
+        for t in range(T):
+            rows = np.stack([orc.expert(mats[e][0], *mats[e][1:], x[t], dim, ff)[1] for e in ids[t]])
+            want[t] = orc.combine(ids[t], w[t], rows)
+        per = np.array([rel_l2(got[t], want[t]) for t in range(T)])
+        assert rel_l2(got, want) <= REL_L2 and max_abs_rel(got, want) <= MAX_ABS_REL
+        assert np.median(per) <= 1e-4 and per.max() <= 1e-2, (np.median(per), per.max())
+    finally:
+        bank.close()
+
+
+def test_prefill_rejects_unsupported_shape(cb, orc):
+    dim, ff, E = 2048, 256, 8  # ff below the GEMM's 512 minimum
     bank = cb.ExpertBank(n_layers=1, n_experts=E, dim=dim, ff=ff, max_picks=2, device=0)
     try:
-        bank.fill_synthetic(1, 3)  # all IQ2_XS
+        bank.fill_synthetic(1, 3)
         ids = np.array([[0, 1]], np.int32)
         w = np.array([[0.5, 0.5]], np.float32)
         with pytest.raises(cb.ClbError) as ei:

@@ -1,0 +1,106 @@
+"""GPU parity of the batched stack decode (clb_stack_batch*: T tokens through consecutive
+layers, each layer one grouped prefill over the batch) against the CPU oracle's stack
+(h <- h + layer(RMSNorm(h)) per layer, mode-A routing) run token by token. Multi-layer
+outputs are compared under the stack's own sensitivity bound: Q8_K re-quantisation between
+layers turns fp32 reassociation into whole quantisation steps, so the bound is
+max(1e-3, 4 x the oracle's rel_l2 between the stack of h0 and of h0 moved by one ulp)."""
+import numpy as np
+import pytest
+
+from oracle_lib import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 1e-3
+
+
+@pytest.fixture(scope="module")
+def cb(cuda):
+    import crosslane_b200
+    return crosslane_b200
+
+
+def zipf_logits(rng, L, T, E, s=1.1):
+    """Router logits whose top-k follows Zipf(s) expert popularity over a per-layer
+    permutation (Gumbel top-k of log p)."""
+    out = np.empty((L, T, E), np.float32)
+    for l in range(L):
+        perm = rng.permutation(E)
+        logp = -s * np.log(np.arange(1, E + 1, dtype=np.float64))
+        g = rng.gumbel(size=(T, E))
+        out[l] = (logp[np.argsort(perm)][None, :] + g).astype(np.float32)
+    return out
+
+
+@pytest.mark.parametrize("policy,T,E,L,zipf", [(2, 40, 32, 3, False), (1, 24, 300, 2, False), (4, 64, 48, 2, True)])
+def test_stack_batch_matches_oracle(cb, orc, policy, T, E, L, zipf):
+    dim, ff, seed, k = 1024, 512, 13, 6
+    bank = cb.ExpertBank(n_layers=L + 1, n_experts=E, dim=dim, ff=ff, max_picks=k, device=0)
+    try:
+        bank.fill_synthetic(seed, policy)
+        rng = np.random.default_rng(T + E + L)
+        h0 = rng.standard_normal((T, dim)).astype(np.float32)
+        logits = zipf_logits(rng, L, T, E) if zipf else rng.standard_normal((L, T, E)).astype(np.float32)
+        got = bank.stack_batch(1, L, h0, logits)
+        for t in range(T):
+            want = orc.stack(policy, seed, h0[t], logits[:, t, :], dim, ff, k, first=1)
+            bound = max(REL_L2, 4 * orc.stack_sensitivity(policy, seed, h0[t], logits[:, t, :], dim, ff, k, first=1))
+            assert rel_l2(got[t], want) <= bound, (t, rel_l2(got[t], want), bound)
+        again = bank.stack_batch(1, L, h0, logits)
+        assert np.array_equal(got.view(np.uint32), again.view(np.uint32)), "batched stack not run-to-run identical"
+    finally:
+        bank.close()
+
+
+def test_stack_batch_one_layer_is_the_prefill_layer(cb, orc):
+    """One layer: h + layer(RMSNorm(h)) equals the oracle layer on the oracle's RMSNorm (the
+    fused norm + Q8_K kernel reproduces the single-token stack's fixed-order scale)."""
+    dim, ff, E, k, T, seed, policy = 2048, 768, 24, 6, 50, 3, 2
+    bank = cb.ExpertBank(n_layers=1, n_experts=E, dim=dim, ff=ff, max_picks=k, device=0)
+    try:
+        bank.fill_synthetic(seed, policy)
+        rng = np.random.default_rng(1)
+        h0 = rng.standard_normal((T, dim)).astype(np.float32)
+        logits = rng.standard_normal((1, T, E)).astype(np.float32)
+        got = bank.stack_batch(0, 1, h0, logits)
+        want = np.stack([orc.stack(policy, seed, h0[t], logits[:, t, :], dim, ff, k) for t in range(T)])
+        per = np.array([rel_l2(got[t] - h0[t], want[t] - h0[t]) for t in range(T)])
+        assert rel_l2(got - h0, want - h0) <= REL_L2 and np.median(per) <= 1e-4 and per.max() <= 1e-2, per.max()
+    finally:
+        bank.close()
+
+
+def test_stack_batch_device_entry(cb, orc, cuda):
+    """Device routing (clb_route_device's kernel) and device buffers agree with the host entry."""
+    torch = cuda
+    dim, ff, E, k, T, L, seed, policy = 1024, 512, 40, 6, 33, 2, 5, 2
+    bank = cb.ExpertBank(n_layers=L, n_experts=E, dim=dim, ff=ff, max_picks=k, device=0)
+    try:
+        bank.fill_synthetic(seed, policy)
+        rng = np.random.default_rng(2)
+        h0 = rng.standard_normal((T, dim)).astype(np.float32)
+        logits = rng.standard_normal((L, T, E)).astype(np.float32)
+        host = bank.stack_batch(0, L, h0, logits)
+        d_h = torch.from_numpy(h0.copy()).cuda()
+        d_lg = torch.from_numpy(logits).cuda()
+        d_ws = torch.empty(bank.stack_batch_workspace_bytes(T), dtype=torch.uint8, device="cuda")
+        bank.stack_batch_device(0, L, d_h, d_lg, d_ws)
+        bank.synchronize()
+        dev = d_h.cpu().numpy()
+        for t in range(T):
+            bound = max(REL_L2, 4 * orc.stack_sensitivity(policy, seed, h0[t], logits[:, t, :], dim, ff, k))
+            assert rel_l2(dev[t], host[t]) <= bound, (t, rel_l2(dev[t], host[t]))
+    finally:
+        bank.close()
+
+
+def test_stack_batch_rejects_partial_bank(cb, orc):
+    bank = cb.ExpertBank(n_layers=1, n_experts=16, dim=1024, ff=512, max_picks=2, device=0,
+                         expert_begin=0, expert_end=8)
+    try:
+        bank.fill_synthetic(1, 0)
+        with pytest.raises(cb.ClbError) as ei:
+            bank.stack_batch(0, 1, np.zeros((2, 1024), np.float32), np.zeros((1, 2, 16), np.float32))
+        assert ei.value.code == 1
+    finally:
+        bank.close()
