@@ -339,6 +339,141 @@ def run_prefill(args, rank, world, local):
         dist.destroy_process_group()
 
 
+SK_BATCH = 64
+SK_METRIC = "routed-expert decode tok/s (40-layer stack, batch 64, Zipf(1.1) routing)"
+SK_WORKLOAD = "BASELINE config 5: skewed-routing decode at batch 64 through the 40-layer stack"
+
+
+def zipf_logits(rng, layers, T, E, s=1.1):
+    """[layers][T][E] router logits whose top-k follows Zipf(s) expert popularity over a
+    per-layer seeded permutation of the experts: log p(rank) + Gumbel noise per token, so
+    top-k of the logits is a draw of k distinct experts with probabilities p (Gumbel top-k)."""
+    logp = -s * np.log(np.arange(1, E + 1, dtype=np.float64))
+    out = np.empty((layers, T, E), np.float32)
+    for l in range(layers):
+        rank = np.argsort(np.random.default_rng(SEED + 7919 * l).permutation(E))  # rank of expert e
+        out[l] = (logp[rank][None, :] + rng.gumbel(size=(T, E))).astype(np.float32)
+    return out
+
+
+def run_skewed(args, rank, world, local):
+    """Config 5: a batch of 64 tokens (one per sequence) through the 40-layer stack per step,
+    Zipf(1.1) routing, each layer one grouped prefill over the batch (clb_stack_batch)."""
+    import torch
+
+    import crosslane_b200 as cb
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        res = cpu_baseline(samples=max(1, min(args.steps, 3)))
+        if res is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref.so was not built"}))
+            return
+        print(json.dumps({"metric": SK_METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": world,
+                          "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": SK_BATCH * 1e3 / res["value"], "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "int8xIQ/fp32", "data": "synthetic",
+                          "config": {"workload": SK_WORKLOAD, "batch": SK_BATCH}, "impl": "reference",
+                          "cpu_baseline": res,
+                          "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    if world > 1:
+        raise SystemExit("--skewed runs on one GPU (the batched stack needs every expert on its bank)")
+    torch.cuda.set_device(local)
+    T, k, L = SK_BATCH, PICKS, args.layers
+    bank = cb.ExpertBank(n_layers=L, n_experts=args.experts, dim=DIM, ff=FF, max_picks=k, device=local)
+    bank.fill_synthetic(SEED, args.policy)
+    stream = torch.cuda.ExternalStream(bank.stream)
+    rng = np.random.default_rng(5000 + rank)
+    n_in = 3
+    xs = rng.standard_normal((n_in, T, DIM)).astype(np.float32)
+    lgs = np.stack([zipf_logits(rng, L, T, args.experts) for _ in range(n_in)])
+    # algorithmic bytes: every distinct picked expert of every layer read once, + h in/out per layer
+    ebytes = {}
+    alg = []
+    for i in range(n_in):
+        tot = 0
+        for l in range(L):
+            picked = set()
+            for t in range(T):
+                ids, _ = cb.route_host(0, lgs[i, l, t], k)
+                picked.update(int(e) for e in ids)
+            for e in picked:
+                if (l, e) not in ebytes:
+                    ebytes[(l, e)] = bank.expert_info(l, e)[1]
+                tot += ebytes[(l, e)]
+            tot += 2 * T * DIM * 4
+        alg.append(tot)
+    alg_bytes = float(np.mean(alg))
+    distinct = float(np.mean([len({int(e) for t in range(T) for e in cb.route_host(0, lgs[0, l, t], k)[0]})
+                              for l in range(L)]))
+    d_x = torch.from_numpy(xs).cuda()
+    d_lg = torch.from_numpy(lgs).cuda()
+    d_h = torch.empty((T, DIM), dtype=torch.float32, device="cuda")
+    d_ws = torch.empty(bank.stack_batch_workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+
+    def step(i):
+        j = i % n_in
+        with torch.cuda.stream(stream):
+            d_h.copy_(d_x[j])
+        bank.stack_batch_device(0, L, d_h, d_lg[j], d_ws)
+
+    for i in range(args.warmup):
+        step(i)
+    bank.synchronize()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    bank.synchronize()
+    ms_per_step = ms / args.steps
+    value = T * args.steps / (ms / 1e3)
+    # e2e: host h and logits through clb_stack_batch (host routing, copies in the timed region)
+    e2e_steps = 2 if args.quick else max(2, min(args.steps, 5))
+    bank.stack_batch(0, L, xs[0], lgs[0])
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        bank.stack_batch(0, L, xs[i % n_in], lgs[i % n_in])
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    hbm, hbm_kind = peaks()
+    achieved = alg_bytes / (ms_per_step / 1e3) / 1e9
+    cpu = None
+    if rank == 0 and not (args.no_cpu_baseline or args.quick):
+        cpu = cpu_baseline(samples=1)
+        if cpu is not None:
+            cpu["sample"] += "; the CPU lane decodes the batch token by token (no batched path)"
+    line = {
+        "metric": SK_METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 integers x fp16 integers -> fp32 (IQ x Q8_K)", "data": "synthetic",
+        "config": {"workload": SK_WORKLOAD, "batch": T, "layers": L, "experts": args.experts, "dim": DIM, "ff": FF,
+                   "picks": k, "types": "IQ2_XXS/IQ2_XS/IQ1_M per (layer, expert)",
+                   "routing": "top-6 of log Zipf(1.1) over a per-layer seeded permutation + Gumbel noise",
+                   "distinct_experts_per_layer": round(distinct, 1), "parallelism": "single GPU",
+                   "l2": "inputs larger than L2: %.1f GB of distinct expert weights per step" % (alg_bytes / 1e9)},
+        "e2e": {"value": round(T / e2e_s, 1), "unit": "tok/s",
+                "h2d_bytes_per_step": T * DIM * 4 + L * T * k * 8, "d2h_bytes_per_step": T * DIM * 4},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "kernel": "whole step (per layer: route, group, norm+Q8_K, gather, 2 x clb::k_prefill_gemm, "
+                               "SwiGLU+Q8_K, combine)",
+                     "algorithmic_bytes_per_step": alg_bytes, "peak_source": hbm_kind},
+        "cpu_baseline": cpu,
+        "clocks": clocks.summary(),
+        "gpu_launches": 8 * L * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+    bank.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -355,6 +490,8 @@ def main():
                     help="with N>1: independent full-bank replicas per GPU instead of expert-ID sharding")
     ap.add_argument("--exact-order", action="store_true",
                     help="reference summation order (CLB_BANK_EXACT_ORDER): bit-identical to the CPU lane")
+    ap.add_argument("--skewed", action="store_true",
+                    help="BASELINE config 5: batch-64 decode through the stack with Zipf(1.1) routing")
     ap.add_argument("--prefill", action="store_true",
                     help="BASELINE config 4 instead: 2048 tokens through one IQ2_XXS layer per step (own JSON line)")
     args = ap.parse_args()
@@ -368,6 +505,10 @@ def main():
         if args.steps == 200:
             args.steps = 20
         return run_prefill(args, rank, world, local)
+    if args.skewed:
+        if args.steps == 200:
+            args.steps = 10
+        return run_skewed(args, rank, world, local)
 
     if args.impl == "reference":
         return run_reference(args, rank, world)
