@@ -95,6 +95,7 @@ constexpr uint32_t kPfSpin = 1u << 22;        // drain wait polls
 constexpr uint32_t kPfSuspendNs = 20000;      // try_wait suspend hint
 constexpr uint64_t kPfTimeoutNs = 1000000000; // 1 s: a pipeline wait longer than this is an error
 constexpr int kErrPrefillWait = 3;
+constexpr int kPfColdMax = 2;                 // experts with at most this many picks take the row-dot path
 
 // Values biased by +128 so that 0x64XX = 1024 + XX as fp16. IQ2: +8, +25, +43 and -8, -25, -43
 // (selector nibble: symbol, bit 2 the sign). IQ1_M: 8 g + delta for g = -1, 0, +1 (symbol
@@ -743,16 +744,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
 }
 
 // ---------------------------------------------------------------------------------------
-// Grouping of the T x k picks by expert (one CTA of 1024 threads): list[] holds the slots
-// t*k+p expert after expert, in slot order within an expert, each expert's run padded with
-// -1 to a multiple of 16 entries; tiles[] one entry per chunk of at most kPfMaxN entries.
+// Grouping of the T x k picks by expert (one CTA of 1024 threads). Experts with more than
+// `cold_max` picks go to the GEMMs: list[] holds their slots t*k+p expert after expert, in
+// slot order within an expert, each expert's run padded with -1 to a multiple of 16 entries;
+// tiles[] one entry per chunk of at most kPfMaxN entries. The slots of the other experts go
+// to pairs[] (*npairs of them, in no particular order) for the row-dot path, which decodes a
+// weight for one token at a third of the GEMM decoder's cost per weight.
 __global__ void __launch_bounds__(1024) k_prefill_group(const int* __restrict__ ids, int T, int k, int E, int P,
-                                                        int* __restrict__ list, int4* __restrict__ tiles,
-                                                        int* __restrict__ ntiles, int* __restrict__ err) {
+                                                        int cold_max, int* __restrict__ list, int4* __restrict__ tiles,
+                                                        int* __restrict__ ntiles, int* __restrict__ pairs,
+                                                        int* __restrict__ npairs, int* __restrict__ err) {
     __shared__ int cnt[kMaxExperts], off[kMaxExperts], toff[kMaxExperts];
+    __shared__ int np_s;
     const int n = T * k;
     for (int p = threadIdx.x; p < P; p += blockDim.x) list[p] = -1;
     for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    if (threadIdx.x == 0) np_s = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int e = ids[i];
@@ -764,12 +771,18 @@ __global__ void __launch_bounds__(1024) k_prefill_group(const int* __restrict__ 
         int o = 0, to = 0;
         for (int e = 0; e < E; ++e) {
             off[e] = o, toff[e] = to;
-            o += (cnt[e] + 15) & ~15;
-            to += (cnt[e] + kPfMaxN - 1) / kPfMaxN;
+            if (cnt[e] > cold_max) {
+                o += (cnt[e] + 15) & ~15;
+                to += (cnt[e] + kPfMaxN - 1) / kPfMaxN;
+            }
         }
         *ntiles = to;
     }
     __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = ids[i];
+        if (e >= 0 && e < E && cnt[e] <= cold_max) pairs[atomicAdd(&np_s, 1)] = i;
+    }
     // stable placement by one warp, 32 slots at a time: slot i goes after every smaller slot
     // of the same expert (rank among equal lanes from __match_any_sync)
     if (threadIdx.x < 32) {
@@ -777,7 +790,7 @@ __global__ void __launch_bounds__(1024) k_prefill_group(const int* __restrict__ 
         for (int i0 = 0; i0 < n; i0 += 32) {
             const int i = i0 + lane;
             const int e = i < n ? ids[i] : -1;
-            const bool valid = e >= 0 && e < E;
+            const bool valid = e >= 0 && e < E && cnt[e] > cold_max;
             const unsigned m = __match_any_sync(0xffffffffu, valid ? e : -1);
             const int rank = __popc(m & ((1u << lane) - 1u));
             const int base = valid ? off[e] : 0;
@@ -790,10 +803,87 @@ __global__ void __launch_bounds__(1024) k_prefill_group(const int* __restrict__ 
         }
     }
     __syncthreads();
+    if (threadIdx.x == 0) *npairs = np_s;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        if (cnt[e] <= cold_max) continue;
         const int start = off[e] - cnt[e];
         for (int j = 0; j * kPfMaxN < cnt[e]; ++j)
             tiles[toff[e] + j] = make_int4(e, start + j * kPfMaxN, min(kPfMaxN, cnt[e] - j * kPfMaxN), 0);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Row-dot path of the sparsely picked experts (pairs[]: one slot = one token of one expert):
+// the decode kernels' one-row-per-lane fast order (lane_row_partial) over whole rows, the
+// token's Q8_K activation read from global memory (L1 broadcast), one warp per 32 rows.
+// Persistent: one CTA of kPcThreads per SM, decode tables in shared memory.
+constexpr int kPcThreads = 512;
+constexpr size_t kPcSmem = kRowTableBytes + 2944 * 4;  // tables + their staging area
+
+__global__ void __launch_bounds__(kPcThreads, 1)
+    k_pairs_gateup(const ExpertDesc* __restrict__ desc, const int* __restrict__ ids, const int* __restrict__ pairs,
+                   const int* __restrict__ npairs, int k, const int8_t* __restrict__ qx, const float* __restrict__ dx,
+                   int dim, int ff, const uint32_t* __restrict__ tables, float* __restrict__ gu, int* __restrict__ err) {
+    const int np = *npairs;
+    if (np == 0) return;
+    fill_row_tables(tables, reinterpret_cast<uint32_t*>(clb_dyn_smem + kRowTableBytes));
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int groups = ff >> 5, nb = dim >> 8;
+    const int items = np * 2 * groups;
+    for (int it = blockIdx.x * nw + warp; it < items; it += gridDim.x * nw) {
+        const int pr = it / (2 * groups), rem = it - pr * 2 * groups;
+        const int mat = rem & 1, row = (rem >> 1) * 32 + lane;  // gate and up of the same rows adjacent
+        const int sl = pairs[pr], t = sl / k;
+        const ExpertDesc& ex = desc[ids[sl]];
+        const PackedMat& m = mat ? ex.up : ex.gate;
+        float y = 0.0f;
+        if (m.body != nullptr && m.k == dim && m.n == ff)
+            y = lane_row_partial_any<256>(m, row, 0, nb, qx + (size_t)t * dim, dx + (size_t)t * nb);
+        else if (lane == 0)
+            atomicExch(err, 1);
+        gu[((size_t)pr * 2 + mat) * ff + row] = y;
+    }
+}
+
+// SwiGLU of a pair's gate/up rows and Q8_K(h) (unpadded rows); one warp per 256 values.
+__global__ void __launch_bounds__(256) k_pairs_act(const int* __restrict__ npairs, int ff, float limit,
+                                                   const float* __restrict__ gu, int8_t* __restrict__ qh,
+                                                   float* __restrict__ dh) {
+    const int nbr = ff >> 8;
+    const int blk = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (blk >= *npairs * nbr) return;
+    const int p = blk / nbr, b = blk % nbr;
+    const float* g = gu + (size_t)p * 2 * ff + b * 256 + lane * 8;
+    const float* u = g + ff;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = swiglu(g[i], u[i], limit);
+    warp_quant_regs(v, qh + (size_t)p * ff + b * 256, dh + (size_t)p * nbr + b);
+}
+
+// Down rows of every pair into the slot-ordered expert rows y[slot][dim] that the combine reads.
+__global__ void __launch_bounds__(kPcThreads, 1)
+    k_pairs_down(const ExpertDesc* __restrict__ desc, const int* __restrict__ ids, const int* __restrict__ pairs,
+                 const int* __restrict__ npairs, const int8_t* __restrict__ qh, const float* __restrict__ dh, int dim,
+                 int ff, const uint32_t* __restrict__ tables, float* __restrict__ y, int* __restrict__ err) {
+    const int np = *npairs;
+    if (np == 0) return;
+    fill_row_tables(tables, reinterpret_cast<uint32_t*>(clb_dyn_smem + kRowTableBytes));
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int groups = dim >> 5, nbh = ff >> 8;
+    const int items = np * groups;
+    for (int it = blockIdx.x * nw + warp; it < items; it += gridDim.x * nw) {
+        const int pr = it / groups, row = (it - pr * groups) * 32 + lane;
+        const int sl = pairs[pr];
+        const PackedMat& m = desc[ids[sl]].down;
+        float v = 0.0f;
+        if (m.body != nullptr && m.k == ff && m.n == dim)
+            v = lane_row_partial_any<256>(m, row, 0, nbh, qh + (size_t)pr * ff, dh + (size_t)pr * nbh);
+        else if (lane == 0)
+            atomicExch(err, 1);
+        y[(size_t)sl * dim + row] = v;
     }
 }
 
@@ -949,6 +1039,11 @@ namespace {
 struct PrefillWs {
     int P;
     int* list;
+    int* pairs;
+    int* npairs;
+    float* pgu;
+    int8_t* pqh;
+    float* pdh;
     int4* tiles;
     int* ntiles;
     int8_t* qx;
@@ -974,6 +1069,9 @@ size_t carve(void* base, int T, int k, int dim, int ff, int E, PrefillWs* ws) {
         return r;
     };
     const size_t o_list = take(P * 4), o_tiles = take(((size_t)E + slots / kPfMaxN + 1) * 16), o_nt = take(16);
+    const size_t maxp = std::min<size_t>(slots, (size_t)E * kPfColdMax);  // row-dot pairs
+    const size_t o_pairs = take(slots * 4), o_np = take(16), o_pgu = take(maxp * 2 * ff * 4), o_pqh = take(maxp * ff),
+                 o_pdh = take(maxp * nbh * 4);
     const size_t o_qx = take((size_t)T * dim), o_dx = take((size_t)T * nbx * 4), o_qx16 = take((size_t)T * dim * 2);
     const size_t o_xg16 = take(P * dim * 2), o_dxg = take(nbx * P * 4), o_gu = take(P * 2 * ff * 4);
     const size_t o_qh = take(P * ff), o_qh16 = take(P * ff * 2), o_dhg = take(nbh * P * 4), o_y = take(slots * dim * 4);
@@ -981,6 +1079,11 @@ size_t carve(void* base, int T, int k, int dim, int ff, int E, PrefillWs* ws) {
         uint8_t* p = static_cast<uint8_t*>(base);
         ws->P = (int)P;
         ws->list = reinterpret_cast<int*>(p + o_list);
+        ws->pairs = reinterpret_cast<int*>(p + o_pairs);
+        ws->npairs = reinterpret_cast<int*>(p + o_np);
+        ws->pgu = reinterpret_cast<float*>(p + o_pgu);
+        ws->pqh = reinterpret_cast<int8_t*>(p + o_pqh);
+        ws->pdh = reinterpret_cast<float*>(p + o_pdh);
         ws->tiles = reinterpret_cast<int4*>(p + o_tiles);
         ws->ntiles = reinterpret_cast<int*>(p + o_nt);
         ws->qx = reinterpret_cast<int8_t*>(p + o_qx);
@@ -1050,9 +1153,16 @@ cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const 
     if ((e = cudaFuncSetAttribute(k_prefill_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PfSmem::total)) !=
         cudaSuccess)
         return e;
+    if ((e = cudaFuncSetAttribute(k_pairs_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPcSmem)) !=
+        cudaSuccess)
+        return e;
+    if ((e = cudaFuncSetAttribute(k_pairs_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPcSmem)) !=
+        cudaSuccess)
+        return e;
     const int nbx = dim / 256, nbh = ff / 256;
     if (phase_mask & 1) {
-        k_prefill_group<<<1, 1024, 0, s>>>(ids, T, k, E, P, ws.list, ws.tiles, ws.ntiles, err);
+        k_prefill_group<<<1, 1024, 0, s>>>(ids, T, k, E, P, kPfColdMax, ws.list, ws.tiles, ws.ntiles, ws.pairs,
+                                           ws.npairs, err);
         if (norm_x)
             k_prefill_norm_quant<<<T, 1024, 0, s>>>(x, dim, ws.qx, ws.dx, ws.qx16);
         else
@@ -1076,9 +1186,14 @@ cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const 
         g.mtiles = ff / 64;
         g.out = ws.gu;
         k_prefill_gemm<<<sms, kPfThreads, PfSmem::total, s>>>(g);
+        k_pairs_gateup<<<sms, kPcThreads, kPcSmem, s>>>(desc, ids, ws.pairs, ws.npairs, k, ws.qx, ws.dx, dim, ff,
+                                                         tables, ws.pgu, err);
     }
-    if (phase_mask & 4)
+    if (phase_mask & 4) {
         k_prefill_act<<<(P * nbh + 7) / 8, 256, 0, s>>>(ws.list, P, ff, limit, ws.gu, ws.qh, ws.qh16, ws.dhg);
+        const int maxp = std::min(T * k, E * kPfColdMax);
+        k_pairs_act<<<(maxp * nbh + 7) / 8, 256, 0, s>>>(ws.npairs, ff, limit, ws.pgu, ws.pqh, ws.pdh);
+    }
     if (phase_mask & 8) {
         if ((e = encode_bmaps(g.bmaps, ws.qh16, P, ff)) != cudaSuccess) return e;
         g.role = 1;
@@ -1088,6 +1203,8 @@ cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const 
         g.mtiles = dim / 128;
         g.out = ws.y;
         k_prefill_gemm<<<sms, kPfThreads, PfSmem::total, s>>>(g);
+        k_pairs_down<<<sms, kPcThreads, kPcSmem, s>>>(desc, ids, ws.pairs, ws.npairs, ws.pqh, ws.pdh, dim, ff, tables,
+                                                       ws.y, err);
     }
     if (phase_mask & 16) k_prefill_combine<<<T, 256, 0, s>>>(ws.y, ids, w, k, dim, resid, out);
     return cudaGetLastError();

@@ -248,8 +248,10 @@ __device__ __forceinline__ float seg_row_dot_t(const PackedMat& m, int row, cons
 // contiguous bytes. Returns the row's partial over blocks [b0, b1) in block order:
 // IQ2: 0.125 * sum d_b M_b; IQ1_M: sum d_b M_b + 0.125 * sum d_b D_b (block_sum's
 // integers, d_b = d_w * d_x). The caller adds the partials of a row's K segments in a
-// fixed order.
-template <int T>
+// fixed order. AS: byte stride of the activation's 256-value blocks (kActStride in shared
+// memory; 256 for an unpadded Q8_K row read from global memory, where the warp-wide
+// broadcast reads hit L1).
+template <int T, int AS = kActStride>
 __device__ __noinline__ float lane_row_partial(const PackedMat& m, int row, int b0, int b1, const int8_t* act_qs,
                                                const float* act_d) {
     constexpr int NP = T == CLB_IQ1_M ? 3 : 4;
@@ -275,7 +277,7 @@ __device__ __noinline__ float lane_row_partial(const PackedMat& m, int row, int 
         if (T != CLB_IQ2_XXS) r.sc = __ldg(reinterpret_cast<const uint2*>(sc));
         if (T != CLB_IQ1_M) r.d = __ldg(dp);
         int M, D;
-        block_sum<T>(r, act_qs + (size_t)b * kActStride, lb, M, D);
+        block_sum<T>(r, act_qs + (size_t)b * AS, lb, M, D);
         const float dd = __fmul_rn(raw_scale<T>(r), act_d[b]);
         acc = __fmaf_rn(dd, (float)M, acc);
         if (T == CLB_IQ1_M) dacc = __fmaf_rn(dd, (float)D, dacc);
@@ -286,11 +288,12 @@ __device__ __noinline__ float lane_row_partial(const PackedMat& m, int row, int 
     if (T == CLB_IQ1_M) return __fadd_rn(acc, __fmul_rn(0.125f, dacc));
     return __fmul_rn(0.125f, acc);
 }
+template <int AS = kActStride>
 __device__ __forceinline__ float lane_row_partial_any(const PackedMat& m, int row, int b0, int b1, const int8_t* aq,
                                                       const float* ad) {
-    if (m.type == CLB_IQ2_XXS) return lane_row_partial<CLB_IQ2_XXS>(m, row, b0, b1, aq, ad);
-    if (m.type == CLB_IQ2_XS) return lane_row_partial<CLB_IQ2_XS>(m, row, b0, b1, aq, ad);
-    return lane_row_partial<CLB_IQ1_M>(m, row, b0, b1, aq, ad);
+    if (m.type == CLB_IQ2_XXS) return lane_row_partial<CLB_IQ2_XXS, AS>(m, row, b0, b1, aq, ad);
+    if (m.type == CLB_IQ2_XS) return lane_row_partial<CLB_IQ2_XS, AS>(m, row, b0, b1, aq, ad);
+    return lane_row_partial<CLB_IQ1_M, AS>(m, row, b0, b1, aq, ad);
 }
 
 // S in {1, 2, 3, 4, 6, 8} (kSegChoices); anything else is treated as 1.
