@@ -379,20 +379,29 @@ def run_skewed(args, rank, world, local):
                           "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}), flush=True)
         return
-    if world > 1:
-        raise SystemExit("--skewed runs on one GPU (the batched stack needs every expert on its bank)")
+    import torch.distributed as dist
+
     torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     T, k, L = SK_BATCH, PICKS, args.layers
-    bank = cb.ExpertBank(n_layers=L, n_experts=args.experts, dim=DIM, ff=FF, max_picks=k, device=local)
+    if world > 1:  # expert-ID sharding: rank r holds experts [r*E/N, (r+1)*E/N); rows summed over NCCL per layer
+        from crosslane_b200.sharded import ShardedBank
+        bank = ShardedBank(n_layers=L, n_experts=args.experts, dim=DIM, ff=FF, max_picks=k, device=local, rank=rank,
+                           world=world)
+    else:
+        bank = cb.ExpertBank(n_layers=L, n_experts=args.experts, dim=DIM, ff=FF, max_picks=k, device=local)
     bank.fill_synthetic(SEED, args.policy)
     stream = torch.cuda.ExternalStream(bank.stream)
-    rng = np.random.default_rng(5000 + rank)
+    rng = np.random.default_rng(5000)  # the same batch on every rank
     n_in = 3
     xs = rng.standard_normal((n_in, T, DIM)).astype(np.float32)
     lgs = np.stack([zipf_logits(rng, L, T, args.experts) for _ in range(n_in)])
-    # algorithmic bytes: every distinct picked expert of every layer read once, + h in/out per layer
-    ebytes = {}
-    alg = []
+    # algorithmic bytes: every distinct picked expert of every layer read once (summed over the
+    # ranks that own them), + h in/out per layer
+    own_b, own_e = (bank.expert_begin, bank.expert_end) if world > 1 else (0, args.experts)
+    alg, distinct = [], []
     for i in range(n_in):
         tot = 0
         for l in range(L):
@@ -400,30 +409,38 @@ def run_skewed(args, rank, world, local):
             for t in range(T):
                 ids, _ = cb.route_host(0, lgs[i, l, t], k)
                 picked.update(int(e) for e in ids)
-            for e in picked:
-                if (l, e) not in ebytes:
-                    ebytes[(l, e)] = bank.expert_info(l, e)[1]
-                tot += ebytes[(l, e)]
-            tot += 2 * T * DIM * 4
+            tot += sum(bank.expert_info(l, e)[1] for e in picked if own_b <= e < own_e)
+            distinct.append(len(picked))
         alg.append(tot)
-    alg_bytes = float(np.mean(alg))
-    distinct = float(np.mean([len({int(e) for t in range(T) for e in cb.route_host(0, lgs[0, l, t], k)[0]})
-                              for l in range(L)]))
+    if world > 1:
+        t = torch.tensor(alg, dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        alg = t.cpu().tolist()
+    alg_bytes = float(np.mean(alg)) + L * 2 * T * DIM * 4
     d_x = torch.from_numpy(xs).cuda()
     d_lg = torch.from_numpy(lgs).cuda()
     d_h = torch.empty((T, DIM), dtype=torch.float32, device="cuda")
     d_ws = torch.empty(bank.stack_batch_workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    d_rows = torch.zeros((T * k, DIM), dtype=torch.float32, device="cuda") if world > 1 else None
     torch.cuda.synchronize()
+
+    def run(j):
+        if world > 1:
+            bank.stack_batch_device(0, L, d_h, d_lg[j], d_ws, d_rows)
+        else:
+            bank.stack_batch_device(0, L, d_h, d_lg[j], d_ws)
 
     def step(i):
         j = i % n_in
         with torch.cuda.stream(stream):
             d_h.copy_(d_x[j])
-        bank.stack_batch_device(0, L, d_h, d_lg[j], d_ws)
+        run(j)
 
     for i in range(args.warmup):
         step(i)
     bank.synchronize()
+    if world > 1:
+        dist.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -434,44 +451,87 @@ def run_skewed(args, rank, world, local):
         ev1.synchronize()
     ms = ev0.elapsed_time(ev1)
     bank.synchronize()
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     ms_per_step = ms / args.steps
     value = T * args.steps / (ms / 1e3)
-    # e2e: host h and logits through clb_stack_batch (host routing, copies in the timed region)
+    # e2e: host h and logits in, h out, through the public API
     e2e_steps = 2 if args.quick else max(2, min(args.steps, 5))
-    bank.stack_batch(0, L, xs[0], lgs[0])
-    t0 = time.perf_counter()
-    for i in range(e2e_steps):
-        bank.stack_batch(0, L, xs[i % n_in], lgs[i % n_in])
-    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    if world == 1:  # clb_stack_batch: host routing, copies inside the call
+        bank.stack_batch(0, L, xs[0], lgs[0])
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            bank.stack_batch(0, L, xs[i % n_in], lgs[i % n_in])
+        e2e_s = (time.perf_counter() - t0) / e2e_steps
+    else:  # pinned host buffers up, the sharded device path, h down
+        hx = torch.from_numpy(xs).pin_memory()
+        hl = torch.from_numpy(lgs).pin_memory()
+        hout = torch.empty((T, DIM), dtype=torch.float32).pin_memory()
+        d_l1 = torch.empty_like(d_lg[0])
+
+        def e2e_step(i):
+            j = i % n_in
+            with torch.cuda.stream(stream):
+                d_h.copy_(hx[j], non_blocking=True)
+                d_l1.copy_(hl[j], non_blocking=True)
+            bank.stack_batch_device(0, L, d_h, d_l1, d_ws, d_rows)
+            with torch.cuda.stream(stream):
+                hout.copy_(d_h, non_blocking=True)
+            stream.synchronize()
+
+        e2e_step(0)
+        dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            e2e_step(i)
+        e2e_s = (time.perf_counter() - t0) / e2e_steps
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
     hbm, hbm_kind = peaks()
     achieved = alg_bytes / (ms_per_step / 1e3) / 1e9
     cpu = None
-    if rank == 0 and not (args.no_cpu_baseline or args.quick):
+    if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
         cpu = cpu_baseline(samples=1)
         if cpu is not None:
             cpu["sample"] += "; the CPU lane decodes the batch token by token (no batched path)"
     line = {
         "metric": SK_METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "fp16 integers x fp16 integers -> fp32 (IQ x Q8_K)", "data": "synthetic",
         "config": {"workload": SK_WORKLOAD, "batch": T, "layers": L, "experts": args.experts, "dim": DIM, "ff": FF,
                    "picks": k, "types": "IQ2_XXS/IQ2_XS/IQ1_M per (layer, expert)",
                    "routing": "top-6 of log Zipf(1.1) over a per-layer seeded permutation + Gumbel noise",
-                   "distinct_experts_per_layer": round(distinct, 1), "parallelism": "single GPU",
+                   "distinct_experts_per_layer": round(float(np.mean(distinct)), 1),
+                   "parallelism": f"expert-ID sharded x{world}, rows all-reduced over NCCL per layer" if world > 1
+                   else "single GPU",
                    "l2": "inputs larger than L2: %.1f GB of distinct expert weights per step" % (alg_bytes / 1e9)},
         "e2e": {"value": round(T / e2e_s, 1), "unit": "tok/s",
                 "h2d_bytes_per_step": T * DIM * 4 + L * T * k * 8, "d2h_bytes_per_step": T * DIM * 4},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": None,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm * world, "unit": "GB/s",
+                     "frac": round(achieved / (hbm * world), 4), "traffic": None,
                      "kernel": "whole step (per layer: route, group, norm+Q8_K, gather, 2 x clb::k_prefill_gemm, "
                                "SwiGLU+Q8_K, combine)",
                      "algorithmic_bytes_per_step": alg_bytes, "peak_source": hbm_kind},
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
-        "gpu_launches": 8 * L * args.steps,
+        "gpu_launches": 11 * L * args.steps,
     }
-    print(json.dumps(line), flush=True)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    # tensors used on the bank stream (the all-reduce recorded it on them) go before the stream
+    torch.cuda.synchronize()
+    del d_x, d_lg, d_h, d_ws, d_rows
+    if world > 1:
+        del hx, hl, hout, d_l1
+    torch.cuda.synchronize()
     bank.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():

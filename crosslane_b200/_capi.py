@@ -99,6 +99,7 @@ SIGNATURES = {
     "clb_stack_batch_workspace_bytes": (C.c_uint64, [_P, _I]),
     "clb_stack_batch_device": (_I, [_P, _U32, _I, _I, _P, _P, _P, C.c_uint64, _P, _PE]),
     "clb_stack_batch": (_I, [_P, _U32, _I, _I, _P, _P, _PE]),
+    "clb_stack_batch_layer_device": (_I, [_P, _U32, _I, _P, _P, _P, _P, C.c_uint64, _I, _P, _PE]),
     "clb_bank_stream": (_P, [_P]),
     "clb_bank_synchronize": (_I, [_P, _PE]),
     "clb_warm_execute": (_I, [_P, _U32, _P, _P, _I, _P, _P, HOST_EXPERT_FN, _P, _P, _PE]),

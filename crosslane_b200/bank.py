@@ -277,6 +277,15 @@ class ExpertBank:
             self._h, first_layer, n_layers, d_h.shape[0], C.c_void_p(d_logits.data_ptr()), C.c_void_p(d_h.data_ptr()),
             C.c_void_p(d_ws.data_ptr()), d_ws.numel(), C.c_void_p(stream) if stream else None, C.byref(err)), err)
 
+    def stack_batch_layer_device(self, layer: int, d_h, d_logits, d_rows, d_ws, phase_mask: int, stream=None) -> None:
+        """One layer of the batched stack (clb_stack_batch_layer_device): phase bit 1 computes
+        this bank's expert rows into d_rows [T*k][dim], bit 2 adds the combine of d_rows to d_h."""
+        err = ErrorV1()
+        check(lib.clb_stack_batch_layer_device(
+            self._h, layer, d_h.shape[0], C.c_void_p(d_logits.data_ptr()), C.c_void_p(d_h.data_ptr()),
+            C.c_void_p(d_rows.data_ptr()), C.c_void_p(d_ws.data_ptr()), d_ws.numel(), phase_mask,
+            C.c_void_p(stream) if stream else None, C.byref(err)), err)
+
     def expert_info(self, layer: int, expert: int):
         """(ggml type id, payload bytes of gate+up+down) of a resident expert."""
         t = C.c_int32()

@@ -1241,6 +1241,48 @@ int32_t clb_stack_batch_device(clb_bank* bank, uint32_t first, int32_t nl, int32
     });
 }
 
+int32_t clb_stack_batch_layer_device(clb_bank* bank, uint32_t layer, int32_t tokens, const float* d_logits, float* d_h,
+                                     float* d_rows, void* d_ws, uint64_t ws_bytes, int32_t phase_mask, void* stream,
+                                     clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    return guarded(err, [&] {
+        bank->check_usable();
+        const auto& c = bank->cfg;
+        require(layer < (uint32_t)c.n_layers, CLB_E_INVALID, "layer %u out of range", layer);
+        require(tokens >= 1 && tokens <= (1 << 16) && (int64_t)tokens * c.max_picks <= (1 << 24), CLB_E_INVALID,
+                "invalid batch size (%d tokens)", tokens);
+        require(clb::prefill_shape_supported(c.dim, c.ff), CLB_E_UNSUPPORTED,
+                "batched stack decode needs dim, ff multiples of 256 in [512, 8192]");
+        require(phase_mask >= 1 && phase_mask <= 3, CLB_E_INVALID, "invalid phase mask");
+        require(d_logits && d_h && d_rows && d_ws, CLB_E_INVALID, "null device buffer");
+        require(ws_bytes >= clb_stack_batch_workspace_bytes(bank, tokens), CLB_E_INVALID,
+                "stack batch workspace too small");
+        for (int e = c.expert_begin; e < c.expert_end; ++e)
+            require(bank->resident[(size_t)layer * bank->E() + (size_t)e], CLB_E_INVALID, "expert (%u, %d) not resident",
+                    layer, e);
+        DeviceGuard g(c.device);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : bank->stream;
+        bank->device_step([&] {
+            const int k = c.max_picks;
+            int* ids = nullptr;
+            float* w = nullptr;
+            clb::stack_batch_routes(d_ws, tokens, k, c.dim, c.ff, c.n_experts, &ids, &w);
+            const clb::ExpertDesc* desc = bank->d_desc + (size_t)layer * bank->E();
+            if (phase_mask & 1) {  // route, RMSNorm + Q8_K, this bank's experts into d_rows
+                cuda_check(clb::launch_route_sigmoid(d_logits, c.n_experts, k, tokens, ids, w, s), "route");
+                cuda_check(clb::launch_prefill(desc, c.n_experts, d_h, ids, w, tokens, k, c.dim, c.ff, c.limit, d_h, d_h,
+                                               d_ws, bank->d_err, 1 | 2 | 4 | 8, s, true, c.expert_begin, c.expert_end,
+                                               d_rows),
+                           "stack batch layer");
+            }
+            if (phase_mask & 2)  // h += ascending-id combine of every pick's row
+                cuda_check(clb::launch_prefill(desc, c.n_experts, d_h, ids, w, tokens, k, c.dim, c.ff, c.limit, d_h, d_h,
+                                               d_ws, bank->d_err, 16, s, true, c.expert_begin, c.expert_end, d_rows),
+                           "stack batch combine");
+        });
+    });
+}
+
 int32_t clb_stack_batch(clb_bank* bank, uint32_t first, int32_t nl, int32_t tokens, const float* logits, float* h,
                         clb_error_v1* err) {
     if (!bank) return fail(err, CLB_E_INVALID, "null bank");

@@ -61,10 +61,16 @@ cudaError_t launch_mv2(const PackedMat& m, const void* q, float* y, cudaStream_t
 // phase_mask: 1 group + quantise x, 2 gate/up GEMM, 4 SwiGLU + quantise h, 8 down GEMM, 16 combine.
 size_t prefill_workspace_bytes(int T, int k, int dim, int ff, int E);
 bool prefill_shape_supported(int dim, int ff);
-// norm_x: x <- RMSNorm(x) (the stack's fixed-order pre-norm) before Q8_K.
+// norm_x: x <- RMSNorm(x) (the stack's fixed-order pre-norm) before Q8_K. Only picks of
+// experts [e_begin, e_end) are computed (e_end < 0: all); with a partial range the expert
+// rows of the other picks are zero. rows: caller-owned expert rows [T*k][dim] (slot order)
+// instead of the workspace's.
 cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const int* ids, const float* w, int T, int k,
                            int dim, int ff, float limit, const float* resid, float* out, void* ws, int* err,
-                           int phase_mask, cudaStream_t s, bool norm_x = false);
+                           int phase_mask, cudaStream_t s, bool norm_x = false, int e_begin = 0, int e_end = -1,
+                           float* rows = nullptr);
+// The routing slots of the batched stack's workspace: ids [T][k] and weights [T][k].
+void stack_batch_routes(void* ws, int T, int k, int dim, int ff, int E, int** ids, float** w);
 // T tokens through nl layers (desc [nl][E]): h <- h + layer(RMSNorm(h)) per layer, in place.
 // Routes from ids_all / w_all ([nl][T][k]) or, when those are null, from logits ([nl][T][E]).
 size_t stack_batch_workspace_bytes(int T, int k, int dim, int ff, int E);

@@ -751,9 +751,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
 // to pairs[] (*npairs of them, in no particular order) for the row-dot path, which decodes a
 // weight for one token at a third of the GEMM decoder's cost per weight.
 __global__ void __launch_bounds__(1024) k_prefill_group(const int* __restrict__ ids, int T, int k, int E, int P,
-                                                        int cold_max, int* __restrict__ list, int4* __restrict__ tiles,
-                                                        int* __restrict__ ntiles, int* __restrict__ pairs,
-                                                        int* __restrict__ npairs, int* __restrict__ err) {
+                                                        int e_begin, int e_end, int cold_max, int* __restrict__ list,
+                                                        int4* __restrict__ tiles, int* __restrict__ ntiles,
+                                                        int* __restrict__ pairs, int* __restrict__ npairs,
+                                                        int* __restrict__ err) {
     __shared__ int cnt[kMaxExperts], off[kMaxExperts], toff[kMaxExperts];
     __shared__ int np_s;
     const int n = T * k;
@@ -764,7 +765,7 @@ __global__ void __launch_bounds__(1024) k_prefill_group(const int* __restrict__ 
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int e = ids[i];
         if (e < 0 || e >= E) atomicExch(err, 1);
-        else atomicAdd(&cnt[e], 1);
+        else if (e >= e_begin && e < e_end) atomicAdd(&cnt[e], 1);  // picks of other GPUs' experts are skipped
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -781,7 +782,7 @@ __global__ void __launch_bounds__(1024) k_prefill_group(const int* __restrict__ 
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int e = ids[i];
-        if (e >= 0 && e < E && cnt[e] <= cold_max) pairs[atomicAdd(&np_s, 1)] = i;
+        if (e >= e_begin && e < e_end && cnt[e] <= cold_max) pairs[atomicAdd(&np_s, 1)] = i;
     }
     // stable placement by one warp, 32 slots at a time: slot i goes after every smaller slot
     // of the same expert (rank among equal lanes from __match_any_sync)
@@ -790,7 +791,7 @@ __global__ void __launch_bounds__(1024) k_prefill_group(const int* __restrict__ 
         for (int i0 = 0; i0 < n; i0 += 32) {
             const int i = i0 + lane;
             const int e = i < n ? ids[i] : -1;
-            const bool valid = e >= 0 && e < E && cnt[e] > cold_max;
+            const bool valid = e >= e_begin && e < e_end && cnt[e] > cold_max;
             const unsigned m = __match_any_sync(0xffffffffu, valid ? e : -1);
             const int rank = __popc(m & ((1u << lane) - 1u));
             const int base = valid ? off[e] : 0;
@@ -805,7 +806,7 @@ __global__ void __launch_bounds__(1024) k_prefill_group(const int* __restrict__ 
     __syncthreads();
     if (threadIdx.x == 0) *npairs = np_s;
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        if (cnt[e] <= cold_max) continue;
+        if (e < e_begin || e >= e_end || cnt[e] <= cold_max) continue;
         const int start = off[e] - cnt[e];
         for (int j = 0; j * kPfMaxN < cnt[e]; ++j)
             tiles[toff[e] + j] = make_int4(e, start + j * kPfMaxN, min(kPfMaxN, cnt[e] - j * kPfMaxN), 0);
@@ -1140,9 +1141,11 @@ cudaError_t encode_bmaps(CUtensorMap* maps, const __half* base, int P, int K) {
 
 cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const int* ids, const float* w, int T, int k,
                            int dim, int ff, float limit, const float* resid, float* out, void* wsp, int* err,
-                           int phase_mask, cudaStream_t s, bool norm_x) {
+                           int phase_mask, cudaStream_t s, bool norm_x, int e_begin, int e_end, float* rows) {
     PrefillWs ws{};
     carve(wsp, T, k, dim, ff, E, &ws);
+    if (e_end < 0) e_end = E;
+    if (rows) ws.y = rows;
     const int P = ws.P;
     const uint32_t* tables = nullptr;
     cudaError_t e = tables_device_ptr(&tables);
@@ -1161,8 +1164,11 @@ cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const 
         return e;
     const int nbx = dim / 256, nbh = ff / 256;
     if (phase_mask & 1) {
-        k_prefill_group<<<1, 1024, 0, s>>>(ids, T, k, E, P, kPfColdMax, ws.list, ws.tiles, ws.ntiles, ws.pairs,
-                                           ws.npairs, err);
+        k_prefill_group<<<1, 1024, 0, s>>>(ids, T, k, E, P, e_begin, e_end, kPfColdMax, ws.list, ws.tiles,
+                                           ws.ntiles, ws.pairs, ws.npairs, err);
+        // rows of other GPUs' picks stay zero, so a sum over the GPUs' row buffers is exact
+        if ((e_begin > 0 || e_end < E) && (e = cudaMemsetAsync(ws.y, 0, (size_t)T * k * dim * 4, s)) != cudaSuccess)
+            return e;
         if (norm_x)
             k_prefill_norm_quant<<<T, 1024, 0, s>>>(x, dim, ws.qx, ws.dx, ws.qx16);
         else
@@ -1219,6 +1225,14 @@ size_t stack_batch_workspace_bytes(int T, int k, int dim, int ff, int E) {
     const size_t a = (prefill_workspace_bytes(T, k, dim, ff, E) + 255) & ~(size_t)255;
     const size_t r = ((size_t)T * k * 4 + 255) & ~(size_t)255;
     return a + 2 * r + (size_t)T * dim * 4;
+}
+
+void stack_batch_routes(void* wsp, int T, int k, int dim, int ff, int E, int** ids, float** w) {
+    uint8_t* base = static_cast<uint8_t*>(wsp);
+    const size_t a = (prefill_workspace_bytes(T, k, dim, ff, E) + 255) & ~(size_t)255;
+    const size_t r = ((size_t)T * k * 4 + 255) & ~(size_t)255;
+    *ids = reinterpret_cast<int*>(base + a);
+    *w = reinterpret_cast<float*>(base + a + r);
 }
 
 cudaError_t launch_stack_batch(const ExpertDesc* desc, int E, int nl, const float* logits, const int* ids_all,

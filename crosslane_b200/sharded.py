@@ -7,6 +7,11 @@ stack together: every rank calls `stack_decode*` with the same token, computes t
 it owns, and the rows of every pick reach every GPU through peer stores inside the
 persistent kernel (clb_bank_connect). Mirrors the lane split of crosslane's
 `warm_execute` (runtime.cpp:121-189), with GPUs in place of lanes.
+
+The batched stack (`stack_batch_device`, a batch of tokens per step) exchanges per layer
+the [T*k][dim] expert rows: each rank fills the rows of the picks it owns (the others are
+zero), an all-reduce (sum) over the process group (NCCL on GPUs) gives every rank every
+row exactly, and every rank runs the same ascending-id combine.
 """
 from __future__ import annotations
 
@@ -50,3 +55,19 @@ class ShardedBank(ExpertBank):
         self.rank, self.world = rank, world
         if world > 1:
             self.connect(rank, world, exchange_handles(self.exchange_handle(), group))
+
+    def stack_batch_device(self, first_layer: int, n_layers: int, d_h, d_logits, d_ws, d_rows, group=None) -> None:
+        """d_h [T][dim] (identical on every rank, updated in place), d_logits [n_layers][T][E],
+        d_ws (stack_batch_workspace_bytes), d_rows float32 [T*k][dim]; all on this rank's GPU,
+        enqueued on the bank stream (the all-reduce is ordered on it too, which makes torch's
+        allocator record that stream on d_rows: free d_rows before closing the bank)."""
+        import torch
+        import torch.distributed as dist
+
+        stream = torch.cuda.ExternalStream(self.stream)
+        with torch.cuda.stream(stream):
+            for l in range(n_layers):
+                self.stack_batch_layer_device(first_layer + l, d_h, d_logits[l], d_rows, d_ws, 1)
+                if self.world > 1:
+                    dist.all_reduce(d_rows, group=group)
+                self.stack_batch_layer_device(first_layer + l, d_h, d_logits[l], d_rows, d_ws, 2)

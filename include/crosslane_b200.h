@@ -343,6 +343,20 @@ int32_t clb_stack_batch_device(clb_bank* bank, uint32_t first_layer, int32_t n_l
 int32_t clb_stack_batch(clb_bank* bank, uint32_t first_layer, int32_t n_layers, int32_t tokens, const float* logits,
                         float* h, clb_error_v1* err);
 
+/* One layer of the batched stack in two phases, for expert-ID sharding over GPUs (the bank
+ * holds experts [expert_begin, expert_end) and the caller sums the GPUs' row buffers):
+ *   phase bit 1: route d_logits [tokens][n_experts] on the device, RMSNorm + Q8_K of d_h,
+ *                and this bank's picks into d_rows [tokens * max_picks][dim] (slot t*k+p;
+ *                the rows of other banks' picks are zero);
+ *   phase bit 2: d_h += the ascending-id combine of the rows of every pick.
+ * Between the two, an element-wise sum of d_rows over the GPUs (e.g. an NCCL all-reduce)
+ * gives every GPU every row exactly (each row is non-zero on one GPU only), so the GPUs'
+ * residual streams stay identical. The workspace is clb_stack_batch_workspace_bytes and
+ * must be kept between the phases of a layer. */
+int32_t clb_stack_batch_layer_device(clb_bank* bank, uint32_t layer, int32_t tokens, const float* d_logits,
+                                     float* d_h, float* d_rows, void* d_ws, uint64_t ws_bytes, int32_t phase_mask,
+                                     void* stream, clb_error_v1* err);
+
 /* The bank's CUDA stream (cudaStream_t) and a synchronisation helper. */
 void* clb_bank_stream(clb_bank* bank);
 int32_t clb_bank_synchronize(clb_bank* bank, clb_error_v1* err);

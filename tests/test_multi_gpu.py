@@ -36,3 +36,28 @@ def test_sharded_stack_two_gpus(orc, tmp_path):
     want = orc.stack(2, 4242, x0, logits[0], dim, ff, k=k)
     bound = max(1e-3, 4 * orc.stack_sensitivity(2, 4242, x0, logits[0], dim, ff, k))
     assert rel_l2(d0["host_0"][0], want) <= bound
+
+
+@pytest.mark.gpu
+def test_sharded_batched_stack_two_gpus(orc, tmp_path):
+    """Batched stack sharded by expert ID over 2 GPUs (per-layer all-reduce of the expert
+    rows over NCCL): both GPUs hold the same residual streams, bit-identical to the
+    unsharded batched stack on one GPU, and within the stack's drift bound of the oracle."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", "29541",
+           os.path.join(HERE, "sharded_batch_worker.py"), "--out", str(tmp_path)]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    d0, d1 = (np.load(tmp_path / f"batch_rank{i}.npz") for i in range(2))
+    assert np.array_equal(bits(d0["sharded"]), bits(d1["sharded"]))
+    assert np.array_equal(bits(d0["sharded"]), bits(d0["single"])), "sharded differs from one GPU"
+    h0, logits = d0["h0"], d0["logits"]
+    dim, ff, k, seed = 1024, 512, 6, 606
+    for t in range(0, h0.shape[0], 7):
+        want = orc.stack(2, seed, h0[t], logits[:, t, :], dim, ff, k)
+        bound = max(1e-3, 4 * orc.stack_sensitivity(2, seed, h0[t], logits[:, t, :], dim, ff, k))
+        assert rel_l2(d0["sharded"][t], want) <= bound, t
