@@ -89,6 +89,9 @@ SIGNATURES = {
     "clb_bank_expert_info": (_I, [_P, _U32, _I, C.POINTER(_I), C.POINTER(C.c_uint64)]),
     "clb_route_device": (_I, [_I, _P, _I, _I, _I, _P, _P, _P]),
     "clb_route_host": (_I, [_I, _P, _P, _I, _I, _F, _P, _P]),
+    "clb_router_device": (_I, [_P, _I, _I, _P, _I, _P, _P]),
+    "clb_route_b_device": (_I, [_P, _P, _I, _I, _I, _F, _P, _P, _P, _P]),
+    "clb_moe_block_device": (_I, [_P, _U32, _P, _P, _P, _F, _P, _P, _P, _P, _P, _P, _P, _PE]),
     "clb_stack_decode": (_I, [_P, _U32, _I, _P, _P, _P, _PE]),
     "clb_stack_decode_device": (_I, [_P, _U32, _I, _P, _P, _PE]),
     "clb_prefill_workspace_bytes": (C.c_uint64, [_P, _I, _I]),

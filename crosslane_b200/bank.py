@@ -286,6 +286,15 @@ class ExpertBank:
             C.c_void_p(d_rows.data_ptr()), C.c_void_p(d_ws.data_ptr()), d_ws.numel(), phase_mask,
             C.c_void_p(stream) if stream else None, C.byref(err)), err)
 
+    def moe_block_device(self, layer: int, d_x, d_gate_w, d_bias, scale: float, d_out, d_logits, d_ids, d_w,
+                         d_shared=None, d_resid=None, stream=None) -> None:
+        """Router + route_cpu + experts + combine of one token on the device (clb_moe_block_device)."""
+        err = ErrorV1()
+        vp = lambda t: C.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+        check(lib.clb_moe_block_device(self._h, layer, vp(d_x), vp(d_gate_w), vp(d_bias), scale, vp(d_shared),
+                                       vp(d_resid), vp(d_out), vp(d_logits), vp(d_ids), vp(d_w),
+                                       C.c_void_p(stream) if stream else None, C.byref(err)), err)
+
     def expert_info(self, layer: int, expert: int):
         """(ggml type id, payload bytes of gate+up+down) of a resident expert."""
         t = C.c_int32()
@@ -351,3 +360,19 @@ def q8k_activate(d_g, d_u, d_h, limit: float = 0.0, stream=None) -> None:
 def route_device(d_logits, n_experts: int, k: int, tokens: int, d_ids, d_w, stream=None) -> None:
     check(lib.clb_route_device(0, C.c_void_p(d_logits.data_ptr()), n_experts, k, tokens, C.c_void_p(d_ids.data_ptr()),
                                C.c_void_p(d_w.data_ptr()), _stream(stream)), what="clb_route_device")
+
+
+def router_device(d_x, d_gate_w, d_logits, stream=None) -> None:
+    """d_logits [T][E] = d_gate_w [E][dim] . d_x [T][dim] (fp32, torch tensors on the device)."""
+    T, dim = d_x.shape
+    check(lib.clb_router_device(C.c_void_p(d_x.data_ptr()), T, dim, C.c_void_p(d_gate_w.data_ptr()),
+                                d_gate_w.shape[0], C.c_void_p(d_logits.data_ptr()), _stream(stream)),
+          what="clb_router_device")
+
+
+def route_b_device(d_logits, d_bias, k: int, scale: float, d_ids, d_w, d_status, stream=None) -> None:
+    """route_cpu on the device: d_logits [T][E], d_bias [E] -> d_ids/d_w [T][k]; d_status int32 [1]."""
+    T, E = d_logits.shape
+    check(lib.clb_route_b_device(C.c_void_p(d_logits.data_ptr()), C.c_void_p(d_bias.data_ptr()), E, k, T, scale,
+                                 C.c_void_p(d_ids.data_ptr()), C.c_void_p(d_w.data_ptr()),
+                                 C.c_void_p(d_status.data_ptr()), _stream(stream)), what="clb_route_b_device")

@@ -913,6 +913,54 @@ int32_t clb_bank_expert_info(const clb_bank* bank, uint32_t layer, int32_t exper
     return CLB_OK;
 }
 
+int32_t clb_router_device(const float* d_x, int32_t tokens, int32_t dim, const float* d_gate_w, int32_t n_experts,
+                          float* d_logits, void* stream) {
+    if (!d_x || !d_gate_w || !d_logits || tokens <= 0 || dim <= 0 || dim % 4 != 0 || n_experts <= 0 ||
+        n_experts > clb::kMaxExperts)
+        return CLB_E_INVALID;
+    return clb::launch_router_gemv(d_gate_w, d_x, n_experts, dim, tokens, d_logits,
+                                   static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? CLB_OK
+               : CLB_E_CUDA;
+}
+
+int32_t clb_route_b_device(const float* d_logits, const float* d_bias, int32_t n_experts, int32_t k, int32_t tokens,
+                           float scale, int32_t* d_ids, float* d_w, int32_t* d_status, void* stream) {
+    if (!d_logits || !d_bias || !d_ids || !d_w || !d_status || n_experts <= 0 || n_experts > clb::kMaxExperts ||
+        k <= 0 || k > clb::kMaxPicks || k > n_experts || tokens <= 0 || !std::isfinite(scale) || scale < 0)
+        return CLB_E_INVALID;
+    return clb::launch_route_b(d_logits, d_bias, n_experts, k, tokens, scale, d_ids, d_w, d_status,
+                               static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? CLB_OK
+               : CLB_E_CUDA;
+}
+
+int32_t clb_moe_block_device(clb_bank* bank, uint32_t layer, const float* d_x, const float* d_gate_w,
+                             const float* d_bias, float scale, const float* d_shared, const float* d_resid,
+                             float* d_out, float* d_logits, int32_t* d_ids, float* d_w, void* stream,
+                             clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    return guarded(err, [&] {
+        bank->check_usable();
+        const auto& c = bank->cfg;
+        require(layer < (uint32_t)c.n_layers && d_x && d_gate_w && d_bias && d_out && d_logits && d_ids && d_w,
+                CLB_E_INVALID, "invalid MoE block arguments");
+        require(std::isfinite(scale) && scale >= 0, CLB_E_INVALID, "route scale must be finite and >= 0");
+        require(c.n_experts <= 1024, CLB_E_UNSUPPORTED, "device routing handles at most 1024 experts");
+        DeviceGuard g(c.device);
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : bank->stream;
+        bank->device_step([&] {
+            // router logits, route_cpu's selection, the experts and the ascending-id combine:
+            // one stream, no host round trip (the picks' residency is checked on the device)
+            cuda_check(clb::launch_router_gemv(d_gate_w, d_x, c.n_experts, c.dim, 1, d_logits, s), "router");
+            cuda_check(clb::launch_route_b(d_logits, d_bias, c.n_experts, c.max_picks, 1, scale, d_ids, d_w,
+                                           bank->d_err, s),
+                       "route");
+            bank->enqueue_layer(layer, d_ids, d_w, c.max_picks, d_x, d_shared, d_resid, d_out, nullptr, s);
+        });
+    });
+}
+
 int32_t clb_route_device(int32_t mode, const float* d_logits, int32_t n_experts, int32_t k, int32_t tokens,
                          int32_t* d_ids, float* d_w, void* stream) {
     if (mode != 0 || !d_logits || !d_ids || !d_w || n_experts <= 0 || n_experts > clb::kMaxExperts || k <= 0 ||

@@ -1,6 +1,7 @@
 // sm_100a kernels of the routed-expert decode path. See clb_device.cuh for the
 // arithmetic contract and clb_types.h for the packed weight layout.
 #include <cuda_runtime.h>
+#include <cfloat>
 
 #include <algorithm>
 #include <cstdlib>
@@ -311,6 +312,90 @@ __global__ void k_route_sigmoid(const float* __restrict__ logits, int n, int k, 
 }
 
 // ------------------------------------------------------------------------------
+// Router logits on the device: logits[t][e] = gate_w[e] . x[t] in fp32, one warp per
+// (token, expert): lane j accumulates float4 groups j, j + 32, ... with fused multiply-adds
+// in order, then a butterfly sum over the lanes (fixed order: run-to-run identical).
+__global__ void __launch_bounds__(256) k_router_gemv(const float* __restrict__ gw, const float* __restrict__ x, int n,
+                                                     int dim, int tokens, float* __restrict__ logits) {
+    const int item = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (item >= n * tokens) return;
+    const int t = item / n, e = item - t * n;
+    const float4* wr = reinterpret_cast<const float4*>(gw + (size_t)e * dim);
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * dim);
+    float acc = 0.0f;
+    for (int i = lane; i < (dim >> 2); i += 32) {
+        const float4 a = __ldg(wr + i), v = __ldg(xr + i);
+        acc = __fmaf_rn(a.x, v.x, acc);
+        acc = __fmaf_rn(a.y, v.y, acc);
+        acc = __fmaf_rn(a.z, v.z, acc);
+        acc = __fmaf_rn(a.w, v.w, acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+    if (lane == 0) logits[(size_t)t * n + e] = acc;
+}
+
+// Mode-B routing on the device (crosslane route_cpu, engine/strata/sycl/route/route.cpp:15-37):
+// sc = sqrt(softplus(l)) with softplus(l) = l above 20, else log1p(exp(l)) as two float
+// roundings (exp and log1p evaluated in double and rounded once each: the correctly rounded
+// float results); selection by sc + bias, largest first, ties to the lower id; sum of the
+// picks' sc in selection order; w = sc / (sum + 1e-20) * scale. One CTA per token, one
+// thread per expert (n <= 1024). A non-finite score sets *err = 1.
+__global__ void __launch_bounds__(1024) k_route_b(const float* __restrict__ logits, const float* __restrict__ bias, int n,
+                                                  int k, float scale, int* __restrict__ ids, float* __restrict__ w,
+                                                  int* __restrict__ err) {
+    __shared__ float scs[1024];
+    __shared__ float wbest[32];
+    __shared__ int wi[32];
+    __shared__ int pick[kMaxPicks];
+    const int t = blockIdx.x, e = threadIdx.x, lane = e & 31, warp = e >> 5;
+    float sc = 0.0f, bs = -FLT_MAX;
+    if (e < n) {
+        const float l = logits[(size_t)t * n + e];
+        const float sp = l > 20.0f ? l : (float)log1p((double)(float)exp((double)l));
+        sc = __fsqrt_rn(sp);
+        bs = __fadd_rn(sc, bias[e]);
+        if (!isfinite(bs)) atomicExch(err, 1);
+        scs[e] = sc;
+    }
+    for (int i = 0; i < k; ++i) {
+        float v = e < n ? bs : -INFINITY;
+        int vi = e < n ? e : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, vi, o);
+            if (ov > v || (ov == v && oi < vi)) v = ov, vi = oi;
+        }
+        if (lane == 0) wbest[warp] = v, wi[warp] = vi;
+        __syncthreads();
+        if (warp == 0) {
+            const int nw = (blockDim.x + 31) >> 5;
+            v = lane < nw ? wbest[lane] : -INFINITY;
+            vi = lane < nw ? wi[lane] : 0x7fffffff;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, vi, o);
+                if (ov > v || (ov == v && oi < vi)) v = ov, vi = oi;
+            }
+            if (lane == 0) pick[i] = vi;
+        }
+        __syncthreads();
+        if (e == pick[i]) bs = -FLT_MAX;  // the host marks a chosen expert with the lowest float
+    }
+    if (e == 0) {
+        float sum = 0.0f;
+        for (int i = 0; i < k; ++i) sum = __fadd_rn(sum, scs[pick[i]]);
+        const float den = __fadd_rn(sum, 1e-20f);
+        for (int i = 0; i < k; ++i) {
+            ids[(size_t)t * k + i] = pick[i];
+            w[(size_t)t * k + i] = __fmul_rn(__fdiv_rn(scs[pick[i]], den), scale);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------
 // Synthetic fill: one thread per ggml block, written straight into the packed layout.
 __global__ void k_synth_fill(uint8_t* __restrict__ packed, PackedLayout l, int type, int n, int k, uint64_t seed,
                              uint32_t layer, uint32_t expert, uint32_t role, const uint16_t* __restrict__ scales) {
@@ -389,6 +474,16 @@ cudaError_t launch_down_combine(const ExpertDesc* experts, const int* ids, const
 }
 cudaError_t launch_route_sigmoid(const float* logits, int n, int k, int tokens, int* ids, float* w, cudaStream_t s) {
     k_route_sigmoid<<<(tokens + 3) / 4, 128, 0, s>>>(logits, n, k, tokens, ids, w);
+    return cudaGetLastError();
+}
+cudaError_t launch_router_gemv(const float* gate_w, const float* x, int n, int dim, int tokens, float* logits,
+                               cudaStream_t s) {
+    k_router_gemv<<<(n * tokens + 7) / 8, 256, 0, s>>>(gate_w, x, n, dim, tokens, logits);
+    return cudaGetLastError();
+}
+cudaError_t launch_route_b(const float* logits, const float* bias, int n, int k, int tokens, float scale, int* ids,
+                           float* w, int* err, cudaStream_t s) {
+    k_route_b<<<tokens, (n + 31) / 32 * 32, 0, s>>>(logits, bias, n, k, scale, ids, w, err);
     return cudaGetLastError();
 }
 cudaError_t launch_synth_fill(uint8_t* packed, const PackedLayout& l, int type, int n, int k, uint64_t seed,

@@ -40,6 +40,12 @@ cudaError_t launch_down_combine(const ExpertDesc* experts, const int* ids, const
                                 const int8_t* hqs, const float* hd, int dim, int ff, const float* shared,
                                 const float* resid, float* out, float* y_rows, int* err, cudaStream_t s);
 cudaError_t launch_route_sigmoid(const float* logits, int n, int k, int tokens, int* ids, float* w, cudaStream_t s);
+// logits [tokens][n] = gate_w [n][dim] . x [tokens][dim] (fp32, fixed order); dim % 4 == 0.
+cudaError_t launch_router_gemv(const float* gate_w, const float* x, int n, int dim, int tokens, float* logits,
+                               cudaStream_t s);
+// route_cpu (mode B) on the device; n <= 1024; *err = 1 on a non-finite score.
+cudaError_t launch_route_b(const float* logits, const float* bias, int n, int k, int tokens, float scale, int* ids,
+                           float* w, int* err, cudaStream_t s);
 cudaError_t launch_synth_fill(uint8_t* packed, const PackedLayout& l, int type, int n, int k, uint64_t seed,
                               uint32_t layer, uint32_t expert, uint32_t role, const uint16_t* scales, cudaStream_t s);
 cudaError_t launch_pack(const uint8_t* aos, uint8_t* packed, const PackedLayout& l, int type, int n, int k, int* bad,

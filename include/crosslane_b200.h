@@ -260,6 +260,34 @@ int32_t clb_bank_expert_info(const clb_bank* bank, uint32_t layer, int32_t exper
 int32_t clb_route_device(int32_t mode, const float* d_logits, int32_t n_experts, int32_t k, int32_t tokens,
                          int32_t* d_ids, float* d_w, void* stream);
 
+/* Router logits on the device: d_logits [tokens][n_experts] = d_gate_w [n_experts][dim] .
+ * d_x [tokens][dim], fp32 with a fixed summation order (run-to-run identical); dim % 4 == 0.
+ * Replaces the router gemv of the GPU stage's MoE block (hip_backend.cpp:640). */
+int32_t clb_router_device(const float* d_x, int32_t tokens, int32_t dim, const float* d_gate_w, int32_t n_experts,
+                          float* d_logits, void* stream);
+
+/* Mode-1 routing (crosslane route_cpu, engine/strata/sycl/route/route.cpp:15-37) on the
+ * device, `tokens` rows: sc = sqrt(softplus(l)), top-k of sc + d_bias (ties to the lower
+ * id), w = sc / (sum of the picks' sc + 1e-20) * scale; exp and log1p are the correctly
+ * rounded float results, IEEE sqrt, add and divide. The picks equal clb_route_host(1, ...);
+ * a weight differs from it by an ulp or two where glibc's expf or log1pf is not correctly
+ * rounded (about 1.4 % of the scores; each such score moves every weight of its token).
+ * *d_status (device int) is set to 1 if a score is not finite. n_experts <= 1024. */
+int32_t clb_route_b_device(const float* d_logits, const float* d_bias, int32_t n_experts, int32_t k, int32_t tokens,
+                           float scale, int32_t* d_ids, float* d_w, int32_t* d_status, void* stream);
+
+/* The whole routed-expert MoE block of one token on the device, no host round trip
+ * (the GPU stage today reads route, x back to the host for warm_execute and copies the
+ * result up, hip_backend.cpp:640-742): router logits (clb_router_device) into d_logits
+ * [n_experts], route_cpu's picks (max_picks of them) into d_ids/d_w, then
+ * d_out = [d_resid +] combine over the picks of expert(d_x) [+ d_shared]
+ * (clb_layer_forward_device). Non-finite scores or non-resident picks surface as an
+ * error on the bank's next synchronising call. */
+int32_t clb_moe_block_device(clb_bank* bank, uint32_t layer, const float* d_x, const float* d_gate_w,
+                             const float* d_bias, float scale, const float* d_shared, const float* d_resid,
+                             float* d_out, float* d_logits, int32_t* d_ids, float* d_w, void* stream,
+                             clb_error_v1* err);
+
 /* Host routing for one token. mode 0 as above; mode 1 = route_cpu:
  * sqrt(softplus(l)) + bias, top-k, w = sc / (sum + 1e-20) * scale. */
 int32_t clb_route_host(int32_t mode, const float* logits, const float* bias, int32_t n_experts, int32_t k,
