@@ -196,6 +196,24 @@ struct clb_bank {
         }
     }
 
+    // Weight types among the layer's resident experts (clb::kTypeBit* bits), which selects
+    // the grouped GEMM's decoder instantiation.
+    int layer_types(uint32_t layer) const {
+        int m = 0;
+        for (size_t e = 0; e < E(); ++e) {
+            if (!resident[(size_t)layer * E() + e]) continue;
+            const auto& d = desc[(size_t)layer * E() + e];
+            for (int t : {d.gate.type, d.up.type, d.down.type})
+                m |= t == CLB_IQ2_XXS ? clb::kTypeBitXXS : t == CLB_IQ2_XS ? clb::kTypeBitXS : clb::kTypeBitIQ1M;
+        }
+        return m ? m : clb::kTypeBitAll;
+    }
+    std::vector<int> layer_types(uint32_t first, int nl) const {
+        std::vector<int> v((size_t)nl);
+        for (int l = 0; l < nl; ++l) v[(size_t)l] = layer_types(first + (uint32_t)l);
+        return v;
+    }
+
     void validate_ids(uint32_t layer, const int32_t* ids, int n, bool need_resident) {
         require(layer < (uint32_t)cfg.n_layers, CLB_E_INVALID, "layer %u out of range", layer);
         require(n >= 1 && n <= cfg.max_picks, CLB_E_INVALID, "pick count %d outside [1, %d]", n, cfg.max_picks);
@@ -1153,7 +1171,7 @@ static int32_t prefill_device(clb_bank* bank, uint32_t layer, int32_t tokens, in
             const auto& c = bank->cfg;
             cuda_check(clb::launch_prefill(bank->d_desc + (size_t)layer * bank->E(), c.n_experts, d_x, d_ids, d_w,
                                            tokens, k, c.dim, c.ff, c.limit, d_resid, d_out, d_ws, bank->d_err,
-                                           phase_mask, s),
+                                           phase_mask, s, false, 0, -1, nullptr, bank->layer_types(layer)),
                        "prefill launch");
         });
     });
@@ -1235,7 +1253,8 @@ int32_t clb_prefill_layer(clb_bank* bank, uint32_t layer, int32_t tokens, int32_
             cuda_check(cudaMemcpyAsync(bank->pf_dw, bank->pf_hw, np * 4, cudaMemcpyHostToDevice, bank->stream), "w H2D");
             cuda_check(clb::launch_prefill(bank->d_desc + (size_t)layer * bank->E(), c.n_experts, bank->pf_dx,
                                            bank->pf_dids, bank->pf_dw, tokens, k, c.dim, c.ff, c.limit, nullptr,
-                                           bank->pf_dout, bank->pf_ws, bank->d_err, 31, bank->stream),
+                                           bank->pf_dout, bank->pf_ws, bank->d_err, 31, bank->stream, false, 0, -1,
+                                           nullptr, bank->layer_types(layer)),
                        "prefill launch");
             cuda_check(cudaMemcpyAsync(bank->pf_hx, bank->pf_dout, nx * 4, cudaMemcpyDeviceToHost, bank->stream),
                        "out D2H");
@@ -1281,9 +1300,10 @@ int32_t clb_stack_batch_device(clb_bank* bank, uint32_t first, int32_t nl, int32
         cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : bank->stream;
         bank->device_step([&] {
             const auto& c = bank->cfg;
+            const std::vector<int> types = bank->layer_types(first, nl);
             cuda_check(clb::launch_stack_batch(bank->d_desc + (size_t)first * bank->E(), c.n_experts, nl, d_logits,
                                                nullptr, nullptr, d_h, tokens, c.max_picks, c.dim, c.ff, c.limit, d_ws,
-                                               bank->d_err, s),
+                                               bank->d_err, s, types.data()),
                        "stack batch launch");
         });
     });
@@ -1320,7 +1340,7 @@ int32_t clb_stack_batch_layer_device(clb_bank* bank, uint32_t layer, int32_t tok
                 cuda_check(clb::launch_route_sigmoid(d_logits, c.n_experts, k, tokens, ids, w, s), "route");
                 cuda_check(clb::launch_prefill(desc, c.n_experts, d_h, ids, w, tokens, k, c.dim, c.ff, c.limit, d_h, d_h,
                                                d_ws, bank->d_err, 1 | 2 | 4 | 8, s, true, c.expert_begin, c.expert_end,
-                                               d_rows),
+                                               d_rows, bank->layer_types(layer)),
                            "stack batch layer");
             }
             if (phase_mask & 2)  // h += ascending-id combine of every pick's row
@@ -1383,9 +1403,10 @@ int32_t clb_stack_batch(clb_bank* bank, uint32_t first, int32_t nl, int32_t toke
                        "route ids H2D");
             cuda_check(cudaMemcpyAsync(bank->sb_dw, bank->sb_hw, nr * 4, cudaMemcpyHostToDevice, bank->stream),
                        "route weights H2D");
+            const std::vector<int> types = bank->layer_types(first, nl);
             cuda_check(clb::launch_stack_batch(bank->d_desc + (size_t)first * bank->E(), c.n_experts, nl, nullptr,
                                                bank->sb_dids, bank->sb_dw, bank->sb_dh, tokens, k, c.dim, c.ff,
-                                               c.limit, bank->sb_ws, bank->d_err, bank->stream),
+                                               c.limit, bank->sb_ws, bank->d_err, bank->stream, types.data()),
                        "stack batch launch");
             cuda_check(cudaMemcpyAsync(bank->sb_hh, bank->sb_dh, nh * 4, cudaMemcpyDeviceToHost, bank->stream),
                        "h D2H");

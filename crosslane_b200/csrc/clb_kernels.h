@@ -71,10 +71,13 @@ bool prefill_shape_supported(int dim, int ff);
 // experts [e_begin, e_end) are computed (e_end < 0: all); with a partial range the expert
 // rows of the other picks are zero. rows: caller-owned expert rows [T*k][dim] (slot order)
 // instead of the workspace's.
+// type_mask: the weight types among the layer's experts (kTypeBit*; a single type selects
+// a kernel that decodes that type alone; experts of a type outside the mask raise *err = 1).
+constexpr int kTypeBitXXS = 1, kTypeBitXS = 2, kTypeBitIQ1M = 4, kTypeBitAll = 7;
 cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const int* ids, const float* w, int T, int k,
                            int dim, int ff, float limit, const float* resid, float* out, void* ws, int* err,
                            int phase_mask, cudaStream_t s, bool norm_x = false, int e_begin = 0, int e_end = -1,
-                           float* rows = nullptr);
+                           float* rows = nullptr, int type_mask = kTypeBitAll);
 // The routing slots of the batched stack's workspace: ids [T][k] and weights [T][k].
 void stack_batch_routes(void* ws, int T, int k, int dim, int ff, int E, int** ids, float** w);
 // T tokens through nl layers (desc [nl][E]): h <- h + layer(RMSNorm(h)) per layer, in place.
@@ -82,7 +85,7 @@ void stack_batch_routes(void* ws, int T, int k, int dim, int ff, int E, int** id
 size_t stack_batch_workspace_bytes(int T, int k, int dim, int ff, int E);
 cudaError_t launch_stack_batch(const ExpertDesc* desc, int E, int nl, const float* logits, const int* ids_all,
                                const float* w_all, float* h, int T, int k, int dim, int ff, float limit, void* ws,
-                               int* err, cudaStream_t s);
+                               int* err, cudaStream_t s, const int* type_masks = nullptr);
 
 // persistent whole-stack kernel (clb_stack.cu)
 constexpr int kMaxPeers = 8;  // GPUs of one node

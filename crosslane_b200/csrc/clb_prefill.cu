@@ -318,6 +318,10 @@ __device__ __forceinline__ float iq1m_scale(uint2 sc) {
     return __half2float(__ushort_as_half((uint16_t)h));
 }
 
+__host__ __device__ constexpr int pf_type_bit(int type) {
+    return type == CLB_IQ2_XXS ? kTypeBitXXS : type == CLB_IQ2_XS ? kTypeBitXS : type == CLB_IQ1_M ? kTypeBitIQ1M : 0;
+}
+
 // Type of the matrix that supplies a warp's 32 rows (lane quarter `quarter`) of a tile, from
 // the tile's packed types (gate | up << 8 | down << 16).
 __device__ __forceinline__ int pf_row_type(int types, int role, int quarter) {
@@ -366,6 +370,9 @@ __device__ __forceinline__ PfTile pf_tile(const PrefillGemm& G, int i) {  // CTA
     return PfTile{c.x, t % G.mtiles, c.y, c.z};
 }
 
+// TYPES: the weight types this instantiation decodes (kTypeBitXXS | kTypeBitXS | kTypeBitIQ1M);
+// a layer whose experts share one type runs the instantiation for that type alone.
+template <int TYPES>
 __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_constant__ PrefillGemm G) {
     uint8_t* sm = clb_dyn_smem;
     const uint32_t sbase = smem_u32(sm);
@@ -413,7 +420,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
             const bool split = G.role == 0;  // 64 gate rows + 64 up rows per tile
             const uint32_t rb = split ? 64u : 128u;
             auto fits = [&](const PackedMat& m) {
-                return m.body && m.k == G.K &&
+                return m.body && m.k == G.K && (pf_type_bit(m.type) & TYPES) &&
                        (m.type == CLB_IQ2_XXS ? m.d != nullptr
                         : m.type == CLB_IQ2_XS ? (m.d != nullptr && m.sc != nullptr)
                                                : (m.type == CLB_IQ1_M && m.sc != nullptr));
@@ -586,8 +593,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
             if (!uwait(kAccFull + acc.slot, acc.phase)) break;
             const bool last = b == nb - 1;
             if (c0 < ntok) {
-                const float dw = type == CLB_IQ1_M
-                                     ? iq1m_scale(*reinterpret_cast<const uint2*>(slot + 256 + row * 8))
+                const bool iq1 = TYPES == kTypeBitIQ1M || (TYPES != kTypeBitXXS && TYPES != kTypeBitXS && type == CLB_IQ1_M);
+                const float dw = iq1 ? iq1m_scale(*reinterpret_cast<const uint2*>(slot + 256 + row * 8))
                                      : __half2float(reinterpret_cast<const __half*>(slot)[row]);
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");  // the previous block's R stores
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -714,9 +721,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_prefill_gemm(const __grid_con
             const int type =
                 pf_row_type(*reinterpret_cast<const int*>(sm + PfSmem::raw + rr.slot * kPfRawBlock + kPfRawHdr),
                             G.role, quarter);
-            const bool ok = type == CLB_IQ2_XXS ? block(std::integral_constant<int, CLB_IQ2_XXS>())
-                            : type == CLB_IQ2_XS ? block(std::integral_constant<int, CLB_IQ2_XS>())
-                                                 : block(std::integral_constant<int, CLB_IQ1_M>());
+            bool ok;
+            if (TYPES == kTypeBitXXS)
+                ok = block(std::integral_constant<int, CLB_IQ2_XXS>());
+            else if (TYPES == kTypeBitXS)
+                ok = block(std::integral_constant<int, CLB_IQ2_XS>());
+            else if (TYPES == kTypeBitIQ1M)
+                ok = block(std::integral_constant<int, CLB_IQ1_M>());
+            else
+                ok = type == CLB_IQ2_XXS ? block(std::integral_constant<int, CLB_IQ2_XXS>())
+                     : type == CLB_IQ2_XS ? block(std::integral_constant<int, CLB_IQ2_XS>())
+                                          : block(std::integral_constant<int, CLB_IQ1_M>());
             if (!ok) break;
             rr.next();
         }
@@ -1141,7 +1156,8 @@ cudaError_t encode_bmaps(CUtensorMap* maps, const __half* base, int P, int K) {
 
 cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const int* ids, const float* w, int T, int k,
                            int dim, int ff, float limit, const float* resid, float* out, void* wsp, int* err,
-                           int phase_mask, cudaStream_t s, bool norm_x, int e_begin, int e_end, float* rows) {
+                           int phase_mask, cudaStream_t s, bool norm_x, int e_begin, int e_end, float* rows,
+                           int type_mask) {
     PrefillWs ws{};
     carve(wsp, T, k, dim, ff, E, &ws);
     if (e_end < 0) e_end = E;
@@ -1153,7 +1169,11 @@ cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const 
     int dev = 0, sms = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    if ((e = cudaFuncSetAttribute(k_prefill_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PfSmem::total)) !=
+    void (*gemm)(PrefillGemm) = type_mask == kTypeBitXXS    ? k_prefill_gemm<kTypeBitXXS>
+                                : type_mask == kTypeBitXS  ? k_prefill_gemm<kTypeBitXS>
+                                : type_mask == kTypeBitIQ1M ? k_prefill_gemm<kTypeBitIQ1M>
+                                                            : k_prefill_gemm<kTypeBitAll>;
+    if ((e = cudaFuncSetAttribute(gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PfSmem::total)) !=
         cudaSuccess)
         return e;
     if ((e = cudaFuncSetAttribute(k_pairs_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPcSmem)) !=
@@ -1191,7 +1211,7 @@ cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const 
         g.nrows = ff;
         g.mtiles = ff / 64;
         g.out = ws.gu;
-        k_prefill_gemm<<<sms, kPfThreads, PfSmem::total, s>>>(g);
+        gemm<<<sms, kPfThreads, PfSmem::total, s>>>(g);
         k_pairs_gateup<<<sms, kPcThreads, kPcSmem, s>>>(desc, ids, ws.pairs, ws.npairs, k, ws.qx, ws.dx, dim, ff,
                                                          tables, ws.pgu, err);
     }
@@ -1208,7 +1228,7 @@ cudaError_t launch_prefill(const ExpertDesc* desc, int E, const float* x, const 
         g.nrows = dim;
         g.mtiles = dim / 128;
         g.out = ws.y;
-        k_prefill_gemm<<<sms, kPfThreads, PfSmem::total, s>>>(g);
+        gemm<<<sms, kPfThreads, PfSmem::total, s>>>(g);
         k_pairs_down<<<sms, kPcThreads, kPcSmem, s>>>(desc, ids, ws.pairs, ws.npairs, ws.pqh, ws.pdh, dim, ff, tables,
                                                        ws.y, err);
     }
@@ -1237,7 +1257,7 @@ void stack_batch_routes(void* wsp, int T, int k, int dim, int ff, int E, int** i
 
 cudaError_t launch_stack_batch(const ExpertDesc* desc, int E, int nl, const float* logits, const int* ids_all,
                                const float* w_all, float* h, int T, int k, int dim, int ff, float limit, void* wsp,
-                               int* err, cudaStream_t s) {
+                               int* err, cudaStream_t s, const int* type_masks) {
     uint8_t* base = static_cast<uint8_t*>(wsp);
     const size_t a = (prefill_workspace_bytes(T, k, dim, ff, E) + 255) & ~(size_t)255;
     const size_t r = ((size_t)T * k * 4 + 255) & ~(size_t)255;
@@ -1252,7 +1272,7 @@ cudaError_t launch_stack_batch(const ExpertDesc* desc, int E, int nl, const floa
         if (!ids_all && (e = launch_route_sigmoid(logits + (size_t)l * T * E, E, k, T, rids, rw, s)) != cudaSuccess)
             return e;
         if ((e = launch_prefill(desc + (size_t)l * E, E, hin, ids, w, T, k, dim, ff, limit, hin, hout, wsp, err, 31, s,
-                                true)) != cudaSuccess)
+                                true, 0, -1, nullptr, type_masks ? type_masks[l] : kTypeBitAll)) != cudaSuccess)
             return e;
         float* t = hin;
         hin = hout;
