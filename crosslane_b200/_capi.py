@@ -29,6 +29,17 @@ class ClbError(RuntimeError):
         self.code = code
 
 
+class TimingV1(C.Structure):
+    _fields_ = [("ns", C.c_uint64), ("h2d_bytes", C.c_uint64), ("d2h_bytes", C.c_uint64), ("layer", C.c_int32),
+                ("layers", C.c_int32), ("picks", C.c_int32), ("reserved", C.c_int32)]
+
+
+class LaneConfigV1(C.Structure):
+    _fields_ = [("experts", C.c_int32), ("exact_math", C.c_int32), ("bytes", C.c_uint64), ("device_first", C.c_int32),
+                ("device_last", C.c_int32), ("timing", C.c_int32), ("bank_flags", C.c_int32),
+                ("reserved", C.c_int32 * 6)]
+
+
 class ErrorV1(C.Structure):
     _fields_ = [("code", C.c_int32), ("message", C.c_char * 512)]
 
@@ -104,6 +115,8 @@ SIGNATURES = {
     "clb_stack_batch": (_I, [_P, _U32, _I, _I, _P, _P, _PE]),
     "clb_stack_batch_layer_device": (_I, [_P, _U32, _I, _P, _P, _P, _P, C.c_uint64, _I, _P, _PE]),
     "clb_bank_stream": (_P, [_P]),
+    "clb_bank_last_timing": (_I, [_P, _P]),
+    "clb_lane_config_parse": (_I, [C.c_char_p, _P, _PE]),
     "clb_bank_synchronize": (_I, [_P, _PE]),
     "clb_warm_execute": (_I, [_P, _U32, _P, _P, _I, _P, _P, HOST_EXPERT_FN, _P, _P, _PE]),
     "clb_expert_forward_noalloc": (_I, [_I, _P, _P, _P, _P, _P, _I, _I, _F, _P, _PE]),

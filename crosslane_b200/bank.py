@@ -11,12 +11,13 @@ import ctypes as C
 import numpy as np
 
 from . import _capi
-from ._capi import BankConfigV1, ErrorV1, HOST_EXPERT_FN, check, lib
+from ._capi import BankConfigV1, ErrorV1, HOST_EXPERT_FN, LaneConfigV1, TimingV1, check, lib
 
 IQ2_XXS, IQ2_XS, IQ1_M = 16, 17, 29
 BLOCK_BYTES = {IQ2_XXS: 66, IQ2_XS: 74, IQ1_M: 56}
 EXACT_ORDER = 1  # CLB_BANK_EXACT_ORDER
 PER_LAYER_KERNELS = 2  # CLB_BANK_PER_LAYER_KERNELS
+TIMING = 4  # CLB_BANK_TIMING
 EXCHANGE_HANDLE_BYTES = 64  # CLB_EXCHANGE_HANDLE_BYTES
 ROLE_GATE, ROLE_UP, ROLE_DOWN = 0, 1, 2
 Q8K_BLOCK_BYTES = 292
@@ -46,8 +47,9 @@ class ExpertBank:
 
     def __init__(self, *, n_layers: int, n_experts: int, dim: int, ff: int, max_picks: int = 6,
                  limit: float = 0.0, device: int = 0, expert_begin: int = 0, expert_end: int = 0,
-                 exact_order: bool = False, per_layer_kernels: bool = False):
-        flags = (EXACT_ORDER if exact_order else 0) | (PER_LAYER_KERNELS if per_layer_kernels else 0)
+                 exact_order: bool = False, per_layer_kernels: bool = False, timing: bool = False):
+        flags = ((EXACT_ORDER if exact_order else 0) | (PER_LAYER_KERNELS if per_layer_kernels else 0) |
+                 (TIMING if timing else 0))
         cfg = BankConfigV1(device=device, n_layers=n_layers, n_experts=n_experts, dim=dim, ff=ff,
                            max_picks=max_picks, limit=limit, expert_begin=expert_begin, expert_end=expert_end,
                            flags=flags)
@@ -295,6 +297,12 @@ class ExpertBank:
                                        vp(d_resid), vp(d_out), vp(d_logits), vp(d_ids), vp(d_w),
                                        C.c_void_p(stream) if stream else None, C.byref(err)), err)
 
+    def last_timing(self) -> dict:
+        """The last CLB_BANK_TIMING span (clb_bank_last_timing) as a dict."""
+        t = TimingV1()
+        check(lib.clb_bank_last_timing(self._h, C.byref(t)), what="clb_bank_last_timing")
+        return {f: getattr(t, f) for f, _ in TimingV1._fields_ if f != "reserved"}
+
     def expert_info(self, layer: int, expert: int):
         """(ggml type id, payload bytes of gate+up+down) of a resident expert."""
         t = C.c_int32()
@@ -376,3 +384,12 @@ def route_b_device(d_logits, d_bias, k: int, scale: float, d_ids, d_w, d_status,
     check(lib.clb_route_b_device(C.c_void_p(d_logits.data_ptr()), C.c_void_p(d_bias.data_ptr()), E, k, T, scale,
                                  C.c_void_p(d_ids.data_ptr()), C.c_void_p(d_w.data_ptr()),
                                  C.c_void_p(d_status.data_ptr()), _stream(stream)), what="clb_route_b_device")
+
+
+def lane_config_parse(text: str) -> dict:
+    """The CUDA lane's keys of a stage config (clb_lane_config_parse) as a dict; raises
+    ClbError on a malformed, duplicate or unknown key."""
+    c = LaneConfigV1()
+    err = ErrorV1()
+    check(lib.clb_lane_config_parse(text.encode(), C.byref(c), C.byref(err)), err)
+    return {f: getattr(c, f) for f, _ in LaneConfigV1._fields_ if f != "reserved"}

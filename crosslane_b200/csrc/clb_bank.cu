@@ -97,6 +97,8 @@ bool finite_all(const float* v, size_t n) {
 struct clb_bank {
     clb_bank_config_v1 cfg{};
     cudaStream_t stream = nullptr;
+    cudaEvent_t t_ev0 = nullptr, t_ev1 = nullptr;  // CLB_BANK_TIMING spans
+    clb_timing_v1 last_timing{};
     bool poisoned = false;
     std::mutex call_mutex;  // one caller at a time (crosslane's WarmWorker guarantee)
 
@@ -172,6 +174,31 @@ struct clb_bank {
     std::vector<void*> host_allocations;
 
     void check_usable() { require(!poisoned, CLB_E_STATE, "bank poisoned by an earlier device failure"); }
+
+    // device_step of a synchronous host call, timed under CLB_BANK_TIMING: events on the bank
+    // stream around everything f enqueues (f ends with its copies back), one JSON line.
+    template <class F>
+    void timed_step(const char* call, int layer, int layers, int picks, uint64_t h2d, uint64_t d2h, F&& f) {
+        if (!t_ev0) {
+            device_step(f);
+            return;
+        }
+        device_step([&] {
+            cuda_check(cudaEventRecord(t_ev0, stream), "timing event");
+            f();
+            cuda_check(cudaEventRecord(t_ev1, stream), "timing event");
+            cuda_check(cudaEventSynchronize(t_ev1), "timing sync");
+            float ms = 0.0f;
+            cuda_check(cudaEventElapsedTime(&ms, t_ev0, t_ev1), "timing");
+            last_timing = clb_timing_v1{(uint64_t)((double)ms * 1e6), h2d, d2h, layer, layers, picks, 0};
+            std::fprintf(stderr,
+                         "{\"schema\":\"clb-cuda-timing-v1\",\"lane\":\"cuda\",\"device\":%d,\"call\":\"%s\","
+                         "\"layer\":%d,\"layers\":%d,\"picks\":%d,\"h2d_bytes\":%llu,\"d2h_bytes\":%llu,"
+                         "\"ns\":%llu}\n",
+                         cfg.device, call, layer, layers, picks, (unsigned long long)h2d, (unsigned long long)d2h,
+                         (unsigned long long)last_timing.ns);
+        });
+    }
 
     // Runs f; on a device failure the bank is poisoned (abi_backend_plugin.cpp:31-39 convention).
     template <class F>
@@ -327,6 +354,8 @@ struct clb_bank {
         for (auto& g : device_graphs) cudaGraphExecDestroy(g.second);
         for (void* p : allocations) cudaFree(p);
         for (void* p : host_allocations) cudaFreeHost(p);
+        if (t_ev0) cudaEventDestroy(t_ev0);
+        if (t_ev1) cudaEventDestroy(t_ev1);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -433,8 +462,8 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         require(cfg.max_picks >= 1 && cfg.max_picks <= clb::kMaxPicks && cfg.max_picks <= cfg.n_experts,
                 CLB_E_INVALID, "max_picks must be in [1, min(16, n_experts)]");
         require(std::isfinite(cfg.limit) && cfg.limit >= 0, CLB_E_INVALID, "SwiGLU limit must be finite and >= 0");
-        require((cfg.flags & ~(CLB_BANK_EXACT_ORDER | CLB_BANK_PER_LAYER_KERNELS)) == 0, CLB_E_INVALID,
-                "unknown bank flags 0x%x", cfg.flags);
+        require((cfg.flags & ~(CLB_BANK_EXACT_ORDER | CLB_BANK_PER_LAYER_KERNELS | CLB_BANK_TIMING)) == 0,
+                CLB_E_INVALID, "unknown bank flags 0x%x", cfg.flags);
         require(cfg.expert_begin >= 0 && cfg.expert_begin < cfg.expert_end && cfg.expert_end <= cfg.n_experts,
                 CLB_E_INVALID, "owned expert range invalid");
         require((size_t)cfg.max_picks * (cfg.ff / 256) <= 256, CLB_E_UNSUPPORTED,
@@ -446,6 +475,10 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         bank = new clb_bank();
         bank->cfg = cfg;
         cuda_check(cudaStreamCreateWithFlags(&bank->stream, cudaStreamNonBlocking), "stream");
+        if (cfg.flags & CLB_BANK_TIMING) {
+            cuda_check(cudaEventCreate(&bank->t_ev0), "timing event");
+            cuda_check(cudaEventCreate(&bank->t_ev1), "timing event");
+        }
         ensure_device_ready(cfg.device, bank->stream);
         bank->desc.assign(bank->L() * bank->E(), clb::ExpertDesc{});
         bank->resident.assign(bank->L() * bank->E(), 0);
@@ -798,6 +831,74 @@ int32_t clb_bank_load_strata_pack(clb_bank* bank, const clb_strata_pack* pack, u
 
 void* clb_bank_stream(clb_bank* bank) { return bank ? bank->stream : nullptr; }
 
+int32_t clb_bank_last_timing(const clb_bank* bank, clb_timing_v1* out) {
+    if (!bank || !out) return CLB_E_INVALID;
+    *out = bank->last_timing;
+    return CLB_OK;
+}
+
+int32_t clb_lane_config_parse(const char* text, clb_lane_config_v1* out, clb_error_v1* err) {
+    return guarded(err, [&] {
+        require(text && out, CLB_E_INVALID, "null lane config");
+        clb_lane_config_v1 c{};
+        std::set<std::string> seen;
+        std::string all(text), line;
+        size_t pos = 0;
+        auto canonical_u64 = [](const std::string& v, uint64_t* r) {
+            if (v.empty() || v.size() > 20) return false;
+            for (char ch : v)
+                if (ch < '0' || ch > '9') return false;
+            errno = 0;
+            const unsigned long long x = std::strtoull(v.c_str(), nullptr, 10);
+            if (errno == ERANGE || std::to_string(x) != v) return false;
+            *r = (uint64_t)x;
+            return true;
+        };
+        while (pos <= all.size()) {
+            const size_t nl = all.find('\n', pos);
+            line = all.substr(pos, nl == std::string::npos ? std::string::npos : nl - pos);
+            pos = nl == std::string::npos ? all.size() + 1 : nl + 1;
+            if (line.empty() || line[0] == '#') continue;
+            const size_t eq = line.find('=');
+            require(eq != std::string::npos, CLB_E_INVALID, "lane config line without '=': %s", line.c_str());
+            const std::string k = line.substr(0, eq), v = line.substr(eq + 1);
+            require(seen.insert(k).second, CLB_E_INVALID, "duplicate lane config key: %s", k.c_str());
+            if (k == "warm_cuda_experts") {
+                require(v == "off" || v == "layer-batch-v1" || v == "stack-v1", CLB_E_INVALID,
+                        "unknown warm_cuda_experts mode: %s", v.c_str());
+                c.experts = v == "off" ? 0 : v == "layer-batch-v1" ? 1 : 2;
+            } else if (k == "cuda_expert_math") {
+                require(v == "fast-v1" || v == "cpu-q8k-v1", CLB_E_INVALID, "unknown cuda_expert_math: %s", v.c_str());
+                c.exact_math = v == "cpu-q8k-v1";
+            } else if (k == "warm_cuda_bytes") {
+                require(canonical_u64(v, &c.bytes), CLB_E_INVALID, "invalid warm_cuda_bytes: %s", v.c_str());
+            } else if (k == "cuda_devices") {
+                const size_t dots = v.find("..");
+                uint64_t a = 0, b = 0;
+                const bool ok = dots == std::string::npos ? canonical_u64(v, &a) && (b = a, true)
+                                                          : canonical_u64(v.substr(0, dots), &a) &&
+                                                                canonical_u64(v.substr(dots + 2), &b);
+                require(ok && a <= b && b < 64, CLB_E_INVALID, "cuda_devices must be a or a..b with a <= b < 64: %s",
+                        v.c_str());
+                c.device_first = (int32_t)a;
+                c.device_last = (int32_t)b;
+            } else if (k == "warm_cuda_timing") {
+                require(v == "0" || v == "1", CLB_E_INVALID, "warm_cuda_timing must be 0 or 1");
+                c.timing = v == "1";
+            } else {
+                throw Error(CLB_E_INVALID, "unknown lane config key: " + k);
+            }
+        }
+        const bool lane_keys = seen.count("cuda_expert_math") || seen.count("warm_cuda_bytes") ||
+                               seen.count("cuda_devices") || seen.count("warm_cuda_timing");
+        require(c.experts != 0 || !lane_keys, CLB_E_INVALID,
+                "cuda_expert_math, warm_cuda_bytes, cuda_devices and warm_cuda_timing need warm_cuda_experts on");
+        c.bank_flags = (c.exact_math ? CLB_BANK_EXACT_ORDER : 0) | (c.experts == 1 ? CLB_BANK_PER_LAYER_KERNELS : 0) |
+                       (c.timing ? CLB_BANK_TIMING : 0);
+        *out = c;
+    });
+}
+
 int32_t clb_bank_synchronize(clb_bank* bank, clb_error_v1* err) {
     if (!bank) return fail(err, CLB_E_INVALID, "null bank");
     return guarded(err, [&] {
@@ -812,7 +913,8 @@ static void compute_rows(clb_bank* bank, uint32_t layer, const int32_t* ids, int
     bank->validate_ids(layer, ids, n, true);
     require(finite_all(x, (size_t)c.dim), CLB_E_NONFINITE, "non-finite activation");
     DeviceGuard g(c.device);
-    bank->device_step([&] {
+    bank->timed_step("compute_many", (int)layer, 1, n, sizeof(float) * c.dim + (uint64_t)n * 4,
+                     (uint64_t)n * c.dim * 4, [&] {
         std::memcpy(bank->h_x, x, sizeof(float) * c.dim);
         cuda_check(cudaMemcpyAsync(bank->d_x, bank->h_x, sizeof(float) * c.dim, cudaMemcpyHostToDevice, bank->stream),
                    "x H2D");
@@ -863,7 +965,8 @@ int32_t clb_layer_execute(clb_bank* bank, uint32_t layer, const int32_t* ids, co
         require(finite_all(x, (size_t)c.dim), CLB_E_NONFINITE, "non-finite activation");
         require(!shared || finite_all(shared, (size_t)c.dim), CLB_E_NONFINITE, "non-finite shared output");
         DeviceGuard g(c.device);
-        bank->device_step([&] {
+        bank->timed_step("layer_execute", (int)layer, 1, n, sizeof(float) * c.dim * (shared ? 2 : 1) + (uint64_t)n * 8,
+                         sizeof(float) * c.dim, [&] {
             std::memcpy(bank->h_x, x, sizeof(float) * c.dim);
             cuda_check(cudaMemcpyAsync(bank->d_x, bank->h_x, sizeof(float) * c.dim, cudaMemcpyHostToDevice,
                                        bank->stream),
@@ -1038,7 +1141,8 @@ int32_t clb_stack_decode(clb_bank* bank, uint32_t first, int32_t nl, const float
                         "expert (%u, %d) not resident", first + l, e);
         DeviceGuard g(c.device);
         require(finite_all(logits, (size_t)nl * c.n_experts), CLB_E_NONFINITE, "non-finite router logits");
-        bank->device_step([&] {
+        bank->timed_step("stack_decode", (int)first, nl, nl * c.max_picks,
+                         sizeof(float) * c.dim + (uint64_t)nl * c.max_picks * 8, sizeof(float) * c.dim, [&] {
             // Routing on the host (route.cpp's order and libm), then x and the routes go
             // up; one stack launch (or the captured per-layer graph) and h comes back.
             const int k = c.max_picks;
@@ -1243,7 +1347,7 @@ int32_t clb_prefill_layer(clb_bank* bank, uint32_t layer, int32_t tokens, int32_
         require(finite_all(x, (size_t)tokens * c.dim), CLB_E_NONFINITE, "non-finite activation");
         DeviceGuard g(c.device);
         const size_t nx = (size_t)tokens * c.dim, np = (size_t)tokens * k;
-        bank->device_step([&] {
+        bank->timed_step("prefill_layer", (int)layer, 1, (int)np, nx * 4 + np * 8, nx * 4, [&] {
             std::memcpy(bank->pf_hx, x, nx * 4);
             std::memcpy(bank->pf_hids, ids, np * 4);
             std::memcpy(bank->pf_hw, w, np * 4);
@@ -1388,7 +1492,7 @@ int32_t clb_stack_batch(clb_bank* bank, uint32_t first, int32_t nl, int32_t toke
             bank->sb_tokens = T;
             bank->sb_layers = L;
         }
-        bank->device_step([&] {
+        bank->timed_step("stack_batch", (int)first, nl, (int)nr, nh * 4 + nr * 8, nh * 4, [&] {
             // routing on the host (route.cpp's order and libm, as clb_stack_decode), then h and
             // the routes go up, nl grouped layers run, and h comes back
             for (int l = 0; l < nl; ++l)

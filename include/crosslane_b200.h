@@ -118,6 +118,51 @@ typedef struct clb_bank_config_v1 {
 /* Stack decode (clb_stack_decode*) launches three kernels per layer instead of one
  * persistent kernel holding one CTA on every SM (for processes that share the GPU). */
 #define CLB_BANK_PER_LAYER_KERNELS 2
+/* Device timing of the synchronous host entry points (clb_layer_execute, clb_warm_execute,
+ * clb_stack_decode, clb_prefill_layer, clb_stack_batch): CUDA events on the bank stream
+ * around each call's copies and kernels; one JSON line per call on stderr,
+ *   {"schema":"clb-cuda-timing-v1","lane":"cuda","device":D,"call":"...","layer":L,
+ *    "layers":N,"picks":P,"h2d_bytes":B,"d2h_bytes":B,"ns":T}
+ * and the last span through clb_bank_last_timing. */
+#define CLB_BANK_TIMING 4
+
+/* The last span recorded under CLB_BANK_TIMING (zeros before the first). */
+typedef struct clb_timing_v1 {
+    uint64_t ns;         /* device time from the first copy up to the last copy back */
+    uint64_t h2d_bytes;  /* host -> device bytes of the call */
+    uint64_t d2h_bytes;  /* device -> host bytes of the call */
+    int32_t layer;       /* first layer */
+    int32_t layers;      /* layers the call ran */
+    int32_t picks;       /* routed (token, expert) picks the call computed */
+    int32_t reserved;
+} clb_timing_v1;
+int32_t clb_bank_last_timing(const clb_bank* bank, clb_timing_v1* out);
+
+/* ---- the CUDA lane's keys of the stage config ----
+ * crosslane's stage config is "key=value" lines, parsed strictly: '#' comments and empty
+ * lines skipped, a line without '=', a duplicate key or an unknown key is an error
+ * (engine/strata/sycl/stage/wiring/common.hpp:55-125). The CUDA lane's keys:
+ *   warm_cuda_experts = off | layer-batch-v1 | stack-v1   (default off)
+ *       layer-batch-v1: the lane serves warm_execute's layer batches (per-layer kernels);
+ *       stack-v1: the device-resident persistent stack kernel
+ *   cuda_expert_math  = fast-v1 | cpu-q8k-v1              (default fast-v1)
+ *       cpu-q8k-v1: the CPU lane's summation order, bit for bit (CLB_BANK_EXACT_ORDER)
+ *   warm_cuda_bytes   = canonical decimal byte cap of the bank's payload (0 = none)
+ *   cuda_devices      = a | a..b                          (default 0)
+ *   warm_cuda_timing  = 0 | 1                             (CLB_BANK_TIMING)
+ * A host whose own parser sees these keys forwards those lines here. cpu-q8k-v1 needs the
+ * lane on; warm_cuda_bytes and cuda_devices need it on too. */
+typedef struct clb_lane_config_v1 {
+    int32_t experts;       /* 0 off, 1 layer-batch-v1, 2 stack-v1 */
+    int32_t exact_math;    /* 1 for cpu-q8k-v1 */
+    uint64_t bytes;        /* 0 = no cap */
+    int32_t device_first;  /* cuda_devices range, inclusive */
+    int32_t device_last;
+    int32_t timing;        /* 1 = CLB_BANK_TIMING */
+    int32_t bank_flags;    /* the CLB_BANK_* flags these keys imply */
+    int32_t reserved[6];
+} clb_lane_config_v1;
+int32_t clb_lane_config_parse(const char* text, clb_lane_config_v1* out, clb_error_v1* err);
 
 /* Creates a bank and its fixed workspace on `device` (no allocation afterwards).
  * Replaces the construction half of HipResidentBank::load
