@@ -86,10 +86,50 @@ void route_sigmoid_host(const float* logits, int n, int k, int32_t* ids, float* 
     for (int i = 0; i < k; ++i) w[i] = s[i] / sum;
 }
 
+// Splits [0, n) over up to 16 host threads in chunks of at least `grain` (one thread below
+// that): the host-side loops of batched calls (validation of tens of MB, copies into the
+// pinned staging buffers) would otherwise dominate their end-to-end time.
+template <class F>
+void host_parallel(size_t n, size_t grain, F&& f) {
+    const unsigned hw = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+    const size_t parts = std::min<size_t>(hw, (n + grain - 1) / grain);
+    if (parts <= 1) {
+        f((size_t)0, n);
+        return;
+    }
+    const size_t chunk = (n + parts - 1) / parts;
+    std::vector<std::thread> th;
+    th.reserve(parts - 1);
+    for (size_t p = 1; p < parts; ++p) {
+        const size_t b = p * chunk, e = std::min(n, b + chunk);
+        if (b < e) th.emplace_back([&f, b, e] { f(b, e); });
+    }
+    f((size_t)0, std::min(n, chunk));
+    for (auto& t : th) t.join();
+}
+
+bool finite_span(const float* v, size_t b, size_t e) {
+    uint32_t bad = 0;
+    for (size_t i = b; i < e; ++i) {
+        uint32_t u;
+        std::memcpy(&u, v + i, 4);
+        bad |= (uint32_t)((u & 0x7f800000u) == 0x7f800000u);  // exponent all ones: inf or nan
+    }
+    return bad == 0;
+}
+
 bool finite_all(const float* v, size_t n) {
-    for (size_t i = 0; i < n; ++i)
-        if (!std::isfinite(v[i])) return false;
-    return true;
+    std::atomic<bool> ok{true};
+    host_parallel(n, (size_t)1 << 20, [&](size_t b, size_t e) {
+        if (!finite_span(v, b, e)) ok.store(false, std::memory_order_relaxed);
+    });
+    return ok.load();
+}
+
+void copy_parallel(void* dst, const void* src, size_t bytes) {
+    host_parallel(bytes, (size_t)4 << 20, [&](size_t b, size_t e) {
+        std::memcpy(static_cast<uint8_t*>(dst) + b, static_cast<const uint8_t*>(src) + b, e - b);
+    });
 }
 
 }  // namespace
@@ -1348,7 +1388,7 @@ int32_t clb_prefill_layer(clb_bank* bank, uint32_t layer, int32_t tokens, int32_
         DeviceGuard g(c.device);
         const size_t nx = (size_t)tokens * c.dim, np = (size_t)tokens * k;
         bank->timed_step("prefill_layer", (int)layer, 1, (int)np, nx * 4 + np * 8, nx * 4, [&] {
-            std::memcpy(bank->pf_hx, x, nx * 4);
+            copy_parallel(bank->pf_hx, x, nx * 4);
             std::memcpy(bank->pf_hids, ids, np * 4);
             std::memcpy(bank->pf_hw, w, np * 4);
             cuda_check(cudaMemcpyAsync(bank->pf_dx, bank->pf_hx, nx * 4, cudaMemcpyHostToDevice, bank->stream), "x H2D");
@@ -1364,7 +1404,7 @@ int32_t clb_prefill_layer(clb_bank* bank, uint32_t layer, int32_t tokens, int32_
                        "out D2H");
             bank->check_err_flag();
         });
-        std::memcpy(out, bank->pf_hx, nx * 4);
+        copy_parallel(out, bank->pf_hx, nx * 4);
         require(finite_all(out, nx), CLB_E_NONFINITE, "non-finite prefill output");
     });
 }
@@ -1501,7 +1541,7 @@ int32_t clb_stack_batch(clb_bank* bank, uint32_t first, int32_t nl, int32_t toke
                     route_sigmoid_host(logits + ((size_t)l * tokens + t) * c.n_experts, c.n_experts, k,
                                        bank->sb_hids + r, bank->sb_hw + r);
                 }
-            std::memcpy(bank->sb_hh, h, nh * 4);
+            copy_parallel(bank->sb_hh, h, nh * 4);
             cuda_check(cudaMemcpyAsync(bank->sb_dh, bank->sb_hh, nh * 4, cudaMemcpyHostToDevice, bank->stream), "h H2D");
             cuda_check(cudaMemcpyAsync(bank->sb_dids, bank->sb_hids, nr * 4, cudaMemcpyHostToDevice, bank->stream),
                        "route ids H2D");
@@ -1516,7 +1556,7 @@ int32_t clb_stack_batch(clb_bank* bank, uint32_t first, int32_t nl, int32_t toke
                        "h D2H");
             bank->check_err_flag();
         });
-        std::memcpy(h, bank->sb_hh, nh * 4);
+        copy_parallel(h, bank->sb_hh, nh * 4);
         require(finite_all(h, nh), CLB_E_NONFINITE, "non-finite stack output");
     });
 }
