@@ -620,22 +620,33 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
+    # the K timed steps, with events also at the thirds: three repetitions of K/3 steps
+    # (median / min / max) inside the one timed region
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    cuts = [0, args.steps // 3, 2 * args.steps // 3, args.steps]
     with ClockSampler(local) as clocks:
-        ev0.record(stream)
+        evs[0].record(stream)
         for i in range(args.steps):
             step(args.warmup + i)
-        ev1.record(stream)
-        ev1.synchronize()
+            for c in (1, 2):
+                if i + 1 == cuts[c]:
+                    evs[c].record(stream)
+        evs[3].record(stream)
+        evs[3].synchronize()
     torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
+    ms = evs[0].elapsed_time(evs[3])
+    reps = [evs[c].elapsed_time(evs[c + 1]) / (cuts[c + 1] - cuts[c]) for c in range(3) if cuts[c + 1] > cuts[c]]
     if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        t = torch.tensor([ms] + reps, dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, reps = float(t[0].item()), [float(v) for v in t[1:].tolist()]
         dist.barrier()
     ms_per_step = ms / args.steps
+    units_r = 1 if (world > 1 and not args.replicas) else world
+    repeats = {"runs": len(reps), "unit": "tok/s",
+               "median": round(units_r * 1e3 / statistics.median(reps), 2) if reps else None,
+               "min": round(units_r * 1e3 / max(reps), 2) if reps else None,
+               "max": round(units_r * 1e3 / min(reps), 2) if reps else None}
     units = 1 if sharded else world  # tokens per step of the whole job
     value = units * args.steps / (ms / 1e3)
 
@@ -712,6 +723,7 @@ def main():
                    "l2": "inputs larger than L2: each token streams ~2 GB of distinct expert weights",
                    "bank_gb": round(bank.weight_bytes / 1e9, 2), "fill_s": round(fill_s, 1)},
         "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in e2e.items()},
+        "repeats": repeats,
         "roofline": roofline,
         "cpu_baseline": cpu,
         "clocks": clk,

@@ -139,3 +139,45 @@ def test_stack_batch_rejects_partial_bank(cb, orc):
         assert ei.value.code == 1
     finally:
         bank.close()
+
+
+def test_stack_batch_layer_partial_banks(cb, cuda):
+    """The expert-ID shard path on one GPU: two banks holding experts [0, E/2) and [E/2, E)
+    each compute the rows of their own picks (the others zero); those rows equal the full
+    bank's bit for bit, and combining their sum reproduces the full bank's layer."""
+    torch = cuda
+    dim, ff, E, k, T, seed, policy = 1024, 512, 32, 6, 20, 4, 2
+    rng = np.random.default_rng(12)
+    h0 = rng.standard_normal((T, dim)).astype(np.float32)
+    lg = torch.from_numpy(zipf_logits(rng, 1, T, E)[0]).cuda()
+    banks = [cb.ExpertBank(n_layers=1, n_experts=E, dim=dim, ff=ff, max_picks=k, device=0, expert_begin=b,
+                           expert_end=e) for b, e in ((0, E), (0, E // 2), (E // 2, E))]
+    try:
+        rows, hs = [], []
+        for b in banks:
+            b.fill_synthetic(seed, policy)
+            d_h = torch.from_numpy(h0.copy()).cuda()
+            d_rows = torch.zeros((T * k, dim), dtype=torch.float32, device="cuda")
+            d_ws = torch.zeros(b.stack_batch_workspace_bytes(T), dtype=torch.uint8, device="cuda")
+            b.stack_batch_layer_device(0, d_h, lg, d_rows, d_ws, 1)
+            b.synchronize()
+            rows.append((d_rows, d_ws, d_h))
+        full, lo, hi = (r[0].cpu().numpy() for r in rows)
+        ids = np.zeros((T, k), np.int32)
+        for t in range(T):
+            ids[t], _ = cb.route_host(0, lg[t].cpu().numpy(), k)
+        mine_lo = (ids.reshape(-1) < E // 2)
+        assert np.array_equal(lo[mine_lo].view(np.uint32), full[mine_lo].view(np.uint32))
+        assert np.array_equal(hi[~mine_lo].view(np.uint32), full[~mine_lo].view(np.uint32))
+        assert not lo[~mine_lo].any() and not hi[mine_lo].any()
+        # the exchange (a sum over the shards) then the combine on a shard bank
+        d_sum = rows[1][0] + rows[2][0]
+        banks[1].stack_batch_layer_device(0, rows[1][2], lg, d_sum, rows[1][1], 2)
+        banks[0].stack_batch_layer_device(0, rows[0][2], lg, rows[0][0], rows[0][1], 2)
+        torch.cuda.synchronize()
+        assert torch.equal(rows[1][2], rows[0][2])
+        del d_sum, rows
+        torch.cuda.synchronize()
+    finally:
+        for b in banks:
+            b.close()
