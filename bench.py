@@ -20,9 +20,18 @@ through all 40 layers.
            oracle/_ref/libref.so) on a persistent 64-row-job team over all host
            threads, one token-layer sample, extrapolated to the 40-layer stack.
 
-With --gpus N (torchrun), every rank decodes its own token stream on its own full
-bank (independent replicas); value is the sum over ranks of tokens / the slowest
-rank's time.
+With --gpus N (torchrun), the ranks shard the experts by ID and decode the same token
+stream together (the rows of each layer exchanged by peer stores inside the stack kernel;
+scaling "strong"); --replicas runs independent full-bank replicas instead (value = the sum
+over ranks of tokens / the slowest rank's time, scaling "weak").
+
+Other workloads (own JSON line each, same keys):
+  --prefill : BASELINE config 4, 2048 tokens through one 384-expert IQ2_XXS layer per step
+              (grouped tcgen05 GEMMs; roofline "tensor").
+  --skewed  : BASELINE config 5, a batch of 64 tokens through the 40-layer stack per step
+              with Zipf(1.1) routing (clb_stack_batch; at N GPUs expert-ID sharded with an
+              NCCL all-reduce of the expert rows per layer; roofline "hbm" over the distinct
+              experts' bytes).
 """
 import argparse
 import json
