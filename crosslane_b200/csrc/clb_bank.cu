@@ -1,6 +1,7 @@
 // Host side of the CUDA expert lane: bank, workspace, launches and the C ABI
 // declared in include/crosslane_b200.h.
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <atomic>
@@ -107,6 +108,15 @@ void host_parallel(size_t n, size_t grain, F&& f) {
     f((size_t)0, std::min(n, chunk));
     for (auto& t : th) t.join();
 }
+
+// NVTX range over one entry point ("clb:<call>"), visible in nsys / ncu timelines; a no-op
+// unless a tool is attached.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 bool finite_span(const float* v, size_t b, size_t e) {
     uint32_t bad = 0;
@@ -219,6 +229,9 @@ struct clb_bank {
     // stream around everything f enqueues (f ends with its copies back), one JSON line.
     template <class F>
     void timed_step(const char* call, int layer, int layers, int picks, uint64_t h2d, uint64_t d2h, F&& f) {
+        char name[48];
+        std::snprintf(name, sizeof name, "clb:%s", call);
+        NvtxRange range(name);
         if (!t_ev0) {
             device_step(f);
             return;
@@ -1100,6 +1113,7 @@ int32_t clb_moe_block_device(clb_bank* bank, uint32_t layer, const float* d_x, c
                              const float* d_bias, float scale, const float* d_shared, const float* d_resid,
                              float* d_out, float* d_logits, int32_t* d_ids, float* d_w, void* stream,
                              clb_error_v1* err) {
+    NvtxRange range("clb:moe_block_device");
     if (!bank) return fail(err, CLB_E_INVALID, "null bank");
     return guarded(err, [&] {
         bank->check_usable();
@@ -1239,6 +1253,7 @@ int32_t clb_stack_decode(clb_bank* bank, uint32_t first, int32_t nl, const float
 
 int32_t clb_stack_decode_device(clb_bank* bank, uint32_t first, int32_t nl, float* d_x, const float* d_logits,
                                 clb_error_v1* err) {
+    NvtxRange range("clb:stack_decode_device");
     if (!bank) return fail(err, CLB_E_INVALID, "null bank");
     return guarded(err, [&] {
         bank->check_usable();
@@ -1302,6 +1317,7 @@ uint64_t clb_prefill_workspace_bytes(const clb_bank* bank, int32_t tokens, int32
 static int32_t prefill_device(clb_bank* bank, uint32_t layer, int32_t tokens, int32_t k, const int32_t* d_ids,
                               const float* d_w, const float* d_x, const float* d_resid, float* d_out, void* d_ws,
                               uint64_t ws_bytes, int32_t phase_mask, void* stream, clb_error_v1* err) {
+    NvtxRange range("clb:prefill_device");
     if (!bank) return fail(err, CLB_E_INVALID, "null bank");
     return guarded(err, [&] {
         bank->check_usable();
@@ -1433,6 +1449,7 @@ uint64_t clb_stack_batch_workspace_bytes(const clb_bank* bank, int32_t tokens) {
 
 int32_t clb_stack_batch_device(clb_bank* bank, uint32_t first, int32_t nl, int32_t tokens, const float* d_logits,
                                float* d_h, void* d_ws, uint64_t ws_bytes, void* stream, clb_error_v1* err) {
+    NvtxRange range("clb:stack_batch_device");
     if (!bank) return fail(err, CLB_E_INVALID, "null bank");
     return guarded(err, [&] {
         bank->check_usable();
@@ -1456,6 +1473,7 @@ int32_t clb_stack_batch_device(clb_bank* bank, uint32_t first, int32_t nl, int32
 int32_t clb_stack_batch_layer_device(clb_bank* bank, uint32_t layer, int32_t tokens, const float* d_logits, float* d_h,
                                      float* d_rows, void* d_ws, uint64_t ws_bytes, int32_t phase_mask, void* stream,
                                      clb_error_v1* err) {
+    NvtxRange range("clb:stack_batch_layer_device");
     if (!bank) return fail(err, CLB_E_INVALID, "null bank");
     return guarded(err, [&] {
         bank->check_usable();
