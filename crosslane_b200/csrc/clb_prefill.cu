@@ -2,6 +2,12 @@
 // per expert and each expert's FFN runs as two grouped tensor-core GEMMs over its tokens
 // (gate/up over Q8_K(x), then down over Q8_K(h)), followed by the per-token combine in
 // ascending expert id (engine/strata/warm/runtime.cpp:184-187 applied to every token).
+// Experts with at most kPfColdMax picks skip the GEMMs: their (expert, token) pairs run the
+// decode kernels' one-row-per-lane row dots instead (k_pairs_*), which cost a third of the
+// GEMM decoder per weight. The same layer serves the batched stack decode (T tokens, one per
+// sequence, through consecutive layers: launch_stack_batch, with the stack's fixed-order
+// RMSNorm fused into Q8_K of x) and its expert-ID shards (picks outside [e_begin, e_end)
+// skipped, their rows zero, for a sum over the GPUs).
 //
 // Arithmetic. Per 256-value block b the reference forms exact integers
 // sum_k w_int[k] * q[k] (q8k_core.hpp:43-91) with q the Q8_K activation (|q| <= 127, exact
@@ -46,6 +52,11 @@
 //  * 8 epilogue warps (tensor-memory lane quarter x 32 columns): per block, D * d_w * d_x
 //    added into running tile sums that also live in tensor memory; the tile's last block
 //    writes the rows out.
+// Tile information (types; first entry, entries, row tile; MMA width) reaches the consumer
+// roles through 16-byte shared-memory headers released by the same mbarrier arrive as the
+// data, so no consumer warp loads from global memory per tile. The kernel is instantiated
+// per set of weight types present in the layer (TYPES), so a single-type layer decodes
+// without a type dispatch.
 // Control loops keep ring positions as counters (no divisions in the per-block path).
 // Waits sleep in mbarrier.try_wait (suspend hint) rather than spin, and are bounded in time:
 // on time-out the CTA flags *err and an abort flag that ends every loop, lets copies in
