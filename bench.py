@@ -365,6 +365,18 @@ def zipf_logits(rng, layers, T, E, s=1.1):
     return out
 
 
+def shard_load(ids_by_layer, experts, world):
+    """Mean over layers of (max over GPUs / mean over GPUs) of the distinct picked experts each
+    GPU decodes (its share of the layer's weight reads) when experts are split into `world`
+    contiguous ID blocks; ids_by_layer: [layers][tokens][k]."""
+    ratios = []
+    for ids in ids_by_layer:
+        owner = np.minimum((np.unique(np.asarray(ids)) * world) // experts, world - 1)
+        load = np.bincount(owner, minlength=world)
+        ratios.append(load.max() / load.mean())
+    return float(np.mean(ratios))
+
+
 def run_skewed(args, rank, world, local):
     """Config 5: a batch of 64 tokens (one per sequence) through the 40-layer stack per step,
     Zipf(1.1) routing, each layer one grouped prefill over the batch (clb_stack_batch)."""
@@ -426,6 +438,7 @@ def run_skewed(args, rank, world, local):
         dist.all_reduce(t)
         alg = t.cpu().tolist()
     alg_bytes = float(np.mean(alg)) + L * 2 * T * DIM * 4
+    routes0 = [[cb.route_host(0, lgs[0, l, t], k)[0] for t in range(T)] for l in range(L)]
     d_x = torch.from_numpy(xs).cuda()
     d_lg = torch.from_numpy(lgs).cuda()
     d_h = torch.empty((T, DIM), dtype=torch.float32, device="cuda")
@@ -515,6 +528,7 @@ def run_skewed(args, rank, world, local):
                    "picks": k, "types": "IQ2_XXS/IQ2_XS/IQ1_M per (layer, expert)",
                    "routing": "top-6 of log Zipf(1.1) over a per-layer seeded permutation + Gumbel noise",
                    "distinct_experts_per_layer": round(float(np.mean(distinct)), 1),
+                   "shard_load_max_over_mean": round(shard_load(routes0, args.experts, world), 3),
                    "parallelism": f"expert-ID sharded x{world}, rows all-reduced over NCCL per layer" if world > 1
                    else "single GPU",
                    "l2": "inputs larger than L2: %.1f GB of distinct expert weights per step" % (alg_bytes / 1e9)},

@@ -45,3 +45,20 @@ def test_logits_pick_distinct_experts():
     for l in range(3):
         for t in range(50):
             assert len(set(top_k(lg[l, t]).tolist())) == 6
+
+
+def test_shard_load_matches_contiguous_blocks():
+    """bench.shard_load uses the same contiguous expert blocks as sharded.shard_range, and at
+    8 GPUs the Zipf workload's max/mean load (distinct experts decoded per GPU) is near the
+    published 1.28."""
+    from crosslane_b200 import sharded
+    E = 384
+    for world in (2, 3, 8):
+        for e in range(E):
+            b, end = sharded.shard_range(E, sharded.owner_of(e, E, world), world)
+            assert b <= e < end and min((e * world) // E, world - 1) == sharded.owner_of(e, E, world)
+    rng = np.random.default_rng(4)
+    lg = bench.zipf_logits(rng, 40, 64, E)
+    ratio = bench.shard_load([top_k(lg[l]) for l in range(40)], E, 8)
+    assert 1.2 <= ratio <= 1.4, ratio
+    assert bench.shard_load([top_k(lg[l]) for l in range(40)], E, 1) == 1.0
