@@ -58,20 +58,27 @@ __device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err) {
     return grid_barrier(count, epoch, err, [] {});
 }
 
-// After a layer's down phase (all local CTAs past the grid barrier, their peer stores
-// fenced at system scope): CTA 0 tells every peer that this GPU's rows of layer li are in
-// place (a release add on the peer's flag for this rank), then every CTA waits until each
-// peer has said the same for its rows here. Flags only grow: layer li of the launch with
-// layer count `epoch` before it is complete at epoch + li + 1. Bounded like grid_barrier.
+// At the end of a layer's down phase every CTA tells every peer that its part of this GPU's
+// rows is in place: the CTA barrier orders its threads' peer stores before thread 0's
+// system-scope release add on the peer's flag for this rank (the release is cumulative over
+// the writes the barrier made it observe). No per-thread system fence.
+__device__ void signal_peers(const StackShard& sh) {
+    __syncthreads();
+    if (threadIdx.x == 0)
+        for (int r = 0; r < sh.world; ++r)
+            if (r != sh.rank)
+                asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(sh.peer_flags[r] + sh.rank), "r"(1u)
+                             : "memory");
+}
+
+// After the grid barrier that ends a layer: every CTA waits until every peer's CTAs have
+// signalled their rows of this layer (signal_peers). Flags only grow, by gridDim.x per layer
+// (every GPU runs the same grid): layer li of the launch with `epoch` layers before it is
+// complete at (epoch + li + 1) * gridDim.x, compared modulo 2^32. Bounded like grid_barrier.
 __device__ bool exchange_rows(const StackShard& sh, int li, int* err) {
     int ok = 1;
     if (threadIdx.x == 0) {
-        if (blockIdx.x == 0)
-            for (int r = 0; r < sh.world; ++r)
-                if (r != sh.rank)
-                    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(sh.peer_flags[r] + sh.rank), "r"(1u)
-                                 : "memory");
-        const unsigned target = sh.epoch + (unsigned)li + 1u;
+        const unsigned target = (sh.epoch + (unsigned)li + 1u) * gridDim.x;
         for (int r = 0; r < sh.world && ok; ++r) {
             if (r == sh.rank) continue;
             unsigned v = 0, spins = 0;
@@ -248,7 +255,6 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
 
     for (int li = 0; li <= P.nl; ++li) {
         const int cur = li & 1, prev = cur ^ 1;
-        bool stored_peer = false;  // this thread stored expert rows into a peer's slot
         const ExpertDesc* dl = dsc + cur * k;  // this layer's descriptors
         auto stage_next = [&] {
             if (li + 1 < P.nl) load_routing(li + 1);
@@ -450,7 +456,6 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                         ybuf(li)[o] = t;
                         for (int r = 0; r < sh.world; ++r)  // the peers' copies of this layer's slot
                             if (r != sh.rank) sh.peer_yx[r][((sh.epoch + li) & 1) * yslot + o] = t;
-                        stored_peer = sh.world > 1;
                     }
                 }
                 __syncthreads();
@@ -500,10 +505,9 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                 ybuf(li)[o] = y;
                 for (int r = 0; r < sh.world; ++r)
                     if (r != sh.rank) sh.peer_yx[r][((sh.epoch + li) & 1) * yslot + o] = y;
-                stored_peer = sh.world > 1;
             }
         }
-        if (stored_peer) __threadfence_system();  // this thread's peer stores before the barrier
+        if (sh.world > 1) signal_peers(sh);  // this CTA's peer stores, then one release per peer
         if (!grid_barrier(P.bar, 2 * li + 2, P.err, stage_next)) return;
         if (sh.world > 1 && !exchange_rows(sh, li, P.err)) return;
     }
