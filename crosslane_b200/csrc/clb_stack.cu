@@ -189,7 +189,9 @@ __device__ __forceinline__ double lane_sumsq(const float* hs, int dim, int lane)
     return s;
 }
 
-template <bool FAST, int NT>
+// MULTI: compiled with the expert-ID sharding exchange (peer stores, signals, waits); the
+// one-GPU instantiation carries none of it.
+template <bool FAST, int NT, bool MULTI>
 __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
     constexpr int NW = NT / 32;
     uint8_t* smem = clb_dyn_smem;
@@ -216,7 +218,9 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
     const StackShard& sh = P.sh;
     const size_t yslot = (size_t)k * dim;  // one layer's expert rows
     // expert rows of layer li: the bank's buffer, or (sharded) the exchange slot of its parity
-    auto ybuf = [&](int li) -> float* { return sh.world == 1 ? P.yrows : sh.yx + ((sh.epoch + li) & 1) * yslot; };
+    auto ybuf = [&](int li) -> float* {
+        return !MULTI || sh.world == 1 ? P.yrows : sh.yx + ((sh.epoch + li) & 1) * yslot;
+    };
 
     fill_row_tables(P.tables, xch_all);
     for (int i = tid; i < dim; i += NT) hs[i] = __ldcg(P.h_in + i);
@@ -454,7 +458,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                         for (int j = 0; j < SD; ++j) t = __fadd_rn(t, part[(rr * NW + s2 * SD + j) * 32 + lane]);
                         const size_t o = (size_t)own[pr2 / rgd] * dim + (pr2 % rgd) * 32 + lane;
                         ybuf(li)[o] = t;
-                        for (int r = 0; r < sh.world; ++r)  // the peers' copies of this layer's slot
+                        for (int r = 0; MULTI && r < sh.world; ++r)  // the peers' copies of this layer's slot
                             if (r != sh.rank) sh.peer_yx[r][((sh.epoch + li) & 1) * yslot + o] = t;
                     }
                 }
@@ -503,13 +507,13 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                 const float y = ok ? thread_row_dot_any<false>(m, row, hq, hd) : 0.0f;
                 const size_t o = (size_t)my_pick * dim + row;
                 ybuf(li)[o] = y;
-                for (int r = 0; r < sh.world; ++r)
+                for (int r = 0; MULTI && r < sh.world; ++r)
                     if (r != sh.rank) sh.peer_yx[r][((sh.epoch + li) & 1) * yslot + o] = y;
             }
         }
-        if (sh.world > 1) signal_peers(sh);  // this CTA's peer stores, then one release per peer
+        if (MULTI && sh.world > 1) signal_peers(sh);  // this CTA's peer stores, then one release per peer
         if (!grid_barrier(P.bar, 2 * li + 2, P.err, stage_next)) return;
-        if (sh.world > 1 && !exchange_rows(sh, li, P.err)) return;
+        if (MULTI && sh.world > 1 && !exchange_rows(sh, li, P.err)) return;
     }
     // h after the last layer: each CTA writes its slice
     const int per = (dim + G - 1) / G;
@@ -566,7 +570,9 @@ cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k
     P.sh = shard;
     const int nt = stack_threads(fast);
     const size_t sm = stack_smem(dim, ff, k, fast);
-    void (*kern)(StackParams) = fast ? k_stack<true, 512> : k_stack<false, 512>;
+    const bool multi = shard.world > 1;
+    void (*kern)(StackParams) = fast ? (multi ? k_stack<true, 512, true> : k_stack<true, 512, false>)
+                                     : (multi ? k_stack<false, 512, true> : k_stack<false, 512, false>);
     if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))) return e;
     if ((e = cudaMemsetAsync(bar, 0, sizeof(unsigned), s))) return e;
     void* args[] = {&P};
