@@ -176,6 +176,7 @@ struct clb_bank {
     uint8_t* d_xchg = nullptr;
     size_t xchg_bytes = 0;
     clb::StackShard shard;
+    clb::FlowWork flow;             // workspace of the dataflow stack kernel (fast order)
     std::vector<void*> opened_peers;
     float* d_logits = nullptr;
     int* d_route_ids = nullptr;
@@ -343,6 +344,13 @@ struct clb_bank {
         const int k = cfg.max_picks;
         if (dlogits)
             cuda_check(clb::launch_route_sigmoid(dlogits, cfg.n_experts, k, nl, d_route_ids, d_route_w, s), "route");
+        if (persistent && fast()) {
+            cuda_check(clb::launch_flow(d_desc, cfg.n_experts, (int)first, nl, k, d_route_ids, d_route_w, dx, dx,
+                                        cfg.dim, cfg.ff, cfg.limit, flow, d_err, shard, s),
+                       "dataflow stack kernel");
+            shard.epoch += (unsigned)nl;  // layer parity of the row-group counters (every GPU the same)
+            return;
+        }
         if (persistent) {
             cuda_check(clb::launch_stack(d_desc, cfg.n_experts, (int)first, nl, k, d_route_ids, d_route_w, dx, dx,
                                          cfg.dim, cfg.ff, cfg.limit, d_gu, d_yrows, d_bar, d_err, fast(), shard, s),
@@ -555,15 +563,26 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         cuda_check(cudaMemsetAsync(bank->d_cnt_h, 0, sizeof(int) * k * ff / 256, bank->stream), "memset");
         cuda_check(cudaMemsetAsync(bank->d_cnt_y, 0, sizeof(int) * ((dim + 15) / 16), bank->stream), "memset");
         bank->d_bar = bank->dev_alloc<unsigned>(2);
-        bank->xchg_bytes = 2 * k * dim * sizeof(float) + clb::kMaxPeers * sizeof(unsigned);
+        // exchange region: expert rows [2][k][dim], kMaxPeers peer counters, row-group counters [2][dim / 32]
+        bank->xchg_bytes = 2 * k * dim * sizeof(float) + clb::kMaxPeers * sizeof(unsigned) + 2 * (dim / 32) * sizeof(unsigned);
         bank->d_xchg = bank->dev_alloc<uint8_t>(bank->xchg_bytes);
         cuda_check(cudaMemsetAsync(bank->d_xchg, 0, bank->xchg_bytes, bank->stream), "memset");
         bank->shard.own_begin = cfg.expert_begin;
         bank->shard.own_end = cfg.expert_end;
         bank->shard.yx = reinterpret_cast<float*>(bank->d_xchg);
         bank->shard.flags = reinterpret_cast<unsigned*>(bank->d_xchg + 2 * k * dim * sizeof(float));
+        bank->shard.rgcnt = bank->shard.flags + clb::kMaxPeers;
         bank->persistent = (cfg.flags & CLB_BANK_PER_LAYER_KERNELS) == 0 &&
-                           clb::stack_supported(cfg.dim, cfg.ff, cfg.max_picks, bank->fast());
+                           (bank->fast() ? clb::flow_supported(cfg.dim, cfg.ff, cfg.max_picks)
+                                         : clb::stack_supported(cfg.dim, cfg.ff, cfg.max_picks, false));
+        if (bank->persistent && bank->fast()) {
+            bank->flow.hbuf = bank->dev_alloc<float>(2 * dim);
+            bank->flow.ssbuf = bank->dev_alloc<float>(2 * (dim / 32));
+            bank->flow.gu = bank->d_gu;
+            bank->flow.hq = bank->dev_alloc<int8_t>(k * ff);
+            bank->flow.hd = bank->dev_alloc<float>(k * ff / 256);
+            bank->flow.cnt = bank->dev_alloc<unsigned>(clb::flow_counter_words(cfg.n_layers, (int)k, (int)ff));
+        }
         bank->d_ids = bank->dev_alloc<int>(k);
         bank->d_w = bank->dev_alloc<float>(k);
         bank->d_err = bank->dev_alloc<int>(1);
@@ -707,6 +726,7 @@ int32_t clb_bank_connect(clb_bank* bank, int32_t rank, int32_t world, const void
                 const size_t k = (size_t)bank->cfg.max_picks, dim = (size_t)bank->cfg.dim;
                 sh.peer_yx[r] = static_cast<float*>(p);
                 sh.peer_flags[r] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(p) + 2 * k * dim * sizeof(float));
+                sh.peer_rgcnt[r] = sh.peer_flags[r] + clb::kMaxPeers;
             }
         } catch (...) {
             for (void* p : opened) cudaIpcCloseMemHandle(p);

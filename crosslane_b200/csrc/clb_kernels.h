@@ -93,18 +93,41 @@ constexpr int kMaxPeers = 8;  // GPUs of one node
 // own_end) of every layer and computes only those picks; the expert rows of every layer
 // go to all GPUs through peer stores into double-buffered slots (yx: [2][k][dim] floats,
 // then `flags`: one counter per source GPU). world == 1: no sharding.
+// The dataflow kernel (clb_flow.cu) also keeps per-row-group completion counters there
+// (rgcnt: [2][dim / 32], one set per layer parity), which every GPU increments.
 struct StackShard {
     int world = 1, rank = 0, own_begin = 0, own_end = 0x7fffffff;
-    unsigned epoch = 0;               // layers this bank has run sharded before this launch
+    unsigned epoch = 0;               // layers this bank has run through a stack kernel before this launch
     float* yx = nullptr;
     unsigned* flags = nullptr;
+    unsigned* rgcnt = nullptr;
     float* peer_yx[kMaxPeers] = {};
     unsigned* peer_flags[kMaxPeers] = {};
+    unsigned* peer_rgcnt[kMaxPeers] = {};
 };
 size_t stack_smem(int dim, int ff, int k, bool fast);
 bool stack_supported(int dim, int ff, int k, bool fast);
 cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
                          const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit, float* gu,
                          float* yrows, unsigned* bar, int* err, bool fast, const StackShard& shard, cudaStream_t s);
+
+// Dataflow whole-stack kernel (clb_flow.cu), fast summation order. Workspace:
+//   hbuf [2][dim] residual stream between layers, ssbuf [2][dim / 32] sums of squares per
+//   32-row group, gu [k][ff] SwiGLU outputs, hq [k][ff] + hd [k][ff / 256] their Q8_K,
+//   cnt: flow_counter_words(nl_max, k, ff) counters, zeroed by launch_flow before each launch.
+struct FlowWork {
+    float* hbuf = nullptr;
+    float* ssbuf = nullptr;
+    float* gu = nullptr;
+    int8_t* hq = nullptr;
+    float* hd = nullptr;
+    unsigned* cnt = nullptr;
+};
+size_t flow_counter_words(int nl_max, int k, int ff);
+size_t flow_smem(int dim, int ff, int k);
+bool flow_supported(int dim, int ff, int k);
+cudaError_t launch_flow(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
+                        const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit,
+                        const FlowWork& w, int* err, const StackShard& shard, cudaStream_t s);
 
 }  // namespace clb

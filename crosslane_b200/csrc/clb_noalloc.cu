@@ -30,7 +30,8 @@ constexpr size_t kOffXd = kOffXqs + kNoAllocMaxDim;
 constexpr size_t kOffH = kOffXd + 256;
 constexpr size_t kOffHqs = kOffH + 4 * (size_t)kNoAllocMaxFF;
 constexpr size_t kOffHd = kOffHqs + kNoAllocMaxFF;
-constexpr size_t kNoAllocScratchBytes = kOffHd + 256;  // 57,728 bytes
+constexpr size_t kNoAllocScratchBytes = kOffHd + 256;  // 57,856 bytes
+static_assert(kNoAllocScratchBytes == 57856, "the documented size of the fixed scratch array");
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 

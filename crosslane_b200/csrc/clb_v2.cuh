@@ -296,6 +296,137 @@ __device__ __forceinline__ float lane_row_partial_any(const PackedMat& m, int ro
     return lane_row_partial<CLB_IQ1_M, AS>(m, row, b0, b1, aq, ad);
 }
 
+// ---- fast order, one row per lane, register double buffer (the dataflow stack kernel) ----
+// block_sum's exact integers, except that IQ1_M folds its delta into the main sum: every
+// weight becomes the integer 8q + delta (q in {-1, 0, 1}, delta = +-1 per 8-value group,
+// |8q + delta| <= 9), taken straight from the byte pairs {-7, 1, 9} | {-9, -1, 7} with the
+// group's delta sign as selector bit 2, so one dp4a per 4 weights gives
+// 8 * main + delta (q8k_core.hpp:79-84 keeps them apart: main + delta / 8 is 1/8 of it).
+constexpr uint32_t kIq1DeltaPos = 0x000901F9u;  // -7, 1, 9
+constexpr uint32_t kIq1DeltaNeg = 0x0007FFF7u;  // -9, -1, 7
+template <int T>
+__device__ __forceinline__ int block_sum8(const RowRaw& r, const int8_t* q, uint32_t lb) {
+    if (T != CLB_IQ1_M) {
+        int M, D;
+        block_sum<T>(r, q, lb, M, D);
+        return M;
+    }
+    int M = 0;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint4 qa = *reinterpret_cast<const uint4*>(q + 32 * c);
+        const uint4 qb = *reinterpret_cast<const uint4*>(q + 32 * c + 16);
+        const uint32_t qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        const uint32_t qsw = rw(r, c);
+        const uint32_t qh16 = (rw(r, 8 + (c >> 1)) >> (16 * (c & 1))) & 0xffffu;
+        const uint32_t scw = ((c < 4 ? r.sc.x : r.sc.y) >> (16 * ((c >> 1) & 1))) & 0xffffu;
+        const int s_lo = (int)(((scw >> (6 * (c & 1))) & 7u) << 1) | 1;
+        const int s_hi = (int)(((scw >> (6 * (c & 1) + 3)) & 7u) << 1) | 1;
+        int alo = 0, ahi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t nib = (qh16 >> (4 * j)) & 15u;
+            const uint32_t idx = ((qsw >> (8 * j)) & 0xffu) | ((nib & 7u) << 8);
+            const uint32_t sel = tab32(kRowTabIQ1 + idx * 16u + (lb & 12u)) | ((nib & 8u) ? 0x44444444u : 0u);
+            int& a = j < 2 ? alo : ahi;
+            a = __dp4a((int)prmt_sel(kIq1DeltaPos, kIq1DeltaNeg, sel), (int)qv[2 * j], a);
+            a = __dp4a((int)prmt_sel(kIq1DeltaPos, kIq1DeltaNeg, sel >> 16), (int)qv[2 * j + 1], a);
+        }
+        M += s_lo * alo + s_hi * ahi;
+    }
+    return M;
+}
+
+// Streaming weight loads: read once, so they bypass L1 allocation and leave the L1 lines
+// to the data that is reused (activations, the stack).
+__device__ __forceinline__ uint4 ldg_v4_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ldg_v2_stream(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint16_t ldg_u16_stream(const void* p) {
+    uint16_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+
+template <int T>
+__device__ __forceinline__ void load_raw_at(const uint8_t* p, size_t pstride, const uint8_t* sc, const uint16_t* dp,
+                                            RowRaw& r) {
+    r.b0 = ldg_v4_stream(p);
+    r.b1 = ldg_v4_stream(p + pstride);
+    r.b2 = ldg_v4_stream(p + 2 * pstride);
+    if (T != CLB_IQ1_M) r.b3 = ldg_v4_stream(p + 3 * pstride);
+    if (T != CLB_IQ2_XXS) r.sc = ldg_v2_stream(sc);
+    if (T != CLB_IQ1_M) r.d = ldg_u16_stream(dp);
+}
+
+// Partial of one row over blocks [b0, b1): 0.125 * sum_b (d_w * d_x)_b * M_b with M_b =
+// block_sum8 (for IQ1_M the 8q + delta integer), blocks in order, fp32. The next block's
+// bytes are loaded into registers while the current one is decoded. AS: byte stride of
+// the activation blocks (kActStride in shared memory, 256 for a Q8_K row in global memory).
+template <int T, int AS = kActStride>
+__device__ __noinline__ float lane_row_db(const PackedMat& m, int row, int b0, int b1, const int8_t* act_qs,
+                                          const float* act_d) {
+    constexpr int NP = T == CLB_IQ1_M ? 3 : 4;
+    const uint32_t lb = (threadIdx.x & 31) * 4u;
+    const size_t n = (size_t)m.n, pstride = n * 16, bstride = (size_t)NP * n * 16;
+    const uint8_t* p = m.body + (size_t)b0 * bstride + (size_t)row * 16;
+    const uint8_t* sc = T == CLB_IQ2_XXS ? nullptr : m.sc + ((size_t)b0 * n + (size_t)row) * 8;
+    const uint16_t* dp = T == CLB_IQ1_M ? nullptr : m.d + (size_t)b0 * n + (size_t)row;
+    float acc = 0.0f;
+    auto step = [&](const RowRaw& r, int b) {
+        const int M = block_sum8<T>(r, act_qs + (size_t)b * AS, lb);
+        acc = __fmaf_rn(__fmul_rn(raw_scale<T>(r), act_d[b]), (float)M, acc);
+    };
+    auto advance = [&] {
+        p += bstride;
+        if (T != CLB_IQ2_XXS) sc += n * 8;
+        if (T != CLB_IQ1_M) dp += n;
+    };
+    RowRaw ra, rb;
+    if (b0 < b1) load_raw_at<T>(p, pstride, sc, dp, ra);
+    for (int b = b0; b < b1; b += 2) {
+        if (b + 1 < b1) {
+            advance();
+            load_raw_at<T>(p, pstride, sc, dp, rb);
+        }
+        step(ra, b);
+        if (b + 1 >= b1) break;
+        if (b + 2 < b1) {
+            advance();
+            load_raw_at<T>(p, pstride, sc, dp, ra);
+        }
+        step(rb, b + 1);
+    }
+    return __fmul_rn(0.125f, acc);
+}
+template <int AS = kActStride>
+__device__ __forceinline__ float lane_row_db_any(const PackedMat& m, int row, int b0, int b1, const int8_t* aq,
+                                                 const float* ad) {
+    if (m.type == CLB_IQ2_XXS) return lane_row_db<CLB_IQ2_XXS, AS>(m, row, b0, b1, aq, ad);
+    if (m.type == CLB_IQ2_XS) return lane_row_db<CLB_IQ2_XS, AS>(m, row, b0, b1, aq, ad);
+    return lane_row_db<CLB_IQ1_M, AS>(m, row, b0, b1, aq, ad);
+}
+
+// L2 prefetch of the first block of a row segment (no registers held).
+__device__ __forceinline__ void prefetch_row_block(const PackedMat& m, int row, int b) {
+    const int np = m.type == CLB_IQ1_M ? 3 : 4;
+    const size_t n = (size_t)m.n;
+    const uint8_t* p = m.body + ((size_t)b * np * n + (size_t)row) * 16;
+    prefetch_l2(p);
+    prefetch_l2(p + n * 16);
+    prefetch_l2(p + n * 32);
+    if (np == 4) prefetch_l2(p + n * 48);
+}
+
 // S in {1, 2, 3, 4, 6, 8} (kSegChoices); anything else is treated as 1.
 template <bool PF>
 __device__ __forceinline__ float seg_row_dot_any(const PackedMat& m, int row, int S, const int8_t* aq,

@@ -1,4 +1,4 @@
-"""Frozen warm placement with this library as a lane (SURVEY row "placement / rebalancer").
+"""Frozen warm placement and the rebalancer's cost document with this library as a lane.
 
 crosslane freezes which lane serves each (layer, expert) in a STRATA_WARM_PLACEMENT_V1
 document (engine/strata/warm/frozen_placement.hpp:5-16) and chooses it with a

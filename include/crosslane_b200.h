@@ -443,7 +443,7 @@ int32_t clb_bank_synchronize(clb_bank* bank, clb_error_v1* err);
  * being captured into a CUDA graph, a serving loop that must not risk an allocation's
  * implicit device synchronisation, a plugin whose device memory belongs to another
  * allocator): the quantised input, hidden vector and its quantisation live in one fixed
- * 57,728-byte array inside the library, held by every GPU that loads it until exit.
+ * 57,856-byte array inside the library, held by every GPU that loads it until exit.
  * Limits: dim <= 16384, ff <= 8192 (else CLB_E_UNSUPPORTED with a message). It calls no
  * cudaMalloc/cudaFree. The first call on a device resolves that array's address and
  * uploads the decode tables (a synchronising step): make it before any stream capture.

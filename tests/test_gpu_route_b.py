@@ -1,4 +1,4 @@
-"""Device-side routing of the MoE block (SURVEY 8f item 2): the router GEMV against an fp64
+"""Device-side routing of the MoE block: the router GEMV against an fp64
 reference, crosslane's route_cpu (mode 1) on the device against the host restatement
 (clb_route_host, the oracle's route_cpu) bit for bit, and the whole MoE block on the device
 (router -> route -> experts -> combine, no host round trip) against the oracle layer."""

@@ -5,8 +5,9 @@ CUDA graph, a serving loop that must not risk an allocation's device synchronisa
 plugin whose device memory is owned by another allocator. This entry point takes packed
 weights, x and y from the caller and keeps its own intermediates in a fixed array inside
 the library. Here its output is checked against the bank's warm_compute on the same
-expert, twice in a row (the second call reuses the array with the first call's contents
-still in it), at the parity tolerance used throughout the GPU tests.
+expert and against the CPU oracle's expert, twice in a row (the second call reuses the
+array with the first call's contents still in it), at the parity tolerance used
+throughout the GPU tests; also at the largest shape the array covers (dim 16384, ff 8192).
 """
 import ctypes as C
 
@@ -29,11 +30,11 @@ def _call(cb, qtype, d_gate, d_up, d_down, d_x, d_y, dim, ff, limit):
     return rc, err.message.decode()
 
 
-@pytest.mark.parametrize("qtype", [16, 17, 29])
-def test_noalloc_matches_bank_compute(cuda, orc, qtype):
+@pytest.mark.parametrize("qtype,dim,ff", [(16, 7168, 1536), (17, 7168, 1536), (29, 7168, 1536), (16, 16384, 8192)])
+def test_noalloc_matches_bank_compute(cuda, orc, qtype, dim, ff):
     import crosslane_b200 as cb
     torch = cuda
-    dim, ff, limit, seed = 7168, 1536, 0.0, 314
+    limit, seed = 0.0, 314
     mats = [orc.synth_matrix(qtype, seed, 0, 2, role, n, k)
             for role, (n, k) in enumerate([(ff, dim), (ff, dim), (dim, ff)])]
     bank = cb.ExpertBank(n_layers=1, n_experts=4, dim=dim, ff=ff, max_picks=1, limit=limit)
@@ -46,6 +47,7 @@ def test_noalloc_matches_bank_compute(cuda, orc, qtype):
         for call in range(2):
             x = rng.standard_normal(dim).astype(np.float32)
             want = bank.warm_compute(0, 2, x)
+            _, ref_y = orc.expert(qtype, mats[0], mats[1], mats[2], x, dim, ff, limit)
             d_x = torch.from_numpy(x).cuda()
             d_y = torch.full((dim,), float("nan"), dtype=torch.float32, device="cuda")
             torch.cuda.synchronize()
@@ -55,6 +57,7 @@ def test_noalloc_matches_bank_compute(cuda, orc, qtype):
             got = d_y.cpu().numpy()
             assert np.all(np.isfinite(got)), f"call {call}"
             assert rel_l2(got, want) <= REL_L2 and max_abs_rel(got, want) <= MAX_ABS_REL, f"call {call}"
+            assert rel_l2(got, ref_y) <= REL_L2 and max_abs_rel(got, ref_y) <= MAX_ABS_REL, f"call {call} vs oracle"
     finally:
         bank.close()
 
