@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
 
 #include "clb_device.cuh"
 #include "clb_kernels.h"
@@ -49,8 +50,10 @@ void host_tables(uint32_t* out) {
 }
 
 cudaError_t upload_tables(cudaStream_t stream) {
+    // filled once (threads setting up different devices share the read-only copy)
     static uint32_t host[kTableWords];
-    host_tables(host);
+    static std::once_flag filled;
+    std::call_once(filled, [] { host_tables(host); });
     cudaError_t e = cudaMemcpyToSymbolAsync(g_tables, host, sizeof(host), 0, cudaMemcpyHostToDevice, stream);
     if (e != cudaSuccess) return e;
     return cudaStreamSynchronize(stream);

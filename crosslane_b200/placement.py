@@ -103,10 +103,16 @@ def measure_cuda_costs(bank, layers=None, picks: int = 6, reps: int = 8, seed: i
 
 
 def rebalance_costs(cuda_ns, cpu_ns, decode_tokens: int, profile_bytes: bytes, gpu_slot: str = "hip",
-                    evidence=None):
+                    other_ns=None, evidence=None):
     """A strata-warm-costs-v1 document for crosslane's optimiser (rebalance.py) with the
     CUDA lane in the `gpu_slot` column (the optimiser knows the lanes cpu/hip/sycl): per
-    layer {per_expert_ns, issue_ns: 0}; cuda_ns / cpu_ns: {layer: per-selection ns}."""
+    layer {per_expert_ns, issue_ns: 0}; cuda_ns / cpu_ns / other_ns: {layer: per-selection
+    ns}. other_ns: the measured costs of the lane in the other GPU column (a B65 next to the
+    CUDA lane in the HIP slot, say). Without it that column is an unused lane: the
+    optimiser still requires a positive cost there, so it gets the CPU lane's (it can win
+    nothing), and the plan must give that lane no room (warm_hip_room_bytes = 0 for the
+    HIP column; the SYCL column carries the optimiser's per-layer coverage floor, so a lone
+    CUDA lane takes gpu_slot="sycl")."""
     if gpu_slot not in ("hip", "sycl"):
         raise ValueError("gpu_slot must be one of the optimiser's GPU lanes")
     layers = sorted(set(cuda_ns) | set(cpu_ns))
@@ -114,13 +120,17 @@ def rebalance_costs(cuda_ns, cpu_ns, decode_tokens: int, profile_bytes: bytes, g
         raise ValueError("costs must cover layers 0..n-1")
     rows = []
     for l in layers:
-        if l not in cuda_ns or l not in cpu_ns:
+        if l not in cuda_ns or l not in cpu_ns or (other_ns is not None and l not in other_ns):
             raise ValueError(f"layer {l} lacks a measured cost")
         row = {"cpu": {"per_expert_ns": float(cpu_ns[l]), "issue_ns": 0, "measurement_source": "caller"},
                gpu_slot: {"per_expert_ns": float(cuda_ns[l]), "issue_ns": 0,
                           "measurement_source": "crosslane_b200 clb_bank_compute_many per selection"}}
         other = "sycl" if gpu_slot == "hip" else "hip"
-        row[other] = {"per_expert_ns": float(cuda_ns[l]), "issue_ns": 0, "measurement_source": "unused lane"}
+        if other_ns is not None:
+            row[other] = {"per_expert_ns": float(other_ns[l]), "issue_ns": 0, "measurement_source": "caller"}
+        else:
+            row[other] = {"per_expert_ns": float(cpu_ns[l]), "issue_ns": 0,
+                          "measurement_source": "unused lane (no room in the plan)"}
         rows.append(row)
     return {"schema": "strata-warm-costs-v1", "scope": "measured-decode-excluding-warmup",
             "decode_tokens": int(decode_tokens), "profile_sha256": hashlib.sha256(profile_bytes).hexdigest(),

@@ -11,6 +11,11 @@ if TESTS not in sys.path:
     sys.path.insert(0, TESTS)
 
 
+def pytest_addoption(parser):
+    parser.addoption("--crosslane-ref", default=None,
+                     help="crosslane checkout for the tests that compile against its headers")
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (run with -m gpu on a B200)")
     config.addinivalue_line("markers", "slow: long-running CPU test")

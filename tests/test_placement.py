@@ -96,3 +96,72 @@ def test_bank_holds_placed_experts(cuda, orc):
         assert rel_l2(got, want) <= 1e-3
     finally:
         bank.close()
+
+
+def _reference_rebalance(request):
+    """crosslane's own optimiser module (engine/strata/warm/rebalance.py), loaded from the
+    checkout the tests compile against; skipped where no checkout exists."""
+    import importlib.util
+    import os
+    ref = request.config.getoption("--crosslane-ref") or os.environ.get("CROSSLANE_REF")
+    recorded = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref", "checkout")
+    if not ref and os.path.isfile(recorded):
+        with open(recorded) as f:
+            ref = f.read().strip()
+    path = os.path.join(ref or "", "engine", "strata", "warm", "rebalance.py")
+    if not ref or not os.path.isfile(path):
+        pytest.skip("no crosslane checkout (set CROSSLANE_REF or --crosslane-ref)")
+    spec = importlib.util.spec_from_file_location("crosslane_rebalance", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _plan_and_profile(tmp_path, counts, hip_room, sycl_room, hip_resident, sycl_members):
+    """A two-layer, four-expert plan in the shape crosslane's native planner writes (the
+    fields rebalance.py:25-52 reads) and the decode profile of selection counts."""
+    profile = tmp_path / "decode.bin"
+    profile.write_bytes(b"".join(int(c).to_bytes(4, "little") for c in counts))
+    g = 2 ** 21
+    plan = {"layers": 2, "sycl_footprint": 1_000_000_000, "hip_footprint": 1_000_000_000,
+            "warm_inventory": [[l, e, g, g, "IQ2_XXS", "IQ2_XS", "IQ1_M"] for l in range(2) for e in range(4)],
+            "hip_resident": {"experts": [[l, e, 0, g] for l, e in hip_resident]},
+            "warm_sycl": {"members": [[l, e] for l, e in sycl_members], "reservation_bytes": sycl_room,
+                          "profile_tag": 7},
+            "warm_hip_room_bytes": hip_room}
+    return plan, profile
+
+
+def test_reference_optimiser_accepts_cuda_costs_in_hip_slot(request, tmp_path):
+    """The CUDA lane in the HIP column next to a measured B65 lane: crosslane's optimiser
+    accepts the cost document and moves the hot CPU experts onto the CUDA lane."""
+    rb = _reference_rebalance(request)
+    counts = [1, 1, 10, 0] * 2  # expert 2 of each layer is hot and starts on the CPU lane
+    plan, profile = _plan_and_profile(tmp_path, counts, hip_room=2 * 2 ** 21, sycl_room=2 * 2 ** 21,
+                                      hip_resident=[(0, 0), (1, 0)], sycl_members=[(0, 1), (1, 1)])
+    costs = pl.rebalance_costs({0: 1.0, 1: 1.0}, {0: 10.0, 1: 10.0}, 12, profile.read_bytes(), gpu_slot="hip",
+                               other_ns={0: 2.0, 1: 2.0})
+    assigned, report = rb.optimise(plan, str(profile), costs, min_payload=0)
+    assert report["after_ns"] < report["before_ns"]
+    assert all(assigned[l, 2] == pl.HIP for l in range(2))  # the CUDA lane holds the GPU slot 1
+    text = rb.assignment_text(assigned, plan)
+    lanes, tag = pl.parse(text, 2, 4)  # the optimiser's output is a document this library applies
+    assert tag == 7 and lanes[0, 2] == pl.HIP
+
+
+def test_reference_optimiser_with_lone_cuda_lane(request, tmp_path):
+    """The CUDA lane alone, in the SYCL column (the one with the optimiser's per-layer
+    coverage floor); the unused HIP column has no room, so nothing can land there."""
+    rb = _reference_rebalance(request)
+    counts = [1, 10, 1, 0] * 2
+    plan, profile = _plan_and_profile(tmp_path, counts, hip_room=0, sycl_room=2 * 2 ** 21, hip_resident=[],
+                                      sycl_members=[(0, 0), (1, 0)])
+    costs = pl.rebalance_costs({0: 1.0, 1: 1.0}, {0: 10.0, 1: 10.0}, 12, profile.read_bytes(), gpu_slot="sycl")
+    assert all(r["hip"]["measurement_source"].startswith("unused") for r in costs["layers"])
+    assigned, report = rb.optimise(plan, str(profile), costs, min_payload=0)
+    assert report["after_ns"] < report["before_ns"]
+    assert all(assigned[l, 1] == pl.SYCL for l in range(2))  # the hot expert moved onto the CUDA lane
+    assert all(lane != pl.HIP for lane in assigned.values())  # the lane without room got nothing
+    bad = dict(costs, profile_sha256="0" * 64)  # provenance still enforced
+    with pytest.raises(ValueError):
+        rb.optimise(plan, str(profile), bad, min_payload=0)
