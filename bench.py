@@ -126,57 +126,109 @@ def make_inputs(rng, n, layers=LAYERS, experts=EXPERTS):
     return xs, logits
 
 
-def cpu_baseline(samples=1, threads=0):
-    """Reference CPU lane (oracle/_ref: crosslane q8k_core.hpp) on one token-layer."""
-    sys.path.insert(0, os.path.join(ROOT, "tests"))
-    import oracle_lib
-    ref = oracle_lib.reference()
-    if ref is None:
-        return None
-    orc = oracle_lib.Oracle()
-    rng = np.random.default_rng(99)
-    times = []
-    cores = None
-    for s in range(samples + 1):  # first sample warms the team and page cache
-        layer = s % LAYERS
-        ids, w = orc.route_sigmoid(rng.standard_normal(EXPERTS).astype(np.float32), PICKS)
-        x = rng.standard_normal(DIM).astype(np.float32)
-        mats = []
-        for e in ids:
-            t = orc.expert_type(POLICY, SEED, layer, int(e))
-            mats.append((t, orc.synth_matrix(t, SEED, layer, int(e), 0, FF, DIM),
-                         orc.synth_matrix(t, SEED, layer, int(e), 1, FF, DIM),
-                         orc.synth_matrix(t, SEED, layer, int(e), 2, DIM, FF)))
+class CpuLaneTokens:
+    """Whole config-3 tokens through the timed CPU expert lane (oracle/liblane.so: crosslane's
+    q8k_core.hpp arithmetic vectorised with AVX2, pinned bit-identical to the reference
+    compiled here; layer-batched like the reference lane's Lane::experts on a persistent
+    team of all host threads). Per layer: x = RMSNorm(h), the 6 picked experts, the
+    ascending-id fma combine, h += it -- the GPU step's work on the host. The weights of
+    `pool` token-layers (6 config-3 experts each, ~50 MB per slot, generated once, outside
+    the timed region, 0 store readers) are cycled through the 40 layers, so every layer
+    streams its experts from host memory (the pool exceeds the last-level cache)."""
+
+    def __init__(self, pool=8, threads=0, seed=99):
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        import oracle_lib
+        self.orc = oracle_lib.Oracle()
+        self.lane = oracle_lib.cpu_lane()
+        if self.lane is None:
+            raise RuntimeError("oracle/liblane.so is not built")
+        self.threads = threads
+        rng = np.random.default_rng(seed)
+        self.slots = []
+        for s in range(pool):
+            ids, _ = self.orc.route_sigmoid(rng.standard_normal(EXPERTS).astype(np.float32), PICKS)
+            ts = [self.orc.expert_type(POLICY, SEED, s, int(e)) for e in ids]
+            mats = [[self.orc.synth_matrix(t, SEED, s, int(e), r, *((FF, DIM) if r < 2 else (DIM, FF)))
+                     for r in range(3)] for t, e in zip(ts, ids)]
+            self.slots.append((np.asarray(ids, np.int32), ts, mats))
+        self.cores = self.lane.L.lane_team_threads(threads)
+
+    def token(self, h0, logits):
+        """One token through LAYERS layers; returns (h, seconds)."""
         t0 = time.perf_counter()
-        rows = np.stack([ref.expert(t, g, u, d, x, DIM, FF, 0.0, threads)[1] for t, g, u, d in mats])
-        ref.combine(ids, w, rows)
-        dt = time.perf_counter() - t0
-        if s > 0:
-            times.append(dt)
-        cores = ref.L.ref_team_threads(threads)
-    per_layer = statistics.median(times)
-    return {"value": 1.0 / (per_layer * LAYERS), "unit": "tok/s", "cores": int(cores), "kind": "reference",
-            "sample": f"{samples} token-layer(s) of config 3 (6 experts each, weights generated in RAM, "
-                      f"0 store readers), median {per_layer * 1e3:.1f} ms per token-layer x {LAYERS} layers; "
-                      f"crosslane q8k_core.hpp arithmetic, persistent 64-row-job team"}
+        h = np.ascontiguousarray(h0, np.float32).copy()
+        for l in range(LAYERS):
+            ids, ts, mats = self.slots[l % len(self.slots)]
+            _, w = self.orc.route_sigmoid(logits[l], PICKS)
+            y, _ = self.lane.experts(ts, [m[0] for m in mats], [m[1] for m in mats], [m[2] for m in mats],
+                                     self.orc.rmsnorm(h), DIM, FF, 0.0, self.threads)
+            h = (h + self.orc.combine(ids, w, y)).astype(np.float32)
+        return h, time.perf_counter() - t0
+
+
+def cpu_baseline(tokens=3, threads=0):
+    """The CPU lane timed on `tokens` whole config-3 tokens (median / min / max)."""
+    try:
+        run = CpuLaneTokens(threads=threads)
+    except RuntimeError:
+        return None
+    rng = np.random.default_rng(7)
+    run.token(rng.standard_normal(DIM).astype(np.float32), rng.standard_normal((LAYERS, EXPERTS)).astype(np.float32))
+    times = [run.token(rng.standard_normal(DIM).astype(np.float32),
+                       rng.standard_normal((LAYERS, EXPERTS)).astype(np.float32))[1] for _ in range(tokens)]
+    med = statistics.median(times)
+    return {"value": 1.0 / med, "unit": "tok/s", "cores": int(run.cores), "kind": "port",
+            "sample": f"{tokens} whole config-3 tokens (40 layers x 6 experts, mixed IQ2_XXS/IQ2_XS/IQ1_M) after one "
+                      f"warm-up token; {med * 1e3:.1f} ms per token median, {min(times) * 1e3:.1f} min, "
+                      f"{max(times) * 1e3:.1f} max; crosslane's q8k_core.hpp arithmetic vectorised with AVX2 "
+                      f"(bit-identical to it), layer-batched like Lane::experts on {run.cores} host threads; "
+                      f"weights generated in host memory (0 store readers)",
+            "repeats": {"runs": tokens, "median_ms": round(med * 1e3, 2), "min_ms": round(min(times) * 1e3, 2),
+                        "max_ms": round(max(times) * 1e3, 2)}}
+
+
+def config3(args, world, sharded):
+    return {"workload": WORKLOAD, "layers": args.layers, "experts": args.experts, "dim": DIM, "ff": FF, "picks": PICKS,
+            "types": "IQ2_XXS/IQ2_XS/IQ1_M per (layer, expert), seed-drawn", "batch": 1,
+            "routing": "top-6 by sigmoid of N(0,1) logits, renormalised",
+            "parallelism": (f"expert-ID sharded x{world} (peer-store row exchange in the stack kernel)"
+                            if sharded else f"replica x{world}" if world > 1 else "single GPU"),
+            "summation": "exact reference order" if args.exact_order
+            else "segmented rows, fixed-order partials (run-to-run identical)",
+            "l2": "inputs larger than L2: each token streams ~2 GB of distinct expert weights"}
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the CPU lane on `steps` whole tokens (each step is timed and is
+    one token through the 40-layer stack), after `warmup` untimed tokens."""
     if rank != 0:
         return
-    samples = max(1, args.steps)
-    res = cpu_baseline(samples=samples)
-    if res is None:
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref.so (crosslane q8k_core.hpp) "
-                                                              "was not built on this machine"}))
+    try:
+        run = CpuLaneTokens()
+    except RuntimeError as e:
+        print(json.dumps({"impl": "reference", "unavailable": f"CPU lane not built: {e}"}))
         return
-    line = {"metric": METRIC, "value": res["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1e3 / res["value"], "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8xIQ/fp32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "layers": LAYERS, "experts": EXPERTS, "dim": DIM, "ff": FF,
-                       "picks": PICKS, "types": "IQ2_XXS/IQ2_XS/IQ1_M per (layer, expert)", "batch": 1},
-            "impl": "reference", "cpu_baseline": res,
-            "e2e": {"value": res["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    rng = np.random.default_rng(7)
+    for _ in range(args.warmup):
+        run.token(rng.standard_normal(DIM).astype(np.float32), rng.standard_normal((LAYERS, EXPERTS)).astype(np.float32))
+    times = [run.token(rng.standard_normal(DIM).astype(np.float32),
+                       rng.standard_normal((LAYERS, EXPERTS)).astype(np.float32))[1] for _ in range(args.steps)]
+    total = sum(times)
+    value = args.steps / total
+    med = statistics.median(times)
+    cpu = {"value": value, "unit": "tok/s", "cores": int(run.cores), "kind": "port",
+           "sample": f"{args.steps} whole config-3 tokens timed, each through 40 layers (after {args.warmup} warm-up "
+                     f"tokens); {med * 1e3:.1f} ms per token median; crosslane's q8k_core.hpp arithmetic vectorised "
+                     f"with AVX2 (bit-identical to it), layer-batched like Lane::experts on {run.cores} host threads"}
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+            "scaling": "strong" if world > 1 and not args.replicas else "weak", "vs_baseline": None,
+            "dtype": "int8xIQ/fp32", "data": "synthetic", "config": config3(args, world, world > 1 and not args.replicas),
+            "impl": "reference", "cpu_baseline": cpu,
+            "repeats": {"runs": args.steps, "unit": "ms per token", "median": round(med * 1e3, 2),
+                        "min": round(min(times) * 1e3, 2), "max": round(max(times) * 1e3, 2)},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -387,7 +439,7 @@ def run_skewed(args, rank, world, local):
     if args.impl == "reference":
         if rank != 0:
             return
-        res = cpu_baseline(samples=max(1, min(args.steps, 3)))
+        res = cpu_baseline(tokens=3)
         if res is None:
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref.so was not built"}))
             return
@@ -516,7 +568,7 @@ def run_skewed(args, rank, world, local):
     achieved = alg_bytes / (ms_per_step / 1e3) / 1e9
     cpu = None
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
-        cpu = cpu_baseline(samples=1)
+        cpu = cpu_baseline(tokens=3)
         if cpu is not None:
             cpu["sample"] += "; the CPU lane decodes the batch token by token (no batched path)"
     line = {
@@ -728,7 +780,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
-        cpu = cpu_baseline(samples=2)
+        cpu = cpu_baseline(tokens=max(3, min(args.steps, 20)))
 
     clk = clocks.summary()
     line = {
@@ -736,15 +788,8 @@ def main():
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
         "scaling": "strong" if sharded else "weak",
         "vs_baseline": None, "dtype": "int8xIQ/fp32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "layers": L, "experts": args.experts, "dim": DIM, "ff": FF, "picks": PICKS,
-                   "types": "IQ2_XXS/IQ2_XS/IQ1_M per (layer, expert), seed-drawn", "batch": 1,
-                   "routing": "top-6 by sigmoid of N(0,1) logits, renormalised",
-                   "parallelism": (f"expert-ID sharded x{world} (peer-store row exchange in the stack kernel)"
-                                   if sharded else f"replica x{world}" if world > 1 else "single GPU"),
-                   "summation": "exact reference order" if args.exact_order
-                   else "segmented rows, fixed-tree partials (run-to-run identical)",
-                   "l2": "inputs larger than L2: each token streams ~2 GB of distinct expert weights",
-                   "bank_gb": round(bank.weight_bytes / 1e9, 2), "fill_s": round(fill_s, 1)},
+        "config": config3(args, world, sharded),
+        "bank": {"gb": round(bank.weight_bytes / 1e9, 2), "fill_s": round(fill_s, 1)},
         "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in e2e.items()},
         "repeats": repeats,
         "roofline": roofline,

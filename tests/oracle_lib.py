@@ -251,6 +251,50 @@ def reference():
     return Reference()
 
 
+LANE_SO = os.path.join(os.path.dirname(REF_SO), "..", "liblane.so")
+
+
+class CpuLane:
+    """The timed CPU expert lane (oracle/liblane.so): crosslane's q8k_core.hpp arithmetic
+    vectorised with AVX2, layer-batched like the reference lane's Lane::experts."""
+
+    def __init__(self):
+        L = C.CDLL(LANE_SO)
+        self.L = L
+        L.lane_dot.restype = C.c_float
+        L.lane_dot.argtypes = [C.c_int, VP, VP, C.c_int]
+        L.lane_quantize.argtypes = [VP, C.c_int, VP]
+        L.lane_experts.restype = C.c_int
+        L.lane_experts.argtypes = [C.c_int, VP, VP, VP, VP, VP, C.c_int, C.c_int, C.c_float, C.c_int, VP]
+        L.lane_team_threads.restype = C.c_int
+        L.lane_team_threads.argtypes = [C.c_int]
+
+    def dot(self, qtype, w_row, q, nb):
+        return self.L.lane_dot(qtype, ptr(w_row), ptr(q), nb)
+
+    def quantize(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros(x.size // 256 * Q8K, np.uint8)
+        self.L.lane_quantize(ptr(x), x.size, ptr(out))
+        return out
+
+    def experts(self, types, gates, ups, downs, x, dim, ff, limit=0.0, threads=0):
+        """y [n][dim] of n experts (ggml AoS matrices) on one x; returns (y, team size)."""
+        n = len(types)
+        t = np.ascontiguousarray(types, np.int32)
+        arr = lambda ms: (C.c_void_p * n)(*[m.ctypes.data for m in ms])
+        g, u, d = arr(gates), arr(ups), arr(downs)
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.zeros((n, dim), np.float32)
+        used = self.L.lane_experts(n, ptr(t), C.cast(g, VP), C.cast(u, VP), C.cast(d, VP), ptr(x), dim, ff, limit,
+                                   threads, ptr(y))
+        return y, used
+
+
+def cpu_lane():
+    return CpuLane() if os.path.exists(LANE_SO) else None
+
+
 def bits(a):
     return np.ascontiguousarray(a, np.float32).view(np.uint32)
 

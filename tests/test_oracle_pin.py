@@ -125,3 +125,56 @@ def test_expert_chain_matches_reference(orc, ref):
         ho, yo = orc.expert(qtype, g, u, d, x, dim, ff, 10.0)
         hr, yr = ref.expert(qtype, g, u, d, x, dim, ff, 10.0, threads=4)
         assert np.array_equal(bits(ho), bits(hr)) and np.array_equal(bits(yo), bits(yr))
+
+
+# ---- the timed CPU lane (oracle/liblane.so, AVX2) against the reference arithmetic ----
+
+@pytest.fixture(scope="module")
+def lane():
+    import oracle_lib
+    cl = oracle_lib.cpu_lane()
+    if cl is None:
+        pytest.skip("oracle/liblane.so not built")
+    return cl
+
+
+@pytest.mark.parametrize("qtype", [16, 17, 29])
+@pytest.mark.parametrize("nb", [1, 6, 28])
+def test_cpu_lane_dot_bitexact_to_reference(orc, ref, lane, qtype, nb):
+    rng = np.random.default_rng(qtype * 31 + nb)
+    bb = {16: 66, 17: 74, 29: 56}[qtype]
+    for trial in range(60):
+        if trial % 2:
+            w = rng.integers(0, 256, bb * nb, dtype=np.uint8)  # arbitrary block bytes
+            if qtype != 29:  # keep the fp16 super-scales finite
+                for b in range(nb):
+                    w[bb * b:bb * b + 2] = np.frombuffer(np.float16(rng.uniform(0.001, 0.1)).tobytes(), np.uint8)
+            else:
+                for b in range(nb):
+                    hbits = int(np.float16(rng.uniform(0.001, 0.1)).view(np.uint16))
+                    for j in range(4):  # super-scale nibbles in the top of the four scale words
+                        w[bb * b + 49 + 2 * j] = (w[bb * b + 49 + 2 * j] & 0x0F) | (((hbits >> (4 * j)) & 15) << 4)
+        else:
+            w = orc.synth_matrix(qtype, trial, 5, trial, trial % 3, 1, 256 * nb)
+        x = (rng.standard_normal(256 * nb) * (1 + trial)).astype(np.float32)
+        if trial % 7 == 0:
+            x = tie_probe(256 * nb)
+        qa = ref.quantize(x)
+        assert np.array_equal(lane.quantize(x), qa)
+        assert bits(lane.dot(qtype, w, qa, nb)) == bits(ref.dot(qtype, w, qa, nb)), trial
+
+
+def test_cpu_lane_layer_batch_bitexact_to_oracle(orc, lane):
+    """A token-layer of 6 experts of mixed types through the batched lane equals the
+    oracle's expert chain bit for bit (rows are independent; only the job order differs)."""
+    dim, ff, seed = 2048, 768, 11
+    types = [16, 17, 29, 16, 29, 17]
+    mats = [[orc.synth_matrix(t, seed, 0, e, r, *((ff, dim) if r < 2 else (dim, ff))) for r in range(3)]
+            for e, t in enumerate(types)]
+    x = np.random.default_rng(3).standard_normal(dim).astype(np.float32)
+    y, used = lane.experts(types, [m[0] for m in mats], [m[1] for m in mats], [m[2] for m in mats], x, dim, ff, 0.0,
+                           threads=4)
+    assert used == 4
+    for e, t in enumerate(types):
+        _, want = orc.expert(t, *mats[e], x, dim, ff)
+        assert np.array_equal(bits(y[e]), bits(want)), e
