@@ -199,6 +199,78 @@ def config3(args, world, sharded):
             "l2": "inputs larger than L2: each token streams ~2 GB of distinct expert weights"}
 
 
+def _all_same(vals, world):
+    """True when every rank holds the same bytes (an all-gather of a digest over the process
+    group); vals: this rank's array."""
+    import hashlib
+    import torch.distributed as dist
+    digest = hashlib.sha256(np.ascontiguousarray(vals).tobytes()).hexdigest()
+    if world == 1:
+        return True
+    out = [None] * world
+    dist.all_gather_object(out, digest)
+    return all(d == out[0] for d in out)
+
+
+def parity_config3(args, rank, world, sharded, bank, local):
+    """Correctness of the benchmarked configuration, checked after the timed region on every
+    rank: (1) a 3-layer exact-order bank of the same weights (expert-ID sharded like the
+    benchmarked one) decodes 2 tokens back to back; the residual stream is identical on every
+    rank and equal bit for bit to the CPU oracle's stack (crosslane's q8k_core.hpp arithmetic
+    and the ascending-id fma combine, runtime.cpp:184-187); (2) the benchmarked fast-order
+    bank's first layer, fed the same input, is within the north-star tolerance of the
+    oracle's layer (relative L2 <= 1e-3, max-abs-relative <= 5e-3); (3) a whole 40-layer
+    fast-order token is identical on every rank."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib
+    import crosslane_b200 as cb
+    orc = oracle_lib.Oracle()
+    rng = np.random.default_rng(4040)  # the same inputs on every rank
+    n_ex = 3
+    x0 = rng.standard_normal(DIM).astype(np.float32)
+    logits = rng.standard_normal((2, args.layers, args.experts)).astype(np.float32)
+    if sharded:
+        from crosslane_b200.sharded import ShardedBank
+        ex = ShardedBank(n_layers=n_ex, n_experts=args.experts, dim=DIM, ff=FF, max_picks=PICKS, device=local,
+                         rank=rank, world=world, exact_order=True)
+    else:
+        ex = cb.ExpertBank(n_layers=n_ex, n_experts=args.experts, dim=DIM, ff=FF, max_picks=PICKS, device=local,
+                           exact_order=True)
+    try:
+        ex.fill_synthetic(SEED, args.policy)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        outs, h = [], x0
+        for t in range(2):
+            h = ex.stack_decode(0, n_ex, h, logits[t, :n_ex])
+            outs.append(h)
+    finally:
+        ex.close()
+    exact_same = _all_same(np.stack(outs), world)
+    exact_bits = None
+    if rank == 0:
+        want, exact_bits = x0, True
+        for t in range(2):
+            want = orc.stack(args.policy, SEED, want, logits[t, :n_ex], DIM, FF, k=PICKS)
+            exact_bits = exact_bits and bool(np.array_equal(oracle_lib.bits(outs[t]), oracle_lib.bits(want)))
+    # fast order (the benchmarked bank): one layer against the oracle, a whole token across ranks
+    one = bank.stack_decode(0, 1, x0, logits[0, :1])
+    full = bank.stack_decode(0, args.layers, x0, logits[0])
+    fast_same = _all_same(np.stack([one, full]), world)
+    rl2 = mar = None
+    if rank == 0:
+        want1 = orc.stack(args.policy, SEED, x0, logits[0, :1], DIM, FF, k=PICKS)
+        rl2, mar = oracle_lib.rel_l2(one, want1), oracle_lib.max_abs_rel(one, want1)
+    ok = None
+    if rank == 0:
+        ok = bool(exact_same and exact_bits and fast_same and rl2 <= 1e-3 and mar <= 5e-3)
+    return {"ok": ok, "ranks": world, "exact_order_layers": n_ex, "exact_order_tokens": 2,
+            "exact_ranks_identical": exact_same, "exact_bitexact_vs_oracle": exact_bits,
+            "fast_layer_rel_l2": rl2, "fast_layer_max_abs_rel": mar, "fast_tolerance": [1e-3, 5e-3],
+            "fast_40_layer_token_ranks_identical": fast_same}
+
+
 def run_reference(args, rank, world):
     """The reference arm: the CPU lane on `steps` whole tokens (each step is timed and is
     one token through the 40-layer stack), after `warmup` untimed tokens."""
@@ -619,6 +691,7 @@ def main():
     ap.add_argument("--experts", type=int, default=EXPERTS,
                     help="experts per layer (profiling captures only: a small bank, same per-token work)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the correctness check after the timed region")
     ap.add_argument("--policy", type=int, default=POLICY, help="quant type policy of the bank (2 = config 3 mix)")
     ap.add_argument("--quick", action="store_true", help="skip the e2e pass and the CPU baseline (tuning sweeps)")
     ap.add_argument("--replicas", action="store_true",
@@ -781,6 +854,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
         cpu = cpu_baseline(tokens=max(3, min(args.steps, 20)))
+    parity = None if args.no_parity else parity_config3(args, rank, world, sharded, bank, local)
 
     clk = clocks.summary()
     line = {
@@ -794,6 +868,7 @@ def main():
         "repeats": repeats,
         "roofline": roofline,
         "cpu_baseline": cpu,
+        "parity": parity,
         "clocks": clk,
         "gpu_launches": 2 * args.steps if bank.persistent else (1 + 3 * L) * args.steps,
     }

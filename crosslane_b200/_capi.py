@@ -78,6 +78,7 @@ SIGNATURES = {
     "clb_bank_load_matrix": (_I, [_P, _U32, _I, _I, _I, _P, _SZ, _PE]),
     "clb_bank_weight_bytes": (C.c_uint64, [_P]),
     "clb_bank_stack_persistent": (_I, [_P]),
+    "clb_bank_set_wait_limit": (_I, [_P, C.c_uint32, _PE]),
     "clb_bank_exchange_handle": (_I, [_P, _P, _PE]),
     "clb_bank_connect": (_I, [_P, _I, _I, _P, _PE]),
     "clb_placement_parse": (_I, [C.c_char_p, _SZ, _I, _I, _P, C.POINTER(C.c_uint64), _PE]),

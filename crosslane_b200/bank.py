@@ -90,6 +90,11 @@ class ExpertBank:
         err = ErrorV1()
         check(lib.clb_bank_load_matrix(self._h, layer, expert, role, qtype, _ptr(buf), buf.nbytes, C.byref(err)), err)
 
+    def set_wait_limit(self, polls: int) -> None:
+        """Polls before a stack kernel's bounded device wait gives up (CLB_E_CUDA, bank poisoned)."""
+        err = ErrorV1()
+        check(lib.clb_bank_set_wait_limit(self._h, polls, C.byref(err)), err)
+
     @property
     def persistent(self) -> bool:
         """Stack decode runs as the persistent kernel (else the per-layer kernels)."""

@@ -177,6 +177,7 @@ struct clb_bank {
     size_t xchg_bytes = 0;
     clb::StackShard shard;
     clb::FlowWork flow;             // workspace of the dataflow stack kernel (fast order)
+    unsigned wait_limit = clb::kDefaultWaitLimit;  // polls before a stack kernel's bounded wait gives up
     std::vector<void*> opened_peers;
     float* d_logits = nullptr;
     int* d_route_ids = nullptr;
@@ -271,7 +272,7 @@ struct clb_bank {
         cuda_check(cudaStreamSynchronize(stream), "stream sync");
         if (flag) {
             cuda_check(cudaMemsetAsync(d_err, 0, sizeof(int), stream), "error flag reset");
-            if (flag == 2) throw Error(CLB_E_CUDA, "grid barrier of the stack kernel timed out");
+            if (flag == 2) throw Error(CLB_E_CUDA, "a bounded wait of the stack kernel ran out (a peer GPU or CTA never posted)");
             if (flag == 3) throw Error(CLB_E_CUDA, "a tensor-core pipeline wait of the prefill kernel timed out");
             throw Error(CLB_E_INVALID, "a picked expert is not resident or has a mismatched shape");
         }
@@ -346,14 +347,15 @@ struct clb_bank {
             cuda_check(clb::launch_route_sigmoid(dlogits, cfg.n_experts, k, nl, d_route_ids, d_route_w, s), "route");
         if (persistent && fast()) {
             cuda_check(clb::launch_flow(d_desc, cfg.n_experts, (int)first, nl, k, d_route_ids, d_route_w, dx, dx,
-                                        cfg.dim, cfg.ff, cfg.limit, flow, d_err, shard, s),
+                                        cfg.dim, cfg.ff, cfg.limit, flow, d_err, wait_limit, shard, s),
                        "dataflow stack kernel");
             shard.epoch += (unsigned)nl;  // layer parity of the row-group counters (every GPU the same)
             return;
         }
         if (persistent) {
             cuda_check(clb::launch_stack(d_desc, cfg.n_experts, (int)first, nl, k, d_route_ids, d_route_w, dx, dx,
-                                         cfg.dim, cfg.ff, cfg.limit, d_gu, d_yrows, d_bar, d_err, fast(), shard, s),
+                                         cfg.dim, cfg.ff, cfg.limit, d_gu, d_yrows, d_bar, d_err, fast(), shard, s,
+                                         wait_limit),
                        "persistent stack kernel");
             if (shard.world > 1) shard.epoch += (unsigned)nl;  // every GPU runs the same launches
             return;
@@ -582,6 +584,14 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
             bank->flow.hq = bank->dev_alloc<int8_t>(k * ff);
             bank->flow.hd = bank->dev_alloc<float>(k * ff / 256);
             bank->flow.cnt = bank->dev_alloc<unsigned>(clb::flow_counter_words(cfg.n_layers, (int)k, (int)ff));
+            const std::vector<uint32_t> sched =
+                clb::flow_schedule_table((int)dim, (int)ff, (int)k, clb::flow_grid(), bank->flow.sched_off);
+            uint32_t* d_sched = bank->dev_alloc<uint32_t>(sched.size());
+            cuda_check(cudaMemcpyAsync(d_sched, sched.data(), sched.size() * sizeof(uint32_t), cudaMemcpyHostToDevice,
+                                       bank->stream),
+                       "round schedule upload");
+            cuda_check(cudaStreamSynchronize(bank->stream), "round schedule upload");
+            bank->flow.sched = d_sched;
         }
         bank->d_ids = bank->dev_alloc<int>(k);
         bank->d_w = bank->dev_alloc<float>(k);
@@ -689,6 +699,15 @@ int32_t clb_bank_contains(const clb_bank* bank, uint32_t layer, int32_t expert) 
 }
 
 int32_t clb_bank_stack_persistent(const clb_bank* bank) { return bank && bank->persistent ? 1 : 0; }
+
+int32_t clb_bank_set_wait_limit(clb_bank* bank, uint32_t polls, clb_error_v1* err) {
+    if (!bank) return fail(err, CLB_E_INVALID, "null bank");
+    std::lock_guard<std::mutex> lock(bank->call_mutex);
+    return guarded(err, [&] {
+        require(polls >= 1, CLB_E_INVALID, "wait limit must be at least one poll");
+        bank->wait_limit = polls;
+    });
+}
 
 int32_t clb_bank_exchange_handle(clb_bank* bank, void* handle_out, clb_error_v1* err) {
     if (!bank || !handle_out) return fail(err, CLB_E_INVALID, "null bank/handle");

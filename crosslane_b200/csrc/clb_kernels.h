@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 #include "clb_types.h"
 
 namespace clb {
@@ -89,6 +91,7 @@ cudaError_t launch_stack_batch(const ExpertDesc* desc, int E, int nl, const floa
 
 // persistent whole-stack kernel (clb_stack.cu)
 constexpr int kMaxPeers = 8;  // GPUs of one node
+constexpr unsigned kDefaultWaitLimit = 1u << 22;  // polls of a bounded device wait (a few seconds)
 // Expert-ID sharding of the stack over `world` GPUs: this GPU holds experts [own_begin,
 // own_end) of every layer and computes only those picks; the expert rows of every layer
 // go to all GPUs through peer stores into double-buffered slots (yx: [2][k][dim] floats,
@@ -109,12 +112,18 @@ size_t stack_smem(int dim, int ff, int k, bool fast);
 bool stack_supported(int dim, int ff, int k, bool fast);
 cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
                          const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit, float* gu,
-                         float* yrows, unsigned* bar, int* err, bool fast, const StackShard& shard, cudaStream_t s);
+                         float* yrows, unsigned* bar, int* err, bool fast, const StackShard& shard, cudaStream_t s,
+                         unsigned wait_limit = 1u << 22);
 
 // Dataflow whole-stack kernel (clb_flow.cu), fast summation order. Workspace:
 //   hbuf [2][dim] residual stream between layers, ssbuf [2][dim / 32] sums of squares per
 //   32-row group, gu [k][ff] SwiGLU outputs, hq [k][ff] + hd [k][ff / 256] their Q8_K,
 //   cnt: flow_counter_words(nl_max, k, ff) counters, zeroed by launch_flow before each launch.
+// sched: the round schedules of every pick count (flow_schedule_table), sched_off their
+// offsets. FlowShape: a layer's round shapes (clb_flow.cu).
+struct FlowShape {
+    int rgr, sg, ppr, sd, ngu, nd;
+};
 struct FlowWork {
     float* hbuf = nullptr;
     float* ssbuf = nullptr;
@@ -122,12 +131,17 @@ struct FlowWork {
     int8_t* hq = nullptr;
     float* hd = nullptr;
     unsigned* cnt = nullptr;
+    const uint32_t* sched = nullptr;
+    uint32_t sched_off[kMaxPicks + 2] = {};
 };
 size_t flow_counter_words(int nl_max, int k, int ff);
+int flow_grid();
+// Round schedules for pick counts 0..k on `grid` CTAs; offsets[0..k+1] into the table.
+std::vector<uint32_t> flow_schedule_table(int dim, int ff, int k, int grid, uint32_t* offsets);
 size_t flow_smem(int dim, int ff, int k);
 bool flow_supported(int dim, int ff, int k);
 cudaError_t launch_flow(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
                         const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit,
-                        const FlowWork& w, int* err, const StackShard& shard, cudaStream_t s);
+                        const FlowWork& w, int* err, unsigned wait_limit, const StackShard& shard, cudaStream_t s);
 
 }  // namespace clb

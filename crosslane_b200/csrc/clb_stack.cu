@@ -22,19 +22,18 @@ namespace clb {
 
 namespace {
 
-constexpr unsigned kBarrierSpinLimit = 1u << 22;  // a few seconds of polling before giving up
 constexpr int kErrBarrier = 2;                     // err flag value of a timed-out barrier
 
 // Grid-wide barrier over gridDim.x co-resident CTAs (cooperative launch) on a counter
 // that only grows: barrier number e (1, 2, ...) is passed once the counter reaches
 // e * gridDim.x. Thread 0 of each CTA arrives with a release add (the CTA's writes,
 // ordered before it by the preceding __syncthreads, become visible first) and polls
-// with acquire loads. Bounded: after kBarrierSpinLimit polls the CTA sets *err and
+// with acquire loads. Bounded: after `limit` polls the CTA sets *err and
 // every thread of it gets false, so the kernel can return instead of hanging.
 // `overlap` runs on the threads other than thread 0 while thread 0 waits (work that needs
 // no other CTA's results, e.g. staging the next layer's routing).
 template <class F>
-__device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err, F&& overlap) {
+__device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err, unsigned limit, F&& overlap) {
     __syncthreads();
     int ok = 1;
     if (threadIdx.x != 0) overlap();
@@ -45,7 +44,7 @@ __device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err, F&& over
         while (true) {
             asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(count) : "memory");
             if ((int)(v - target) >= 0) break;
-            if (++spins > kBarrierSpinLimit) {
+            if (++spins > limit) {
                 atomicExch(err, kErrBarrier);
                 ok = 0;
                 break;
@@ -54,8 +53,8 @@ __device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err, F&& over
     }
     return __syncthreads_and(ok) != 0;
 }
-__device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err) {
-    return grid_barrier(count, epoch, err, [] {});
+__device__ bool grid_barrier(unsigned* count, unsigned epoch, int* err, unsigned limit) {
+    return grid_barrier(count, epoch, err, limit, [] {});
 }
 
 // At the end of a layer's down phase every CTA tells every peer that its part of this GPU's
@@ -75,7 +74,7 @@ __device__ void signal_peers(const StackShard& sh) {
 // signalled their rows of this layer (signal_peers). Flags only grow, by gridDim.x per layer
 // (every GPU runs the same grid): layer li of the launch with `epoch` layers before it is
 // complete at (epoch + li + 1) * gridDim.x, compared modulo 2^32. Bounded like grid_barrier.
-__device__ bool exchange_rows(const StackShard& sh, int li, int* err) {
+__device__ bool exchange_rows(const StackShard& sh, int li, int* err, unsigned limit) {
     int ok = 1;
     if (threadIdx.x == 0) {
         const unsigned target = (sh.epoch + (unsigned)li + 1u) * gridDim.x;
@@ -85,7 +84,7 @@ __device__ bool exchange_rows(const StackShard& sh, int li, int* err) {
             while (true) {
                 asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(sh.flags + r) : "memory");
                 if ((int)(v - target) >= 0) break;
-                if (++spins > kBarrierSpinLimit) {
+                if (++spins > limit) {
                     atomicExch(err, kErrBarrier);
                     ok = 0;
                     break;
@@ -145,6 +144,7 @@ struct StackParams {
     float* yrows;            // [k][dim]
     unsigned* bar;           // grid barrier counter, zero before the launch
     int* err;
+    unsigned wait_limit;     // polls before a bounded wait gives up
     const uint32_t* tables;  // compact selector tables (kTableWords)
     StackShard sh;           // expert-ID sharding over GPUs (world == 1: none)
 };
@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                 }
                 __syncthreads();
             }
-            if (!grid_barrier(P.bar, 2 * li + 1, P.err)) return;
+            if (!grid_barrier(P.bar, 2 * li + 1, P.err, P.wait_limit)) return;
 
             // 3. Q8_K(h) of every pick, then the down rows: a CTA round covers 16 / SD
             //    (pick, 32-row group) pairs, each split into SD K segments (one warp each)
@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                 else if (lane == 0) atomicExch(P.err, 1);
                 if (lane % 4 == 0) P.gu[((size_t)pick * 2 + mat) * ff + row] = y;
             }
-            if (!grid_barrier(P.bar, 2 * li + 1, P.err)) return;
+            if (!grid_barrier(P.bar, 2 * li + 1, P.err, P.wait_limit)) return;
 
             // 3. SwiGLU of this CTA's pick over all threads, Q8_K(h) per 256-block, then the
             //    pick's down rows (one thread per row, the reference's lane chains) -> yrows
@@ -512,8 +512,8 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             }
         }
         if (MULTI && sh.world > 1) signal_peers(sh);  // this CTA's peer stores, then one release per peer
-        if (!grid_barrier(P.bar, 2 * li + 2, P.err, stage_next)) return;
-        if (MULTI && sh.world > 1 && !exchange_rows(sh, li, P.err)) return;
+        if (!grid_barrier(P.bar, 2 * li + 2, P.err, P.wait_limit, stage_next)) return;
+        if (MULTI && sh.world > 1 && !exchange_rows(sh, li, P.err, P.wait_limit)) return;
     }
     // h after the last layer: each CTA writes its slice
     const int per = (dim + G - 1) / G;
@@ -544,7 +544,8 @@ bool stack_supported(int dim, int ff, int k, bool fast) {
 
 cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
                          const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit, float* gu,
-                         float* yrows, unsigned* bar, int* err, bool fast, const StackShard& shard, cudaStream_t s) {
+                         float* yrows, unsigned* bar, int* err, bool fast, const StackShard& shard, cudaStream_t s,
+                         unsigned wait_limit) {
     const uint32_t* tables = nullptr;
     cudaError_t e = tables_device_ptr(&tables);
     if (e != cudaSuccess) return e;
@@ -566,6 +567,7 @@ cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k
     P.yrows = yrows;
     P.bar = bar;
     P.err = err;
+    P.wait_limit = wait_limit;
     P.tables = tables;
     P.sh = shard;
     const int nt = stack_threads(fast);

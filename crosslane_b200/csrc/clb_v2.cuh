@@ -369,9 +369,11 @@ __device__ __forceinline__ void load_raw_at(const uint8_t* p, size_t pstride, co
 }
 
 // Partial of one row over blocks [b0, b1): 0.125 * sum_b (d_w * d_x)_b * M_b with M_b =
-// block_sum8 (for IQ1_M the 8q + delta integer), blocks in order, fp32. The next block's
-// bytes are loaded into registers while the current one is decoded. AS: byte stride of
-// the activation blocks (kActStride in shared memory, 256 for a Q8_K row in global memory).
+// block_sum8 (for IQ1_M the 8q + delta integer), blocks in order, fp32. The next block is
+// prefetched into L2 while the current one is decoded. (A register double buffer decodes
+// ~10 % faster in isolation, but at ~127 registers it pushes every function of the
+// dataflow kernel's call graph into local-memory spills, which the weight stream evicts to
+// DRAM.) AS: byte stride of the activation blocks (kActStride in shared memory).
 template <int T, int AS = kActStride>
 __device__ __noinline__ float lane_row_db(const PackedMat& m, int row, int b0, int b1, const int8_t* act_qs,
                                           const float* act_d) {
@@ -391,20 +393,18 @@ __device__ __noinline__ float lane_row_db(const PackedMat& m, int row, int b0, i
         if (T != CLB_IQ2_XXS) sc += n * 8;
         if (T != CLB_IQ1_M) dp += n;
     };
-    RowRaw ra, rb;
-    if (b0 < b1) load_raw_at<T>(p, pstride, sc, dp, ra);
-    for (int b = b0; b < b1; b += 2) {
+    for (int b = b0; b < b1; ++b) {
         if (b + 1 < b1) {
-            advance();
-            load_raw_at<T>(p, pstride, sc, dp, rb);
+            const uint8_t* q = p + bstride;
+            prefetch_l2(q);
+            prefetch_l2(q + pstride);
+            prefetch_l2(q + 2 * pstride);
+            if (T != CLB_IQ1_M) prefetch_l2(q + 3 * pstride);
         }
-        step(ra, b);
-        if (b + 1 >= b1) break;
-        if (b + 2 < b1) {
-            advance();
-            load_raw_at<T>(p, pstride, sc, dp, ra);
-        }
-        step(rb, b + 1);
+        RowRaw r;
+        load_raw_at<T>(p, pstride, sc, dp, r);
+        step(r, b);
+        advance();
     }
     return __fmul_rn(0.125f, acc);
 }

@@ -217,6 +217,13 @@ uint64_t clb_bank_weight_bytes(const clb_bank* bank);
  * (CLB_BANK_PER_LAYER_KERNELS, or a geometry / device the persistent kernel cannot hold). */
 int32_t clb_bank_stack_persistent(const clb_bank* bank);
 
+/* Polls a stack kernel's bounded waits (layer barrier, a down round's inputs, the expert
+ * rows of peer GPUs) make before giving up; default 2^22 (a few seconds). When a wait runs
+ * out the kernel returns, the call fails with CLB_E_CUDA and the bank is poisoned (later
+ * calls: CLB_E_STATE) -- e.g. when a peer GPU of a sharded bank never runs its share.
+ * No counterpart in crosslane (its lanes are host threads joined on the host). */
+int32_t clb_bank_set_wait_limit(clb_bank* bank, uint32_t polls, clb_error_v1* err);
+
 /* ---- expert-ID sharding over the GPUs of one node (one process or thread per GPU) ----
  * Each GPU's bank owns experts [expert_begin, expert_end) of every layer (contiguous
  * blocks, together covering all experts). In clb_stack_decode* every GPU routes the same
