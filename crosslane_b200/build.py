@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libcrosslane_b200.so")
-SOURCES = ["clb_kernels.cu", "clb_bank.cu", "clb_noalloc.cu", "clb_stack.cu", "clb_flow.cu", "clb_prefill.cu",
+SOURCES = ["clb_kernels.cu", "clb_bank.cu", "clb_noalloc.cu", "clb_stack.cu", "clb_prefill.cu",
            "clb_pack_io.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

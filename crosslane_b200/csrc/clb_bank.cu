@@ -176,7 +176,7 @@ struct clb_bank {
     uint8_t* d_xchg = nullptr;
     size_t xchg_bytes = 0;
     clb::StackShard shard;
-    clb::FlowWork flow;             // workspace of the dataflow stack kernel (fast order)
+    clb::StackWork stk;             // fast-order workspace of the persistent stack kernel
     unsigned wait_limit = clb::kDefaultWaitLimit;  // polls before a stack kernel's bounded wait gives up
     std::vector<void*> opened_peers;
     float* d_logits = nullptr;
@@ -345,19 +345,14 @@ struct clb_bank {
         const int k = cfg.max_picks;
         if (dlogits)
             cuda_check(clb::launch_route_sigmoid(dlogits, cfg.n_experts, k, nl, d_route_ids, d_route_w, s), "route");
-        if (persistent && fast()) {
-            cuda_check(clb::launch_flow(d_desc, cfg.n_experts, (int)first, nl, k, d_route_ids, d_route_w, dx, dx,
-                                        cfg.dim, cfg.ff, cfg.limit, flow, d_err, wait_limit, shard, s),
-                       "dataflow stack kernel");
-            shard.epoch += (unsigned)nl;  // layer parity of the row-group counters (every GPU the same)
-            return;
-        }
         if (persistent) {
             cuda_check(clb::launch_stack(d_desc, cfg.n_experts, (int)first, nl, k, d_route_ids, d_route_w, dx, dx,
                                          cfg.dim, cfg.ff, cfg.limit, d_gu, d_yrows, d_bar, d_err, fast(), shard, s,
-                                         wait_limit),
+                                         wait_limit, stk),
                        "persistent stack kernel");
-            if (shard.world > 1) shard.epoch += (unsigned)nl;  // every GPU runs the same launches
+            // layers run through the kernel: the parity and targets of the monotonic row-group
+            // counters and exchange flags (every GPU runs the same launches)
+            shard.epoch += (unsigned)nl;
             return;
         }
         for (int i = 0; i < nl; ++i)
@@ -575,23 +570,13 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         bank->shard.flags = reinterpret_cast<unsigned*>(bank->d_xchg + 2 * k * dim * sizeof(float));
         bank->shard.rgcnt = bank->shard.flags + clb::kMaxPeers;
         bank->persistent = (cfg.flags & CLB_BANK_PER_LAYER_KERNELS) == 0 &&
-                           (bank->fast() ? clb::flow_supported(cfg.dim, cfg.ff, cfg.max_picks)
-                                         : clb::stack_supported(cfg.dim, cfg.ff, cfg.max_picks, false));
+                           clb::stack_supported(cfg.dim, cfg.ff, cfg.max_picks, bank->fast());
         if (bank->persistent && bank->fast()) {
-            bank->flow.hbuf = bank->dev_alloc<float>(2 * dim);
-            bank->flow.ssbuf = bank->dev_alloc<float>(2 * (dim / 32));
-            bank->flow.gu = bank->d_gu;
-            bank->flow.hq = bank->dev_alloc<int8_t>(k * ff);
-            bank->flow.hd = bank->dev_alloc<float>(k * ff / 256);
-            bank->flow.cnt = bank->dev_alloc<unsigned>(clb::flow_counter_words(cfg.n_layers, (int)k, (int)ff));
-            const std::vector<uint32_t> sched =
-                clb::flow_schedule_table((int)dim, (int)ff, (int)k, clb::flow_grid(), bank->flow.sched_off);
-            uint32_t* d_sched = bank->dev_alloc<uint32_t>(sched.size());
-            cuda_check(cudaMemcpyAsync(d_sched, sched.data(), sched.size() * sizeof(uint32_t), cudaMemcpyHostToDevice,
-                                       bank->stream),
-                       "round schedule upload");
-            cuda_check(cudaStreamSynchronize(bank->stream), "round schedule upload");
-            bank->flow.sched = d_sched;
+            bank->stk.hbuf = bank->dev_alloc<float>(2 * dim);
+            bank->stk.ssbuf = bank->dev_alloc<float>(2 * (dim / 32));
+            bank->stk.hq = bank->dev_alloc<int8_t>(k * ff);
+            bank->stk.hd = bank->dev_alloc<float>(k * ff / 256);
+            bank->stk.blk = bank->dev_alloc<unsigned>(clb::stack_block_words(cfg.n_layers, (int)k, (int)ff));
         }
         bank->d_ids = bank->dev_alloc<int>(k);
         bank->d_w = bank->dev_alloc<float>(k);

@@ -96,8 +96,8 @@ constexpr unsigned kDefaultWaitLimit = 1u << 22;  // polls of a bounded device w
 // own_end) of every layer and computes only those picks; the expert rows of every layer
 // go to all GPUs through peer stores into double-buffered slots (yx: [2][k][dim] floats,
 // then `flags`: one counter per source GPU). world == 1: no sharding.
-// The dataflow kernel (clb_flow.cu) also keeps per-row-group completion counters there
-// (rgcnt: [2][dim / 32], one set per layer parity), which every GPU increments.
+// The fast order also keeps per-row-group completion counters there (rgcnt: [2][dim / 32],
+// one set per layer parity), which every GPU increments.
 struct StackShard {
     int world = 1, rank = 0, own_begin = 0, own_end = 0x7fffffff;
     unsigned epoch = 0;               // layers this bank has run through a stack kernel before this launch
@@ -108,40 +108,23 @@ struct StackShard {
     unsigned* peer_flags[kMaxPeers] = {};
     unsigned* peer_rgcnt[kMaxPeers] = {};
 };
+// Fast-order workspace of the persistent kernel: hbuf [2][dim] h between layers, ssbuf
+// [2][dim / 32] its per-32-row-group sums of squares, hq [k][ff] + hd [k][ff / 256] the
+// picks' Q8_K(h) (quantized once per block), blk: stack_block_words(nl_max, k, ff) block
+// counters, zeroed by launch_stack. The row-group counters live in StackShard::rgcnt.
+struct StackWork {
+    float* hbuf = nullptr;
+    float* ssbuf = nullptr;
+    int8_t* hq = nullptr;
+    float* hd = nullptr;
+    unsigned* blk = nullptr;
+};
+size_t stack_block_words(int nl_max, int k, int ff);
 size_t stack_smem(int dim, int ff, int k, bool fast);
 bool stack_supported(int dim, int ff, int k, bool fast);
 cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
                          const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit, float* gu,
                          float* yrows, unsigned* bar, int* err, bool fast, const StackShard& shard, cudaStream_t s,
-                         unsigned wait_limit = 1u << 22);
-
-// Dataflow whole-stack kernel (clb_flow.cu), fast summation order. Workspace:
-//   hbuf [2][dim] residual stream between layers, ssbuf [2][dim / 32] sums of squares per
-//   32-row group, gu [k][ff] SwiGLU outputs, hq [k][ff] + hd [k][ff / 256] their Q8_K,
-//   cnt: flow_counter_words(nl_max, k, ff) counters, zeroed by launch_flow before each launch.
-// sched: the round schedules of every pick count (flow_schedule_table), sched_off their
-// offsets. FlowShape: a layer's round shapes (clb_flow.cu).
-struct FlowShape {
-    int rgr, sg, ppr, sd, ngu, nd;
-};
-struct FlowWork {
-    float* hbuf = nullptr;
-    float* ssbuf = nullptr;
-    float* gu = nullptr;
-    int8_t* hq = nullptr;
-    float* hd = nullptr;
-    unsigned* cnt = nullptr;
-    const uint32_t* sched = nullptr;
-    uint32_t sched_off[kMaxPicks + 2] = {};
-};
-size_t flow_counter_words(int nl_max, int k, int ff);
-int flow_grid();
-// Round schedules for pick counts 0..k on `grid` CTAs; offsets[0..k+1] into the table.
-std::vector<uint32_t> flow_schedule_table(int dim, int ff, int k, int grid, uint32_t* offsets);
-size_t flow_smem(int dim, int ff, int k);
-bool flow_supported(int dim, int ff, int k);
-cudaError_t launch_flow(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
-                        const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit,
-                        const FlowWork& w, int* err, unsigned wait_limit, const StackShard& shard, cudaStream_t s);
+                         unsigned wait_limit, const StackWork& w);
 
 }  // namespace clb

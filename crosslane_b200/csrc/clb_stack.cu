@@ -1,28 +1,61 @@
-// Persistent whole-stack decode kernel: one CTA per SM runs every layer of a token,
-// with two grid barriers per layer, so the tables are staged once per token and no
-// kernel launch or prologue sits between the phases.
+// Persistent whole-stack decode kernel: one CTA per SM runs every layer of a token, so
+// the tables are staged once per token and no kernel launch or prologue sits between the
+// phases.
 //
-// Per layer l (ids/w = the routing of layer l, fixed before the launch):
-//   1. every CTA: h += ascending-id fma combine of the previous layer's expert rows
-//      (runtime.cpp:184-187), x = RMSNorm(h), Q8_K(x) into shared memory (all CTAs
-//      compute the same bits: fixed-order fp64 sum of squares, as k_norm_quant);
-//   2. gate/up rows of every pick, spread over all warps of the grid -> gu (global);
+// Fast summation order, per layer l (ids/w = the routing of layer l, fixed before the
+// launch), one grid barrier per layer:
+//   1. every CTA: h (h_in, or the previous layer's combine in global memory) and its
+//      per-32-row-group sums of squares; x = RMSNorm(h) (fixed-order total), Q8_K(x) into
+//      shared memory;
+//   2. gate/up rows of every pick in CTA rounds (K segments per warp, added in order),
+//      SwiGLU -> gu; each 32-row group counts its 256-row block, and the CTA that completes
+//      a block quantizes it once to Q8_K(h) in global memory and marks it ready;
+//   3. each CTA waits for (only) the blocks of the picks its down rounds touch, copies
+//      them into shared memory and decodes its down rounds -> expert rows (also into every
+//      peer's slot of a sharded bank); each row group counts its rows;
+//   4. the owner warp of each 32-row group waits for the rows of all k picks and applies
+//      h += the ascending-id fma combine (runtime.cpp:184-187), writing h and its sum of
+//      squares for the next layer (the last layer: h_out);
 //   -- grid barrier --
+// Exact order (q8k_core's arithmetic, bit-identical to the CPU lane), per layer:
+//   1. every CTA: h += ascending-id fma combine of the previous layer's expert rows,
+//      x = RMSNorm(h) (fixed-order fp64 sum of squares, as k_norm_quant), Q8_K(x);
+//   2. gate/up rows of every pick (4 threads per row) -> gu;   -- grid barrier --
 //   3. every CTA serves one pick in the down phase: SwiGLU + Q8_K(h) of that pick into
-//      shared memory, then its share of the pick's down rows -> yrows (global);
-//   -- grid barrier --
+//      shared memory, then its share of the pick's down rows -> yrows;   -- grid barrier --
 // After the last layer the combine is applied once more and written to h_out.
 #include <cuda_runtime.h>
 
 #include "clb_device.cuh"
 #include "clb_kernels.h"
+#include "clb_sync.cuh"
 #include "clb_v2.cuh"
 
 namespace clb {
 
+#ifdef CLB_FLOW_TRACE
+// Phase stamps of the lockstep kernel per (layer, CTA), a build-time option (%globaltimer
+// ns): 0 layer start, 1 combine done, 2 norm done, 3 gate/up rounds done, 4 first barrier
+// passed, 5 Q8_K(h) staged, 6 down rounds done, 7 second barrier passed.
+constexpr int kStTraceLayers = 64, kStTraceCtas = 160, kStTraceSlots = 8;
+__device__ unsigned long long g_stack_trace[kStTraceLayers * kStTraceCtas * kStTraceSlots];
+__device__ __forceinline__ void stack_stamp(int li, int slot) {
+    if (threadIdx.x == 0 && li < kStTraceLayers && blockIdx.x < kStTraceCtas) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        g_stack_trace[(li * kStTraceCtas + blockIdx.x) * kStTraceSlots + slot] = t;
+    }
+}
+#define STACK_STAMP(li, slot) stack_stamp((li), (slot))
+#else
+#define STACK_STAMP(li, slot) do { } while (0)
+#endif
+
+
 namespace {
 
-constexpr int kErrBarrier = 2;                     // err flag value of a timed-out barrier
+constexpr int kErrBarrier = 2;                     // err flag value of a timed-out barrier or wait
+constexpr unsigned kBlockReady = 9;                 // block counter: 8 row groups done + quantized
 
 // Grid-wide barrier over gridDim.x co-resident CTAs (cooperative launch) on a counter
 // that only grows: barrier number e (1, 2, ...) is passed once the counter reaches
@@ -147,6 +180,7 @@ struct StackParams {
     unsigned wait_limit;     // polls before a bounded wait gives up
     const uint32_t* tables;  // compact selector tables (kTableWords)
     StackShard sh;           // expert-ID sharding over GPUs (world == 1: none)
+    StackWork w;             // fast order: h between layers, Q8_K(h), block counters
 };
 
 // Shared memory carve-up (bytes), shared by the kernel and the host size query.
@@ -243,7 +277,22 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
         if (lane < k) sord[sl * kMaxPicks + rank] = lane;
         const bool mine = lane < k && e >= sh.own_begin && e < sh.own_end;
         const uint32_t m = __ballot_sync(0xffffffffu, mine);
-        if (mine) sown[sl * (kMaxPicks + 1) + __popc(m & ((1u << lane) - 1u))] = lane;
+        if (FAST) {
+            // the picks computed here ordered by decode speed (IQ2_XXS, IQ2_XS, IQ1_M; pick
+            // order within a type): the rounds are pick-major, so the slowest picks' gate/up
+            // rounds feed the later down rounds. The order decides only which CTA computes
+            // what, not any sum.
+            int key = 0x7fffffff;
+            if (mine) {
+                const int t = __ldcg(&P.desc[(size_t)(P.first + lj) * P.E + e].gate.type);
+                key = (t == CLB_IQ2_XXS ? 0 : t == CLB_IQ2_XS ? 1 : 2) * 32 + lane;
+            }
+            int pos = 0;
+            for (int p = 0; p < k; ++p) pos += __shfl_sync(0xffffffffu, key, p) < key;
+            if (mine) sown[sl * (kMaxPicks + 1) + pos] = lane;
+        } else if (mine) {
+            sown[sl * (kMaxPicks + 1) + __popc(m & ((1u << lane) - 1u))] = lane;
+        }
         if (lane == 0) sown[sl * (kMaxPicks + 1) + kMaxPicks] = __popc(m);
         __syncwarp();
         constexpr int words = (int)(sizeof(ExpertDesc) / 4);
@@ -264,10 +313,11 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             if (li + 1 < P.nl) load_routing(li + 1);
         };
 
-        // 1. h += combine of the previous layer (ascending expert id), in every CTA: four
-        //    rows per thread and two such quads at a time, the rows of up to 3 picks of both
-        //    loaded before the fma chains
-        if (li > 0) {
+        STACK_STAMP(li, 0);
+        // 1. (exact) h += combine of the previous layer (ascending expert id), in every CTA:
+        //    four rows per thread and two such quads at a time, the rows of up to 3 picks of
+        //    both loaded before the fma chains
+        if (!FAST && li > 0) {
             const float* yr = ybuf(li - 1);
             const int nq = dim >> 2;
             for (int q0 = tid; q0 < nq; q0 += 2 * NT) {
@@ -316,6 +366,12 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             __syncthreads();
         }
         if (li == P.nl) break;
+        if (FAST && li > 0) {  // h as the previous layer's owner warps combined it
+            const float4* src = reinterpret_cast<const float4*>(P.w.hbuf + (size_t)(li & 1) * dim);
+            for (int i = tid; i < (dim >> 2); i += NT) reinterpret_cast<float4*>(hs)[i] = __ldcg(src + i);
+            __syncthreads();
+        }
+        STACK_STAMP(li, 1);
 
         // x = RMSNorm(h), Q8_K(x). Exact order: lane t of 1024 sums h[t + 1024 j]^2 in j
         // order in fp64, then a binary tree over the lanes (k_norm_quant's order; with 512
@@ -323,14 +379,25 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
         // fp32 fma chains per thread, butterfly sums in each warp, then over the warps; every
         // CTA evaluates the same expression, so all get the same scale.
         if (FAST) {
-            float s = 0.0f;
-            for (int i = tid; i < dim; i += NT) s = __fmaf_rn(hs[i], hs[i], s);
+            // per 32-row group sums of squares (layer 0 from h; later layers as the owner
+            // warps wrote them, the same expression), then a fixed-order total that every
+            // warp of every CTA evaluates identically
+            float* ssp = reinterpret_cast<float*>(tree);
+            const int nrg = dim >> 5;
+            if (li == 0) {
+                for (int rg = warp; rg < nrg; rg += NW) {
+                    const float v = hs[rg * 32 + lane];
+                    float s = __fmul_rn(v, v);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-            float* red = reinterpret_cast<float*>(tree);
-            if (lane == 0) red[warp] = s;
+                    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+                    if (lane == 0) ssp[rg] = s;
+                }
+            } else {
+                for (int rg = tid; rg < nrg; rg += NT) ssp[rg] = __ldcg(P.w.ssbuf + (size_t)(li & 1) * nrg + rg);
+            }
             __syncthreads();
-            float t = lane < NW ? red[lane] : 0.0f;
+            float t = 0.0f;
+            for (int i = lane; i < nrg; i += 32) t = __fadd_rn(t, ssp[i]);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, o));
             const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)dim), 1e-6f)));
@@ -367,6 +434,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
         }
         __syncthreads();
 
+        STACK_STAMP(li, 2);
         if (FAST) {
             // 2. gate/up, one row per lane: a CTA round covers 8 / SG row groups of 32 rows of
             //    both matrices, each split into SG K segments (one warp each); the segments
@@ -382,7 +450,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                 if (rg < nrg) {
                     const int pick = own[rg / rgpp], row = (rg % rgpp) * 32 + lane;
                     const PackedMat& m = mat ? dl[pick].up : dl[pick].gate;
-                    if (m.body != nullptr && m.k == dim && m.n == ff) y = lane_row_partial_any(m, row, b0, b1, xq, xd);
+                    if (m.body != nullptr && m.k == dim && m.n == ff) y = lane_row_db_any(m, row, b0, b1, xq, xd);
                     else if (lane == 0) atomicExch(P.err, 1);
                 }
                 part[warp * 32 + lane] = y;
@@ -395,12 +463,30 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                             g = __fadd_rn(g, part[((r2 * 2 + 0) * SG + s2) * 32 + lane]);
                             u = __fadd_rn(u, part[((r2 * 2 + 1) * SG + s2) * 32 + lane]);
                         }
-                        P.gu[(size_t)own[rg2 / rgpp] * ff + (rg2 % rgpp) * 32 + lane] = swiglu(g, u, P.limit);
+                        const int slot = own[rg2 / rgpp], rgi = rg2 % rgpp, hb = rgi >> 3;
+                        P.gu[(size_t)slot * ff + rgi * 32 + lane] = swiglu(g, u, P.limit);
+                        // count the 256-row block; the 8th row group quantizes it once for all CTAs
+                        __syncwarp();
+                        unsigned* bc = P.w.blk + ((size_t)li * k + slot) * nbh + hb;
+                        unsigned old = 0;
+                        if (lane == 0) old = atom_add_acq_rel_gpu(bc, 1u);
+                        old = __shfl_sync(0xffffffffu, old, 0);
+                        if (old == 7u) {
+                            const float4* src =
+                                reinterpret_cast<const float4*>(P.gu + (size_t)slot * ff + (size_t)hb * 256 + lane * 8);
+                            const float4 lo = __ldcg(src), hi = __ldcg(src + 1);
+                            float v8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+                            warp_quant_regs(v8, P.w.hq + (size_t)slot * ff + (size_t)hb * 256,
+                                            P.w.hd + (size_t)slot * nbh + hb);
+                            __syncwarp();
+                            if (lane == 0) red_release_gpu(bc, 1u);  // -> kBlockReady
+                        }
                     }
                 }
                 __syncthreads();
             }
-            if (!grid_barrier(P.bar, 2 * li + 1, P.err, P.wait_limit)) return;
+            STACK_STAMP(li, 3);
+            STACK_STAMP(li, 4);
 
             // 3. Q8_K(h) of every pick, then the down rows: a CTA round covers 16 / SD
             //    (pick, 32-row group) pairs, each split into SD K segments (one warp each)
@@ -409,29 +495,32 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             for (int q = blockIdx.x; q * PPR < npair; q += G)
                 for (int j = 0; j < PPR && q * PPR + j < npair; ++j) need |= 1u << own[(q * PPR + j) / rgd];
             const int nneed = __popc(need);
-            for (int w0 = warp; w0 < nneed * nbh; w0 += 3 * NW) {  // up to 3 blocks per warp in flight
-                float v[3][8];
-                int hbs[3];
-#pragma unroll
-                for (int j = 0; j < 3; ++j) {
-                    hbs[j] = -1;
-                    const int wi = w0 + j * NW;
-                    if (wi < nneed * nbh) {
-                        const int nth = wi / nbh;  // nth set bit of `need`
-                        uint32_t m = need;
-                        for (int c = 0; c < nth; ++c) m &= m - 1;
-                        hbs[j] = (__ffs(m) - 1) * nbh + wi % nbh;
-                        const float4* src = reinterpret_cast<const float4*>(P.gu + (size_t)hbs[j] * 256 + lane * 8);
-                        const float4 lo = __ldcg(src), hi = __ldcg(src + 1);
-                        v[j][0] = lo.x, v[j][1] = lo.y, v[j][2] = lo.z, v[j][3] = lo.w;
-                        v[j][4] = hi.x, v[j][5] = hi.y, v[j][6] = hi.z, v[j][7] = hi.w;
+            {  // Q8_K(h) of those picks: wait until each block is ready (quantized by the CTA
+               // that completed it), copy it into shared memory
+                int ok = 1;
+                for (int wi = warp; wi < nneed * nbh; wi += NW) {
+                    const int nth = wi / nbh, b = wi - nth * nbh;  // block b of the nth set bit of `need`
+                    uint32_t m = need;
+                    for (int c = 0; c < nth; ++c) m &= m - 1;
+                    const int slot = __ffs(m) - 1;
+                    int got = 1;
+                    if (lane == 0)
+                        got = wait_reached<false>(P.w.blk + ((size_t)li * k + slot) * nbh + b, kBlockReady, P.err,
+                                                  P.wait_limit, kErrBarrier)
+                                  ? 1
+                                  : 0;
+                    if (!__shfl_sync(0xffffffffu, got, 0)) {
+                        ok = 0;
+                        break;
                     }
+                    if (lane < 16)
+                        *reinterpret_cast<uint4*>(hq + ((size_t)slot * nbh + b) * kActStride + lane * 16) =
+                            __ldcg(reinterpret_cast<const uint4*>(P.w.hq + (size_t)slot * ff + (size_t)b * 256) + lane);
+                    if (lane == 0) hd[slot * nbh + b] = __ldcg(P.w.hd + (size_t)slot * nbh + b);
                 }
-#pragma unroll
-                for (int j = 0; j < 3; ++j)
-                    if (hbs[j] >= 0) warp_quant_regs(v[j], hq + (size_t)hbs[j] * kActStride, hd + hbs[j]);
+                if (!__syncthreads_and(ok)) return;
             }
-            __syncthreads();
+            STACK_STAMP(li, 5);
             const int slot = warp / SD, dseg = warp % SD;
             const int dper = (nbh + SD - 1) / SD, d0 = min(nbh, dseg * dper), d1 = min(nbh, d0 + dper);
             // two CTA rounds per pass: a warp decodes both of its units back to back and the
@@ -445,7 +534,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                         const int pick = own[pr / rgd], row = (pr % rgd) * 32 + lane;
                         const PackedMat& m = dl[pick].down;
                         if (m.body != nullptr && m.k == ff && m.n == dim)
-                            y = lane_row_partial_any(m, row, d0, d1, hq + (size_t)pick * nbh * kActStride, hd + pick * nbh);
+                            y = lane_row_db_any(m, row, d0, d1, hq + (size_t)pick * nbh * kActStride, hd + pick * nbh);
                         else if (lane == 0) atomicExch(P.err, 1);
                     }
                     part[(rr * NW + warp) * 32 + lane] = y;
@@ -456,13 +545,61 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                     if (pr2 < npair) {
                         float t = 0.0f;
                         for (int j = 0; j < SD; ++j) t = __fadd_rn(t, part[(rr * NW + s2 * SD + j) * 32 + lane]);
-                        const size_t o = (size_t)own[pr2 / rgd] * dim + (pr2 % rgd) * 32 + lane;
+                        const int rgi = pr2 % rgd;
+                        const size_t o = (size_t)own[pr2 / rgd] * dim + rgi * 32 + lane;
                         ybuf(li)[o] = t;
                         for (int r = 0; MULTI && r < sh.world; ++r)  // the peers' copies of this layer's slot
                             if (r != sh.rank) sh.peer_yx[r][((sh.epoch + li) & 1) * yslot + o] = t;
+                        // count the row group's rows (here, and on every peer)
+                        __syncwarp();
+                        if (lane == 0) {
+                            const size_t ci = (size_t)((sh.epoch + li) & 1) * rgd + rgi;
+                            red_release_gpu(sh.rgcnt + ci, 1u);
+                            for (int r = 0; MULTI && r < sh.world; ++r)
+                                if (r != sh.rank) red_release_sys(sh.peer_rgcnt[r] + ci, 1u);
+                        }
                     }
                 }
                 __syncthreads();
+            }
+            STACK_STAMP(li, 6);
+            {  // 4. owner warp of row group blockIdx.x + warp * G: combine once all k picks' rows are in
+                const int rg = blockIdx.x + warp * G;
+                int ok = 1;
+                if (rg < rgd) {
+                    const unsigned lg = sh.epoch + (unsigned)li;
+                    const unsigned* rc = sh.rgcnt + (size_t)(lg & 1u) * rgd + rg;
+                    const unsigned tgt = (unsigned)k * ((lg >> 1) + 1u);
+                    if (lane == 0)
+                        ok = (MULTI ? wait_reached<true>(rc, tgt, P.err, P.wait_limit, kErrBarrier)
+                                    : wait_reached<false>(rc, tgt, P.err, P.wait_limit, kErrBarrier))
+                                 ? 1
+                                 : 0;
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (ok) {
+                        const float* yr = ybuf(li);
+                        const int* ord = sord + cur * kMaxPicks;
+                        float yv[kMaxPicks];
+#pragma unroll
+                        for (int o2 = 0; o2 < kMaxPicks; ++o2)
+                            if (o2 < k) yv[o2] = __ldcg(yr + (size_t)ord[o2] * dim + rg * 32 + lane);
+                        float acc = 0.0f;
+#pragma unroll
+                        for (int o2 = 0; o2 < kMaxPicks; ++o2)
+                            if (o2 < k) acc = __fmaf_rn(sw[cur * kMaxPicks + ord[o2]], yv[o2], acc);
+                        const float hn = __fadd_rn(hs[rg * 32 + lane], acc);
+                        if (li == P.nl - 1) {
+                            P.h_out[rg * 32 + lane] = hn;
+                        } else {
+                            P.w.hbuf[(size_t)((li + 1) & 1) * dim + rg * 32 + lane] = hn;
+                            float s2 = __fmul_rn(hn, hn);
+#pragma unroll
+                            for (int o2 = 16; o2 > 0; o2 >>= 1) s2 = __fadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, o2));
+                            if (lane == 0) P.w.ssbuf[(size_t)((li + 1) & 1) * rgd + rg] = s2;
+                        }
+                    }
+                }
+                if (!__syncthreads_and(ok)) return;
             }
         } else {
             // 2. gate/up rows (exact order: 4 threads per row, quad exchange) -> gu
@@ -511,11 +648,15 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                     if (r != sh.rank) sh.peer_yx[r][((sh.epoch + li) & 1) * yslot + o] = y;
             }
         }
-        if (MULTI && sh.world > 1) signal_peers(sh);  // this CTA's peer stores, then one release per peer
-        if (!grid_barrier(P.bar, 2 * li + 2, P.err, P.wait_limit, stage_next)) return;
-        if (MULTI && sh.world > 1 && !exchange_rows(sh, li, P.err, P.wait_limit)) return;
+        if (!FAST) STACK_STAMP(li, 6);
+        if (!FAST && MULTI && sh.world > 1) signal_peers(sh);  // this CTA's peer stores, then one release per peer
+        // barrier number: one per layer in the fast order, two in the exact order
+        if (!grid_barrier(P.bar, FAST ? li + 1 : 2 * li + 2, P.err, P.wait_limit, stage_next)) return;
+        STACK_STAMP(li, 7);
+        if (!FAST && MULTI && sh.world > 1 && !exchange_rows(sh, li, P.err, P.wait_limit)) return;
     }
-    // h after the last layer: each CTA writes its slice
+    // h after the last layer: each CTA writes its slice (the fast order's owner warps wrote it)
+    if (FAST) return;
     const int per = (dim + G - 1) / G;
     for (int i = blockIdx.x * per + tid; i < min(dim, (blockIdx.x + 1) * per); i += NT) P.h_out[i] = hs[i];
 }
@@ -532,6 +673,8 @@ static int stack_grid() {
     return sms > 0 ? sms : 148;
 }
 
+size_t stack_block_words(int nl_max, int k, int ff) { return (size_t)nl_max * k * (ff >> 8); }
+
 bool stack_supported(int dim, int ff, int k, bool fast) {
     int dev = 0, optin = 0, coop = 0;
     cudaGetDevice(&dev);
@@ -545,7 +688,7 @@ bool stack_supported(int dim, int ff, int k, bool fast) {
 cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k, const int* route_ids,
                          const float* route_w, const float* h_in, float* h_out, int dim, int ff, float limit, float* gu,
                          float* yrows, unsigned* bar, int* err, bool fast, const StackShard& shard, cudaStream_t s,
-                         unsigned wait_limit) {
+                         unsigned wait_limit, const StackWork& w) {
     const uint32_t* tables = nullptr;
     cudaError_t e = tables_device_ptr(&tables);
     if (e != cudaSuccess) return e;
@@ -570,6 +713,10 @@ cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k
     P.wait_limit = wait_limit;
     P.tables = tables;
     P.sh = shard;
+    P.w = w;
+    if (fast && (w.hbuf == nullptr || w.ssbuf == nullptr || w.hq == nullptr || w.hd == nullptr || w.blk == nullptr ||
+                 shard.rgcnt == nullptr))
+        return cudaErrorInvalidValue;
     const int nt = stack_threads(fast);
     const size_t sm = stack_smem(dim, ff, k, fast);
     const bool multi = shard.world > 1;
@@ -577,8 +724,16 @@ cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k
                                      : (multi ? k_stack<false, 512, true> : k_stack<false, 512, false>);
     if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))) return e;
     if ((e = cudaMemsetAsync(bar, 0, sizeof(unsigned), s))) return e;
+    if (fast && (e = cudaMemsetAsync(w.blk, 0, stack_block_words(nl, k, ff) * sizeof(unsigned), s))) return e;
     void* args[] = {&P};
     return cudaLaunchCooperativeKernel(reinterpret_cast<void*>(kern), dim3(G), dim3(nt), args, sm, s);
 }
 
 }  // namespace clb
+
+#ifdef CLB_FLOW_TRACE
+extern "C" int clb_stack_trace_read(void* host, size_t bytes) {
+    if (bytes > sizeof(clb::g_stack_trace)) bytes = sizeof(clb::g_stack_trace);
+    return (int)cudaMemcpyFromSymbol(host, clb::g_stack_trace, bytes);
+}
+#endif

@@ -408,6 +408,52 @@ __device__ __noinline__ float lane_row_db(const PackedMat& m, int row, int b0, i
     }
     return __fmul_rn(0.125f, acc);
 }
+// As lane_row_db with the next block's bytes loaded into registers while the current one
+// is decoded (a register double buffer: ~127 registers, for kernels whose call graph has
+// room for them).
+template <int T, int AS = kActStride>
+__device__ __noinline__ float lane_row_db2(const PackedMat& m, int row, int b0, int b1, const int8_t* act_qs,
+                                           const float* act_d) {
+    constexpr int NP = T == CLB_IQ1_M ? 3 : 4;
+    const uint32_t lb = (threadIdx.x & 31) * 4u;
+    const size_t n = (size_t)m.n, pstride = n * 16, bstride = (size_t)NP * n * 16;
+    const uint8_t* p = m.body + (size_t)b0 * bstride + (size_t)row * 16;
+    const uint8_t* sc = T == CLB_IQ2_XXS ? nullptr : m.sc + ((size_t)b0 * n + (size_t)row) * 8;
+    const uint16_t* dp = T == CLB_IQ1_M ? nullptr : m.d + (size_t)b0 * n + (size_t)row;
+    float acc = 0.0f;
+    auto step = [&](const RowRaw& r, int b) {
+        const int M = block_sum8<T>(r, act_qs + (size_t)b * AS, lb);
+        acc = __fmaf_rn(__fmul_rn(raw_scale<T>(r), act_d[b]), (float)M, acc);
+    };
+    auto advance = [&] {
+        p += bstride;
+        if (T != CLB_IQ2_XXS) sc += n * 8;
+        if (T != CLB_IQ1_M) dp += n;
+    };
+    RowRaw ra, rb;
+    if (b0 < b1) load_raw_at<T>(p, pstride, sc, dp, ra);
+    for (int b = b0; b < b1; b += 2) {
+        if (b + 1 < b1) {
+            advance();
+            load_raw_at<T>(p, pstride, sc, dp, rb);
+        }
+        step(ra, b);
+        if (b + 1 >= b1) break;
+        if (b + 2 < b1) {
+            advance();
+            load_raw_at<T>(p, pstride, sc, dp, ra);
+        }
+        step(rb, b + 1);
+    }
+    return __fmul_rn(0.125f, acc);
+}
+template <int AS = kActStride>
+__device__ __forceinline__ float lane_row_db2_any(const PackedMat& m, int row, int b0, int b1, const int8_t* aq,
+                                                  const float* ad) {
+    if (m.type == CLB_IQ2_XXS) return lane_row_db2<CLB_IQ2_XXS, AS>(m, row, b0, b1, aq, ad);
+    if (m.type == CLB_IQ2_XS) return lane_row_db2<CLB_IQ2_XS, AS>(m, row, b0, b1, aq, ad);
+    return lane_row_db2<CLB_IQ1_M, AS>(m, row, b0, b1, aq, ad);
+}
 template <int AS = kActStride>
 __device__ __forceinline__ float lane_row_db_any(const PackedMat& m, int row, int b0, int b1, const int8_t* aq,
                                                  const float* ad) {
