@@ -64,18 +64,58 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 50 ms during the timed region."""
+    """SM clock and clock-event (throttle) reasons of one GPU, read through NVML every 2 ms
+    by a thread while the timed region runs (read-only queries; a timed region of a few
+    tens of ms still gets samples). Falls back to `nvidia-smi -lms 50` without NVML."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self, device):
+    def __init__(self, device, period_s=0.002):
         self.device = device
+        self.period = period_s
         self.proc = None
+        self.nvml = None
         self.lines = []
+        self.samples = []  # (sm_mhz, max_mhz, reason bits)
+        self.stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device)
 
     def __enter__(self):
+        try:
+            self.nvml, h = self._nvml_handle()
+            pn = self.nvml
+            self.bits = {"hw_slowdown": pn.nvmlClocksEventReasonHwSlowdown,
+                         "hw_thermal_slowdown": pn.nvmlClocksEventReasonHwThermalSlowdown,
+                         "sw_thermal_slowdown": pn.nvmlClocksEventReasonSwThermalSlowdown,
+                         "sw_power_cap": pn.nvmlClocksEventReasonSwPowerCap}
+            mx = pn.nvmlDeviceGetMaxClockInfo(h, pn.NVML_CLOCK_SM)
+
+            def poll():
+                while not self.stop.is_set():
+                    try:
+                        self.samples.append((pn.nvmlDeviceGetClockInfo(h, pn.NVML_CLOCK_SM), mx,
+                                             pn.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    except Exception:
+                        pass
+                    self.stop.wait(self.period)
+
+            self.t = threading.Thread(target=poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "50"],
@@ -91,6 +131,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.nvml is not None:
+            self.t.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -101,7 +144,10 @@ class ClockSampler:
 
     def summary(self):
         sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s, m, r in self.samples:
+            sm.append(float(s))
+            mx.append(float(m))
+            reasons.update(n for n, b in self.bits.items() if r & b)
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
@@ -111,13 +157,13 @@ class ClockSampler:
                 mx.append(float(parts[2]))
             except ValueError:
                 continue
-            for name, v in zip(names, parts[5:9]):
+            for name, v in zip(self.NAMES, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(name)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvml" if self.samples else "nvidia-smi"}
 
 
 def make_inputs(rng, n, layers=LAYERS, experts=EXPERTS):

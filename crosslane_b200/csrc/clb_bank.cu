@@ -574,8 +574,6 @@ int32_t clb_bank_create(const clb_bank_config_v1* cfg_in, clb_bank** out, clb_er
         if (bank->persistent && bank->fast()) {
             bank->stk.hbuf = bank->dev_alloc<float>(2 * dim);
             bank->stk.ssbuf = bank->dev_alloc<float>(2 * (dim / 32));
-            bank->stk.hq = bank->dev_alloc<int8_t>(k * ff);
-            bank->stk.hd = bank->dev_alloc<float>(k * ff / 256);
             bank->stk.blk = bank->dev_alloc<unsigned>(clb::stack_block_words(cfg.n_layers, (int)k, (int)ff));
         }
         bank->d_ids = bank->dev_alloc<int>(k);

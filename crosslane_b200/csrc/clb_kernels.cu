@@ -698,9 +698,17 @@ static int v2_variant() {
 }
 static int v2_max_threads() { return v2_variant() == 2 ? 1024 : 512; }
 
+// The most dynamic shared memory the kernel can be launched with: the per-block opt-in
+// limit less the kernel's static shared memory (the decode's prmt byte tables).
 template <typename K>
 static cudaError_t allow_smem(K kernel) {
-    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    int dev = 0, optin = 0;
+    cudaError_t e;
+    if ((e = cudaGetDevice(&dev)) || (e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)))
+        return e;
+    cudaFuncAttributes a{};
+    if ((e = cudaFuncGetAttributes(&a, kernel))) return e;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)a.sharedSizeBytes);
 }
 cudaError_t set_v2_smem_limits() {
     cudaError_t e;

@@ -109,14 +109,12 @@ struct StackShard {
     unsigned* peer_rgcnt[kMaxPeers] = {};
 };
 // Fast-order workspace of the persistent kernel: hbuf [2][dim] h between layers, ssbuf
-// [2][dim / 32] its per-32-row-group sums of squares, hq [k][ff] + hd [k][ff / 256] the
-// picks' Q8_K(h) (quantized once per block), blk: stack_block_words(nl_max, k, ff) block
-// counters, zeroed by launch_stack. The row-group counters live in StackShard::rgcnt.
+// [2][dim / 32] its per-32-row-group sums of squares, blk: stack_block_words(nl_max, k, ff)
+// counters of the SwiGLU output's 256-row blocks (8 row groups each), zeroed by
+// launch_stack. The row-group counters live in StackShard::rgcnt.
 struct StackWork {
     float* hbuf = nullptr;
     float* ssbuf = nullptr;
-    int8_t* hq = nullptr;
-    float* hd = nullptr;
     unsigned* blk = nullptr;
 };
 size_t stack_block_words(int nl_max, int k, int ff);

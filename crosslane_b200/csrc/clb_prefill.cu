@@ -156,7 +156,7 @@ struct PfSmem {
 static_assert(PfSmem::raw % 16 == 0 && PfSmem::dw % 16 == 0 && PfSmem::dxs % 16 == 0 && PfSmem::bars % 8 == 0,
               "aligned regions");
 static_assert(kPfBStage % 1024 == 0 && 2944 * 4 <= 2 * kPfRawBlock, "swizzle atoms; table staging area");
-static_assert(PfSmem::total <= 227 * 1024, "fits one CTA per SM");
+static_assert(PfSmem::total + 16 <= 227 * 1024, "fits one CTA per SM with the 16 bytes of static prmt tables");
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));

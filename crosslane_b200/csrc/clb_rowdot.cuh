@@ -35,6 +35,8 @@ constexpr uint32_t kRowTableBytes = 128 * 1024;
 constexpr uint32_t kPos2 = 0x002B1908u;  // +8, +25, +43
 constexpr uint32_t kNeg2 = 0x00D5E7F8u;  // -8, -25, -43
 constexpr uint32_t kVal1 = 0x000100FFu;  // -1, 0, +1
+constexpr uint32_t kIq1DeltaPos = 0x000901F9u;  // -7, 1, 9 (IQ1_M 8q + delta, delta = +1)
+constexpr uint32_t kIq1DeltaNeg = 0x0007FFF7u;  // -9, -1, 7 (delta = -1)
 
 // Byte permute (PTX prmt.b32, default mode) through the intrinsic, so constant operands
 // become immediates instead of registers the compiler re-materialises.
@@ -45,6 +47,20 @@ __device__ __forceinline__ uint32_t prmt2(uint32_t a, uint32_t b, uint32_t sel) 
 __device__ __forceinline__ uint32_t prmt_sel(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t d;
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+// The byte tables of the prmt decode {kPos2, kNeg2, kIq1DeltaPos, kIq1DeltaNeg} in shared
+// memory, written by fill_row_tables: the decode loads them once per call, so both prmt
+// operands stay in registers (as immediates the compiler re-creates them with a move
+// before every prmt, which doubled the FMA-pipe instructions of the decode).
+__shared__ uint32_t clb_prmt_k[4];
+// prmt_sel with the byte tables A (bytes 0-3) and B (bytes 4-7) of clb_prmt_k.
+template <uint32_t A, uint32_t B>
+__device__ __forceinline__ uint32_t prmt_k(uint32_t sel) {
+    static_assert((A == kPos2 && B == kNeg2) || (A == kIq1DeltaPos && B == kIq1DeltaNeg), "a table of clb_prmt_k");
+    const int i = A == kPos2 ? 0 : 2;
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(clb_prmt_k[i]), "r"(clb_prmt_k[i + 1]), "r"(sel));
     return d;
 }
 // Table word at byte offset `off` of the kernel's dynamic shared memory. Indexing the
@@ -67,6 +83,8 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 // thread of the CTA; the caller syncs afterwards.
 __device__ __forceinline__ void fill_row_tables(const uint32_t* __restrict__ compact, uint32_t* stage) {
     for (int i = threadIdx.x; i < 2944; i += blockDim.x) stage[i] = __ldg(compact + i);
+    if (threadIdx.x < 4) clb_prmt_k[threadIdx.x] = threadIdx.x == 0 ? kPos2 : threadIdx.x == 1 ? kNeg2
+                                                  : threadIdx.x == 2 ? kIq1DeltaPos : kIq1DeltaNeg;
     __syncthreads();
     uint4* a = reinterpret_cast<uint4*>(clb_dyn_smem + kRowTabXXS);
     for (int s = threadIdx.x; s < 4096; s += blockDim.x) {  // slot i: 8 x grid, 8 x sign
@@ -239,8 +257,8 @@ __device__ __forceinline__ void block_sum(const RowRaw& r, const int8_t* q, uint
             int a = 0;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel[j]), (int)qv[2 * j], a);
-                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel[j] >> 16), (int)qv[2 * j + 1], a);
+                a = __dp4a((int)prmt_k<kPos2, kNeg2>(sel[j]), (int)qv[2 * j], a);
+                a = __dp4a((int)prmt_k<kPos2, kNeg2>(sel[j] >> 16), (int)qv[2 * j + 1], a);
             }
             M += scale * a;
         } else if (T == CLB_IQ2_XS) {
@@ -258,8 +276,8 @@ __device__ __forceinline__ void block_sum(const RowRaw& r, const int8_t* q, uint
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 int& a = j < 2 ? alo : ahi;
-                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel[j]), (int)qv[2 * j], a);
-                a = __dp4a((int)prmt_sel(kPos2, kNeg2, sel[j] >> 16), (int)qv[2 * j + 1], a);
+                a = __dp4a((int)prmt_k<kPos2, kNeg2>(sel[j]), (int)qv[2 * j], a);
+                a = __dp4a((int)prmt_k<kPos2, kNeg2>(sel[j] >> 16), (int)qv[2 * j + 1], a);
             }
             M += s_lo * alo + s_hi * ahi;
         } else {

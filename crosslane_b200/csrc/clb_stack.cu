@@ -7,12 +7,13 @@
 //   1. every CTA: h (h_in, or the previous layer's combine in global memory) and its
 //      per-32-row-group sums of squares; x = RMSNorm(h) (fixed-order total), Q8_K(x) into
 //      shared memory;
-//   2. gate/up rows of every pick in CTA rounds (K segments per warp, added in order),
-//      SwiGLU -> gu; each 32-row group counts its 256-row block, and the CTA that completes
-//      a block quantizes it once to Q8_K(h) in global memory and marks it ready;
-//   3. each CTA waits for (only) the blocks of the picks its down rounds touch, copies
-//      them into shared memory and decodes its down rounds -> expert rows (also into every
-//      peer's slot of a sharded bank); each row group counts its rows;
+//   2. gate/up rows of every pick in CTA rounds (K segments per warp, added in order,
+//      rows decoded with lane_row_roll), SwiGLU -> gu; each 32-row group counts its 256-row
+//      block with a release add (no round trip on the producer side);
+//   3. each CTA waits for (only) the blocks of the picks its down rounds touch, quantizes
+//      each block's SwiGLU output to Q8_K(h) in shared memory itself, and decodes its down
+//      rounds -> expert rows (also into every peer's slot of a sharded bank); each row
+//      group counts its rows;
 //   4. the owner warp of each 32-row group waits for the rows of all k picks and applies
 //      h += the ascending-id fma combine (runtime.cpp:184-187), writing h and its sum of
 //      squares for the next layer (the last layer: h_out);
@@ -55,7 +56,7 @@ __device__ __forceinline__ void stack_stamp(int li, int slot) {
 namespace {
 
 constexpr int kErrBarrier = 2;                     // err flag value of a timed-out barrier or wait
-constexpr unsigned kBlockReady = 9;                 // block counter: 8 row groups done + quantized
+constexpr unsigned kBlockReady = 8;                 // block counter: its 8 row groups of SwiGLU output stored
 
 // Grid-wide barrier over gridDim.x co-resident CTAs (cooperative launch) on a counter
 // that only grows: barrier number e (1, 2, ...) is passed once the counter reaches
@@ -128,30 +129,34 @@ __device__ bool exchange_rows(const StackShard& sh, int li, int* err, unsigned l
     return __syncthreads_and(ok) != 0;
 }
 
-// K segments of the fast-order phases for `kown` picks on `grid` CTAs of 16 warps, chosen
+// K segments of the fast-order phases for `kown` picks on `grid` CTAs of `nw` warps, chosen
 // to minimise the blocks one thread decodes (CTA rounds x blocks per segment; the smaller
-// count on ties). gate/up: SG in {1, 2, 4, 8}, a round = 8 / SG row groups of 32 rows x 2
-// matrices x SG segments. down: SD in {1, 2, 3, 4, 6, 8}, a round = 16 / SD (pick, row
-// group) pairs x SD segments. Every thread evaluates the same expression.
-__host__ __device__ inline int gateup_segments(int kown, int ff, int nb, int grid) {
+// count on ties). gate/up: SG divides nw / 2, a round = nw / (2 SG) row groups of 32 rows x 2
+// matrices x SG segments. down: SD in {1, 2, 3, 4, 6, 8}, a round = nw / SD (pick, row
+// group) pairs x SD segments (nw % SD warps idle). Every thread evaluates the same expression.
+__host__ __device__ inline int gateup_segments(int kown, int ff, int nb, int grid, int nw) {
     int best = 1;
     long best_cost = -1;
-    const int choices[4] = {1, 2, 4, 8};
-    for (int i = 0; i < 4; ++i) {
+    const int choices[8] = {1, 2, 3, 4, 6, 8, 12, 16};
+    for (int i = 0; i < 8; ++i) {
         const int SG = choices[i];
-        const long rounds = ((long)kown * (ff / 32) + (8 / SG) - 1) / (8 / SG);
+        if ((nw / 2) % SG != 0) continue;
+        const int rgr = nw / 2 / SG;
+        const long rounds = ((long)kown * (ff / 32) + rgr - 1) / rgr;
         const long cost = (rounds + grid - 1) / grid * ((nb + SG - 1) / SG);
         if (best_cost < 0 || cost < best_cost) best_cost = cost, best = SG;
     }
     return best;
 }
-__host__ __device__ inline int down_segments(int kown, int dim, int nb, int grid) {
+__host__ __device__ inline int down_segments(int kown, int dim, int nb, int grid, int nw) {
     int best = 1;
     long best_cost = -1;
     const int choices[6] = {1, 2, 3, 4, 6, 8};
     for (int i = 0; i < 6; ++i) {
         const int SD = choices[i];
-        const long rounds = ((long)kown * (dim / 32) + (16 / SD) - 1) / (16 / SD);
+        const int ppr = nw / SD;
+        if (ppr < 1) continue;
+        const long rounds = ((long)kown * (dim / 32) + ppr - 1) / ppr;
         const long cost = (rounds + grid - 1) / grid * ((nb + SD - 1) / SD);
         if (best_cost < 0 || cost < best_cost) best_cost = cost, best = SD;
     }
@@ -366,9 +371,11 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             __syncthreads();
         }
         if (li == P.nl) break;
-        if (FAST && li > 0) {  // h as the previous layer's owner warps combined it
-            const float4* src = reinterpret_cast<const float4*>(P.w.hbuf + (size_t)(li & 1) * dim);
-            for (int i = tid; i < (dim >> 2); i += NT) reinterpret_cast<float4*>(hs)[i] = __ldcg(src + i);
+        if (FAST && li > 0) {  // h and its row-group sums of squares as the previous layer's owner warps wrote them
+            const float4* hsrc = reinterpret_cast<const float4*>(P.w.hbuf + (size_t)(li & 1) * dim);
+            float* ssp = reinterpret_cast<float*>(tree);
+            for (int i = tid; i < (dim >> 2); i += NT) reinterpret_cast<float4*>(hs)[i] = __ldcg(hsrc + i);
+            for (int rg = tid; rg < (dim >> 5); rg += NT) ssp[rg] = __ldcg(P.w.ssbuf + (size_t)(li & 1) * (dim >> 5) + rg);
             __syncthreads();
         }
         STACK_STAMP(li, 1);
@@ -392,10 +399,8 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                     for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
                     if (lane == 0) ssp[rg] = s;
                 }
-            } else {
-                for (int rg = tid; rg < nrg; rg += NT) ssp[rg] = __ldcg(P.w.ssbuf + (size_t)(li & 1) * nrg + rg);
+                __syncthreads();
             }
-            __syncthreads();
             float t = 0.0f;
             for (int i = lane; i < nrg; i += 32) t = __fadd_rn(t, ssp[i]);
 #pragma unroll
@@ -441,7 +446,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             //    are added in order and SwiGLU(g, u) goes to hbuf [pick][ff]
             const int* own = sown + cur * (kMaxPicks + 1);
             const int kown = own[kMaxPicks];
-            const int SG = gateup_segments(kown, ff, nbx, G), RGR = 8 / SG, rgpp = ff >> 5, nrg = kown * rgpp;
+            const int SG = gateup_segments(kown, ff, nbx, G, NW), RGR = NW / 2 / SG, rgpp = ff >> 5, nrg = kown * rgpp;
             const int seg = warp % SG, mat = (warp / SG) & 1, rgl = warp / (2 * SG);
             const int per = (nbx + SG - 1) / SG, b0 = min(nbx, seg * per), b1 = min(nbx, b0 + per);
             for (int q = blockIdx.x; q * RGR < nrg; q += G) {
@@ -450,7 +455,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                 if (rg < nrg) {
                     const int pick = own[rg / rgpp], row = (rg % rgpp) * 32 + lane;
                     const PackedMat& m = mat ? dl[pick].up : dl[pick].gate;
-                    if (m.body != nullptr && m.k == dim && m.n == ff) y = lane_row_db_any(m, row, b0, b1, xq, xd);
+                    if (m.body != nullptr && m.k == dim && m.n == ff) y = lane_row_roll_any(m, row, b0, b1, xq, xd);
                     else if (lane == 0) atomicExch(P.err, 1);
                 }
                 part[warp * 32 + lane] = y;
@@ -465,22 +470,9 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                         }
                         const int slot = own[rg2 / rgpp], rgi = rg2 % rgpp, hb = rgi >> 3;
                         P.gu[(size_t)slot * ff + rgi * 32 + lane] = swiglu(g, u, P.limit);
-                        // count the 256-row block; the 8th row group quantizes it once for all CTAs
+                        // count the 256-row block (the consumers quantize it once all 8 row groups are in)
                         __syncwarp();
-                        unsigned* bc = P.w.blk + ((size_t)li * k + slot) * nbh + hb;
-                        unsigned old = 0;
-                        if (lane == 0) old = atom_add_acq_rel_gpu(bc, 1u);
-                        old = __shfl_sync(0xffffffffu, old, 0);
-                        if (old == 7u) {
-                            const float4* src =
-                                reinterpret_cast<const float4*>(P.gu + (size_t)slot * ff + (size_t)hb * 256 + lane * 8);
-                            const float4 lo = __ldcg(src), hi = __ldcg(src + 1);
-                            float v8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-                            warp_quant_regs(v8, P.w.hq + (size_t)slot * ff + (size_t)hb * 256,
-                                            P.w.hd + (size_t)slot * nbh + hb);
-                            __syncwarp();
-                            if (lane == 0) red_release_gpu(bc, 1u);  // -> kBlockReady
-                        }
+                        if (lane == 0) red_release_gpu(P.w.blk + ((size_t)li * k + slot) * nbh + hb, 1u);
                     }
                 }
                 __syncthreads();
@@ -490,13 +482,13 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
 
             // 3. Q8_K(h) of every pick, then the down rows: a CTA round covers 16 / SD
             //    (pick, 32-row group) pairs, each split into SD K segments (one warp each)
-            const int SD = down_segments(kown, dim, nbh, G), PPR = 16 / SD, rgd = dim >> 5, npair = kown * rgd;
+            const int SD = down_segments(kown, dim, nbh, G, NW), PPR = NW / SD, rgd = dim >> 5, npair = kown * rgd;
             uint32_t need = 0;  // picks whose rows this CTA's down rounds touch
             for (int q = blockIdx.x; q * PPR < npair; q += G)
                 for (int j = 0; j < PPR && q * PPR + j < npair; ++j) need |= 1u << own[(q * PPR + j) / rgd];
             const int nneed = __popc(need);
-            {  // Q8_K(h) of those picks: wait until each block is ready (quantized by the CTA
-               // that completed it), copy it into shared memory
+            {  // Q8_K(h) of those picks: wait until each block's 8 row groups of SwiGLU output are
+               // stored, quantize it into shared memory
                 int ok = 1;
                 for (int wi = warp; wi < nneed * nbh; wi += NW) {
                     const int nth = wi / nbh, b = wi - nth * nbh;  // block b of the nth set bit of `need`
@@ -513,10 +505,11 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                         ok = 0;
                         break;
                     }
-                    if (lane < 16)
-                        *reinterpret_cast<uint4*>(hq + ((size_t)slot * nbh + b) * kActStride + lane * 16) =
-                            __ldcg(reinterpret_cast<const uint4*>(P.w.hq + (size_t)slot * ff + (size_t)b * 256) + lane);
-                    if (lane == 0) hd[slot * nbh + b] = __ldcg(P.w.hd + (size_t)slot * nbh + b);
+                    __syncwarp();  // the other lanes' loads after lane 0's acquire
+                    const float4* src = reinterpret_cast<const float4*>(P.gu + (size_t)slot * ff + (size_t)b * 256 + lane * 8);
+                    const float4 lo = __ldcg(src), hi = __ldcg(src + 1);
+                    float v8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+                    warp_quant_regs(v8, hq + ((size_t)slot * nbh + b) * kActStride, hd + slot * nbh + b);
                 }
                 if (!__syncthreads_and(ok)) return;
             }
@@ -534,7 +527,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                         const int pick = own[pr / rgd], row = (pr % rgd) * 32 + lane;
                         const PackedMat& m = dl[pick].down;
                         if (m.body != nullptr && m.k == ff && m.n == dim)
-                            y = lane_row_db_any(m, row, d0, d1, hq + (size_t)pick * nbh * kActStride, hd + pick * nbh);
+                            y = lane_row_roll_any(m, row, d0, d1, hq + (size_t)pick * nbh * kActStride, hd + pick * nbh);
                         else if (lane == 0) atomicExch(P.err, 1);
                     }
                     part[(rr * NW + warp) * 32 + lane] = y;
@@ -662,7 +655,12 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
 }
 
 // Threads per CTA of the persistent kernel (16 warps, up to 128 registers a thread).
-static int stack_threads(bool) { return 512; }
+#ifndef CLB_STACK_FAST_THREADS
+#define CLB_STACK_FAST_THREADS 512
+#endif
+// Threads per CTA of the persistent kernel: the exact order 16 warps (up to 128 registers a
+// thread); the fast order CLB_STACK_FAST_THREADS.
+static int stack_threads(bool fast) { return fast ? CLB_STACK_FAST_THREADS : 512; }
 
 size_t stack_smem(int dim, int ff, int k, bool fast) { return StackSmem(dim, ff, k, !fast, stack_threads(fast)).total; }
 
@@ -714,13 +712,14 @@ cudaError_t launch_stack(const ExpertDesc* desc, int E, int first, int nl, int k
     P.tables = tables;
     P.sh = shard;
     P.w = w;
-    if (fast && (w.hbuf == nullptr || w.ssbuf == nullptr || w.hq == nullptr || w.hd == nullptr || w.blk == nullptr ||
+    if (fast && (w.hbuf == nullptr || w.ssbuf == nullptr || w.blk == nullptr ||
                  shard.rgcnt == nullptr))
         return cudaErrorInvalidValue;
     const int nt = stack_threads(fast);
     const size_t sm = stack_smem(dim, ff, k, fast);
     const bool multi = shard.world > 1;
-    void (*kern)(StackParams) = fast ? (multi ? k_stack<true, 512, true> : k_stack<true, 512, false>)
+    constexpr int FT = CLB_STACK_FAST_THREADS;
+    void (*kern)(StackParams) = fast ? (multi ? k_stack<true, FT, true> : k_stack<true, FT, false>)
                                      : (multi ? k_stack<false, 512, true> : k_stack<false, 512, false>);
     if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))) return e;
     if ((e = cudaMemsetAsync(bar, 0, sizeof(unsigned), s))) return e;

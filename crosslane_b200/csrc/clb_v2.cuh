@@ -3,6 +3,7 @@
 #pragma once
 #include "clb_rowdot.cuh"
 
+
 namespace clb {
 
 constexpr int kV2Threads = 512;          // 16 warps per CTA, one CTA per SM
@@ -296,46 +297,12 @@ __device__ __forceinline__ float lane_row_partial_any(const PackedMat& m, int ro
     return lane_row_partial<CLB_IQ1_M, AS>(m, row, b0, b1, aq, ad);
 }
 
-// ---- fast order, one row per lane, register double buffer (the dataflow stack kernel) ----
+// ---- fast order, one row per lane, rolling register reload (the persistent stack kernel) ----
 // block_sum's exact integers, except that IQ1_M folds its delta into the main sum: every
 // weight becomes the integer 8q + delta (q in {-1, 0, 1}, delta = +-1 per 8-value group,
 // |8q + delta| <= 9), taken straight from the byte pairs {-7, 1, 9} | {-9, -1, 7} with the
 // group's delta sign as selector bit 2, so one dp4a per 4 weights gives
 // 8 * main + delta (q8k_core.hpp:79-84 keeps them apart: main + delta / 8 is 1/8 of it).
-constexpr uint32_t kIq1DeltaPos = 0x000901F9u;  // -7, 1, 9
-constexpr uint32_t kIq1DeltaNeg = 0x0007FFF7u;  // -9, -1, 7
-template <int T>
-__device__ __forceinline__ int block_sum8(const RowRaw& r, const int8_t* q, uint32_t lb) {
-    if (T != CLB_IQ1_M) {
-        int M, D;
-        block_sum<T>(r, q, lb, M, D);
-        return M;
-    }
-    int M = 0;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const uint4 qa = *reinterpret_cast<const uint4*>(q + 32 * c);
-        const uint4 qb = *reinterpret_cast<const uint4*>(q + 32 * c + 16);
-        const uint32_t qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-        const uint32_t qsw = rw(r, c);
-        const uint32_t qh16 = (rw(r, 8 + (c >> 1)) >> (16 * (c & 1))) & 0xffffu;
-        const uint32_t scw = ((c < 4 ? r.sc.x : r.sc.y) >> (16 * ((c >> 1) & 1))) & 0xffffu;
-        const int s_lo = (int)(((scw >> (6 * (c & 1))) & 7u) << 1) | 1;
-        const int s_hi = (int)(((scw >> (6 * (c & 1) + 3)) & 7u) << 1) | 1;
-        int alo = 0, ahi = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint32_t nib = (qh16 >> (4 * j)) & 15u;
-            const uint32_t idx = ((qsw >> (8 * j)) & 0xffu) | ((nib & 7u) << 8);
-            const uint32_t sel = tab32(kRowTabIQ1 + idx * 16u + (lb & 12u)) | ((nib & 8u) ? 0x44444444u : 0u);
-            int& a = j < 2 ? alo : ahi;
-            a = __dp4a((int)prmt_sel(kIq1DeltaPos, kIq1DeltaNeg, sel), (int)qv[2 * j], a);
-            a = __dp4a((int)prmt_sel(kIq1DeltaPos, kIq1DeltaNeg, sel >> 16), (int)qv[2 * j + 1], a);
-        }
-        M += s_lo * alo + s_hi * ahi;
-    }
-    return M;
-}
 
 // Streaming weight loads: read once, so they bypass L1 allocation and leave the L1 lines
 // to the data that is reused (activations, the stack).
@@ -368,15 +335,87 @@ __device__ __forceinline__ void load_raw_at(const uint8_t* p, size_t pstride, co
     if (T != CLB_IQ1_M) r.d = ldg_u16_stream(dp);
 }
 
-// Partial of one row over blocks [b0, b1): 0.125 * sum_b (d_w * d_x)_b * M_b with M_b =
-// block_sum8 (for IQ1_M the 8q + delta integer), blocks in order, fp32. The next block is
-// prefetched into L2 while the current one is decoded. (A register double buffer decodes
-// ~10 % faster in isolation, but at ~127 registers it pushes every function of the
-// dataflow kernel's call graph into local-memory spills, which the weight stream evicts to
-// DRAM.) AS: byte stride of the activation blocks (kActStride in shared memory).
+// One 32-value chunk c of a block: the chunk's exact integer (IQ1_M: 8q + delta), from the
+// chunk's 32 activations qv, with the IQ2_XS / IQ1_M scale bytes taken from scx (chunks
+// 0-3) / scy (chunks 4-7).
+template <int T>
+__device__ __forceinline__ int chunk_sum8_q(const RowRaw& r, const uint32_t qv[8], uint32_t lb, int c, uint32_t scx,
+                                            uint32_t scy) {
+    if (T == CLB_IQ2_XXS) {
+        const uint32_t gw = rw(r, 2 * c), sw = rw(r, 2 * c + 1);
+        const int scale = (int)((((sw & 0x80808080u) | 0x08000000u) * 0x00204081u) >> 27);
+        uint32_t sel[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t sel_j = 0x5504u | ((uint32_t)j << 4);
+            sel[j] = tab32(kRowTabXXS + prmt2(gw, lb, sel_j)) | tab32(kRowTabXXS + 128 + prmt2(sw, lb, sel_j));
+        }
+        int a = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            a = __dp4a((int)prmt_k<kPos2, kNeg2>(sel[j]), (int)qv[2 * j], a);
+            a = __dp4a((int)prmt_k<kPos2, kNeg2>(sel[j] >> 16), (int)qv[2 * j + 1], a);
+        }
+        return scale * a;
+    } else if (T == CLB_IQ2_XS) {
+        const uint32_t scb = ((c < 4 ? scx : scy) >> (8 * (c & 3))) & 0xffu;
+        const int s_lo = (int)((scb & 15u) << 1) | 1, s_hi = (int)((scb >> 4) << 1) | 1;
+        uint32_t sel[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t w = rw(r, 2 * c + (j >> 1));
+            const uint32_t code = (j & 1) ? (w >> 16) : (w & 0xffffu);
+            sel[j] = tab32(kRowTabXS + (code & 511u) * 64u + (lb & 60u)) |
+                     tab32(kRowTabXXS + (code >> 9) * 256u + 128u + lb);
+        }
+        int alo = 0, ahi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            int& a = j < 2 ? alo : ahi;
+            a = __dp4a((int)prmt_k<kPos2, kNeg2>(sel[j]), (int)qv[2 * j], a);
+            a = __dp4a((int)prmt_k<kPos2, kNeg2>(sel[j] >> 16), (int)qv[2 * j + 1], a);
+        }
+        return s_lo * alo + s_hi * ahi;
+    } else {
+        const uint32_t qsw = rw(r, c);
+        const uint32_t qh16 = (rw(r, 8 + (c >> 1)) >> (16 * (c & 1))) & 0xffffu;
+        const uint32_t scw = ((c < 4 ? scx : scy) >> (16 * ((c >> 1) & 1))) & 0xffffu;
+        const int s_lo = (int)(((scw >> (6 * (c & 1))) & 7u) << 1) | 1;
+        const int s_hi = (int)(((scw >> (6 * (c & 1) + 3)) & 7u) << 1) | 1;
+        int alo = 0, ahi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t nib = (qh16 >> (4 * j)) & 15u;
+            const uint32_t idx = ((qsw >> (8 * j)) & 0xffu) | ((nib & 7u) << 8);
+            const uint32_t sel = tab32(kRowTabIQ1 + idx * 16u + (lb & 12u)) | ((nib & 8u) ? 0x44444444u : 0u);
+            int& a = j < 2 ? alo : ahi;
+            a = __dp4a((int)prmt_k<kIq1DeltaPos, kIq1DeltaNeg>(sel), (int)qv[2 * j], a);
+            a = __dp4a((int)prmt_k<kIq1DeltaPos, kIq1DeltaNeg>(sel >> 16), (int)qv[2 * j + 1], a);
+        }
+        return s_lo * alo + s_hi * ahi;
+    }
+}
+template <int T>
+__device__ __forceinline__ int chunk_sum8(const RowRaw& r, const int8_t* q, uint32_t lb, int c, uint32_t scx,
+                                          uint32_t scy) {
+    const uint4 qa = *reinterpret_cast<const uint4*>(q + 32 * c);
+    const uint4 qb = *reinterpret_cast<const uint4*>(q + 32 * c + 16);
+    const uint32_t qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+    return chunk_sum8_q<T>(r, qv, lb, c, scx, scy);
+}
+
+// Partial of one row over blocks [b0, b1): 0.125 * sum_b (d_w * d_x)_b * M_b with M_b the
+// block's exact integer (the sum of chunk_sum8; for IQ1_M 8q + delta), blocks in order,
+// fp32. AS: byte stride of the activation blocks (kActStride in shared memory).
+// Rolling register reload: the next block's 16-byte pieces
+// are loaded into the registers of the current block's pieces as soon as the chunks that
+// read them are done (IQ2: piece p holds chunks 2p, 2p+1; IQ1_M: qs pieces 0 / 1 hold
+// chunks 0-3 / 4-7, the qh piece all of them), and the scale bytes right after they are
+// copied at the block start. Each load gets most of a block's decode time to land, at no
+// register cost beyond the scale copies.
 template <int T, int AS = kActStride>
-__device__ __noinline__ float lane_row_db(const PackedMat& m, int row, int b0, int b1, const int8_t* act_qs,
-                                          const float* act_d) {
+__device__ __noinline__ float lane_row_roll(const PackedMat& m, int row, int b0, int b1, const int8_t* act_qs,
+                                            const float* act_d) {
     constexpr int NP = T == CLB_IQ1_M ? 3 : 4;
     const uint32_t lb = (threadIdx.x & 31) * 4u;
     const size_t n = (size_t)m.n, pstride = n * 16, bstride = (size_t)NP * n * 16;
@@ -384,82 +423,60 @@ __device__ __noinline__ float lane_row_db(const PackedMat& m, int row, int b0, i
     const uint8_t* sc = T == CLB_IQ2_XXS ? nullptr : m.sc + ((size_t)b0 * n + (size_t)row) * 8;
     const uint16_t* dp = T == CLB_IQ1_M ? nullptr : m.d + (size_t)b0 * n + (size_t)row;
     float acc = 0.0f;
-    auto step = [&](const RowRaw& r, int b) {
-        const int M = block_sum8<T>(r, act_qs + (size_t)b * AS, lb);
-        acc = __fmaf_rn(__fmul_rn(raw_scale<T>(r), act_d[b]), (float)M, acc);
-    };
-    auto advance = [&] {
-        p += bstride;
-        if (T != CLB_IQ2_XXS) sc += n * 8;
-        if (T != CLB_IQ1_M) dp += n;
-    };
+    if (b0 >= b1) return 0.0f;
+    RowRaw r;
+    load_raw_at<T>(p, pstride, sc, dp, r);
     for (int b = b0; b < b1; ++b) {
-        if (b + 1 < b1) {
-            const uint8_t* q = p + bstride;
-            prefetch_l2(q);
-            prefetch_l2(q + pstride);
-            prefetch_l2(q + 2 * pstride);
-            if (T != CLB_IQ1_M) prefetch_l2(q + 3 * pstride);
-        }
-        RowRaw r;
-        load_raw_at<T>(p, pstride, sc, dp, r);
-        step(r, b);
-        advance();
-    }
-    return __fmul_rn(0.125f, acc);
-}
-// As lane_row_db with the next block's bytes loaded into registers while the current one
-// is decoded (a register double buffer: ~127 registers, for kernels whose call graph has
-// room for them).
-template <int T, int AS = kActStride>
-__device__ __noinline__ float lane_row_db2(const PackedMat& m, int row, int b0, int b1, const int8_t* act_qs,
-                                           const float* act_d) {
-    constexpr int NP = T == CLB_IQ1_M ? 3 : 4;
-    const uint32_t lb = (threadIdx.x & 31) * 4u;
-    const size_t n = (size_t)m.n, pstride = n * 16, bstride = (size_t)NP * n * 16;
-    const uint8_t* p = m.body + (size_t)b0 * bstride + (size_t)row * 16;
-    const uint8_t* sc = T == CLB_IQ2_XXS ? nullptr : m.sc + ((size_t)b0 * n + (size_t)row) * 8;
-    const uint16_t* dp = T == CLB_IQ1_M ? nullptr : m.d + (size_t)b0 * n + (size_t)row;
-    float acc = 0.0f;
-    auto step = [&](const RowRaw& r, int b) {
-        const int M = block_sum8<T>(r, act_qs + (size_t)b * AS, lb);
-        acc = __fmaf_rn(__fmul_rn(raw_scale<T>(r), act_d[b]), (float)M, acc);
-    };
-    auto advance = [&] {
+        const bool more = b + 1 < b1;
         p += bstride;
         if (T != CLB_IQ2_XXS) sc += n * 8;
         if (T != CLB_IQ1_M) dp += n;
-    };
-    RowRaw ra, rb;
-    if (b0 < b1) load_raw_at<T>(p, pstride, sc, dp, ra);
-    for (int b = b0; b < b1; b += 2) {
-        if (b + 1 < b1) {
-            advance();
-            load_raw_at<T>(p, pstride, sc, dp, rb);
+        const float dd = __fmul_rn(raw_scale<T>(r), act_d[b]);
+        const uint32_t scx = r.sc.x, scy = r.sc.y;
+        if (more) {
+            if (T != CLB_IQ2_XXS) r.sc = ldg_v2_stream(sc);
+            if (T != CLB_IQ1_M) r.d = ldg_u16_stream(dp);
         }
-        step(ra, b);
-        if (b + 1 >= b1) break;
-        if (b + 2 < b1) {
-            advance();
-            load_raw_at<T>(p, pstride, sc, dp, ra);
+        const int8_t* q = act_qs + (size_t)b * AS;
+        int M = 0;
+        if (T != CLB_IQ1_M) {
+            M += chunk_sum8<T>(r, q, lb, 0, scx, scy);
+            M += chunk_sum8<T>(r, q, lb, 1, scx, scy);
+            if (more) r.b0 = ldg_v4_stream(p);
+            M += chunk_sum8<T>(r, q, lb, 2, scx, scy);
+            M += chunk_sum8<T>(r, q, lb, 3, scx, scy);
+            if (more) r.b1 = ldg_v4_stream(p + pstride);
+            M += chunk_sum8<T>(r, q, lb, 4, scx, scy);
+            M += chunk_sum8<T>(r, q, lb, 5, scx, scy);
+            if (more) r.b2 = ldg_v4_stream(p + 2 * pstride);
+            M += chunk_sum8<T>(r, q, lb, 6, scx, scy);
+            M += chunk_sum8<T>(r, q, lb, 7, scx, scy);
+            if (more) r.b3 = ldg_v4_stream(p + 3 * pstride);
+        } else {
+            M += chunk_sum8<T>(r, q, lb, 0, scx, scy);
+            M += chunk_sum8<T>(r, q, lb, 1, scx, scy);
+            M += chunk_sum8<T>(r, q, lb, 2, scx, scy);
+            M += chunk_sum8<T>(r, q, lb, 3, scx, scy);
+            if (more) r.b0 = ldg_v4_stream(p);
+            M += chunk_sum8<T>(r, q, lb, 4, scx, scy);
+            M += chunk_sum8<T>(r, q, lb, 5, scx, scy);
+            M += chunk_sum8<T>(r, q, lb, 6, scx, scy);
+            M += chunk_sum8<T>(r, q, lb, 7, scx, scy);
+            if (more) {
+                r.b1 = ldg_v4_stream(p + pstride);
+                r.b2 = ldg_v4_stream(p + 2 * pstride);
+            }
         }
-        step(rb, b + 1);
+        acc = __fmaf_rn(dd, (float)M, acc);
     }
     return __fmul_rn(0.125f, acc);
 }
 template <int AS = kActStride>
-__device__ __forceinline__ float lane_row_db2_any(const PackedMat& m, int row, int b0, int b1, const int8_t* aq,
-                                                  const float* ad) {
-    if (m.type == CLB_IQ2_XXS) return lane_row_db2<CLB_IQ2_XXS, AS>(m, row, b0, b1, aq, ad);
-    if (m.type == CLB_IQ2_XS) return lane_row_db2<CLB_IQ2_XS, AS>(m, row, b0, b1, aq, ad);
-    return lane_row_db2<CLB_IQ1_M, AS>(m, row, b0, b1, aq, ad);
-}
-template <int AS = kActStride>
-__device__ __forceinline__ float lane_row_db_any(const PackedMat& m, int row, int b0, int b1, const int8_t* aq,
-                                                 const float* ad) {
-    if (m.type == CLB_IQ2_XXS) return lane_row_db<CLB_IQ2_XXS, AS>(m, row, b0, b1, aq, ad);
-    if (m.type == CLB_IQ2_XS) return lane_row_db<CLB_IQ2_XS, AS>(m, row, b0, b1, aq, ad);
-    return lane_row_db<CLB_IQ1_M, AS>(m, row, b0, b1, aq, ad);
+__device__ __forceinline__ float lane_row_roll_any(const PackedMat& m, int row, int b0, int b1, const int8_t* aq,
+                                                   const float* ad) {
+    if (m.type == CLB_IQ2_XXS) return lane_row_roll<CLB_IQ2_XXS, AS>(m, row, b0, b1, aq, ad);
+    if (m.type == CLB_IQ2_XS) return lane_row_roll<CLB_IQ2_XS, AS>(m, row, b0, b1, aq, ad);
+    return lane_row_roll<CLB_IQ1_M, AS>(m, row, b0, b1, aq, ad);
 }
 
 // L2 prefetch of the first block of a row segment (no registers held).
