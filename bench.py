@@ -293,17 +293,22 @@ def parity_config3(args, rank, world, sharded, bank, local):
             outs.append(h)
     finally:
         ex.close()
+    # fast order (the benchmarked bank): one layer against the oracle, a whole token across
+    # ranks. Every sharded decode runs before the host oracle below, so that no rank waits in
+    # a kernel for a peer that is still busy on the host.
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    one = bank.stack_decode(0, 1, x0, logits[0, :1])
+    full = bank.stack_decode(0, args.layers, x0, logits[0])
     exact_same = _all_same(np.stack(outs), world)
+    fast_same = _all_same(np.stack([one, full]), world)
     exact_bits = None
     if rank == 0:
         want, exact_bits = x0, True
         for t in range(2):
             want = orc.stack(args.policy, SEED, want, logits[t, :n_ex], DIM, FF, k=PICKS)
             exact_bits = exact_bits and bool(np.array_equal(oracle_lib.bits(outs[t]), oracle_lib.bits(want)))
-    # fast order (the benchmarked bank): one layer against the oracle, a whole token across ranks
-    one = bank.stack_decode(0, 1, x0, logits[0, :1])
-    full = bank.stack_decode(0, args.layers, x0, logits[0])
-    fast_same = _all_same(np.stack([one, full]), world)
     rl2 = mar = None
     if rank == 0:
         want1 = orc.stack(args.policy, SEED, x0, logits[0, :1], DIM, FF, k=PICKS)

@@ -12,11 +12,13 @@
 //      block with a release add (no round trip on the producer side);
 //   3. each CTA waits for (only) the blocks of the picks its down rounds touch, quantizes
 //      each block's SwiGLU output to Q8_K(h) in shared memory itself, and decodes its down
-//      rounds -> expert rows (also into every peer's slot of a sharded bank); each row
-//      group counts its rows;
-//   4. the owner warp of each 32-row group waits for the rows of all k picks and applies
-//      h += the ascending-id fma combine (runtime.cpp:184-187), writing h and its sum of
-//      squares for the next layer (the last layer: h_out);
+//      rounds -> expert rows (also into every peer's slot of a sharded bank); one GPU: each
+//      row group counts its rows; sharded: each CTA counts itself after one system-scope
+//      fence, and the last CTA of the GPU publishes the layer number to every peer;
+//   4. the owner warp of each 32-row group waits for the rows of all k picks (sharded: for
+//      every local CTA and every peer's flag) and applies h += the ascending-id fma combine
+//      (runtime.cpp:184-187), writing h and its sum of squares for the next layer (the last
+//      layer: h_out);
 //   -- grid barrier --
 // Exact order (q8k_core's arithmetic, bit-identical to the CPU lane), per layer:
 //   1. every CTA: h += ascending-id fma combine of the previous layer's expert rows,
@@ -472,7 +474,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                         P.gu[(size_t)slot * ff + rgi * 32 + lane] = swiglu(g, u, P.limit);
                         // count the 256-row block (the consumers quantize it once all 8 row groups are in)
                         __syncwarp();
-                        if (lane == 0) red_release_gpu(P.w.blk + ((size_t)li * k + slot) * nbh + hb, 1u);
+                        if (lane == 0) red_release_gpu(P.w.blk + 1 + ((size_t)li * k + slot) * nbh + hb, 1u);
                     }
                 }
                 __syncthreads();
@@ -497,7 +499,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                     const int slot = __ffs(m) - 1;
                     int got = 1;
                     if (lane == 0)
-                        got = wait_reached<false>(P.w.blk + ((size_t)li * k + slot) * nbh + b, kBlockReady, P.err,
+                        got = wait_reached<false>(P.w.blk + 1 + ((size_t)li * k + slot) * nbh + b, kBlockReady, P.err,
                                                   P.wait_limit, kErrBarrier)
                                   ? 1
                                   : 0;
@@ -543,17 +545,29 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                         ybuf(li)[o] = t;
                         for (int r = 0; MULTI && r < sh.world; ++r)  // the peers' copies of this layer's slot
                             if (r != sh.rank) sh.peer_yx[r][((sh.epoch + li) & 1) * yslot + o] = t;
-                        // count the row group's rows (here, and on every peer)
+                        // one GPU: count the row group's rows for its owner warp (a sharded bank
+                        // counts whole CTAs after the pass instead, see below)
                         __syncwarp();
-                        if (lane == 0) {
-                            const size_t ci = (size_t)((sh.epoch + li) & 1) * rgd + rgi;
-                            red_release_gpu(sh.rgcnt + ci, 1u);
-                            for (int r = 0; MULTI && r < sh.world; ++r)
-                                if (r != sh.rank) red_release_sys(sh.peer_rgcnt[r] + ci, 1u);
-                        }
+                        if (!MULTI && lane == 0) red_release_gpu(sh.rgcnt + (size_t)((sh.epoch + li) & 1) * rgd + rgi, 1u);
                     }
                 }
                 __syncthreads();
+            }
+            if (MULTI) {
+                // Sharded: this CTA's rows (local slot and every peer's copy) are stored (the
+                // CTA barrier above); one system-scope fence makes them visible to the peers, a
+                // GPU-scope add counts the CTA, and the CTA completing the count publishes the
+                // layer number in its flag on every peer (one writer per flag, no contended
+                // address on the peers).
+                if (tid == 0) {
+                    fence_acq_rel_sys();
+                    const unsigned old = atom_add_acq_rel_gpu(P.w.blk, 1u);
+                    if (old + 1u == (unsigned)G * (unsigned)(li + 1)) {
+                        fence_acq_rel_sys();
+                        for (int r = 0; r < sh.world; ++r)
+                            if (r != sh.rank) st_relaxed_sys(sh.peer_flags[r] + sh.rank, sh.epoch + (unsigned)li + 1u);
+                    }
+                }
             }
             STACK_STAMP(li, 6);
             {  // 4. owner warp of row group blockIdx.x + warp * G: combine once all k picks' rows are in
@@ -561,14 +575,22 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
                 int ok = 1;
                 if (rg < rgd) {
                     const unsigned lg = sh.epoch + (unsigned)li;
-                    const unsigned* rc = sh.rgcnt + (size_t)(lg & 1u) * rgd + rg;
-                    const unsigned tgt = (unsigned)k * ((lg >> 1) + 1u);
-                    if (lane == 0)
-                        ok = (MULTI ? wait_reached<true>(rc, tgt, P.err, P.wait_limit, kErrBarrier)
-                                    : wait_reached<false>(rc, tgt, P.err, P.wait_limit, kErrBarrier))
+                    if (MULTI && lane == 0) {  // every local CTA's rows, then every peer's
+                        ok = wait_reached<false>(P.w.blk, (unsigned)G * (unsigned)(li + 1), P.err, P.wait_limit,
+                                                 kErrBarrier)
                                  ? 1
                                  : 0;
+                        for (int r = 0; ok && r < sh.world; ++r)
+                            if (r != sh.rank)
+                                ok = wait_reached<true>(sh.flags + r, lg + 1u, P.err, P.wait_limit, kErrBarrier) ? 1 : 0;
+                    }
+                    if (!MULTI && lane == 0) {  // one GPU: the k picks' rows of this row group
+                        const unsigned* rc = sh.rgcnt + (size_t)(lg & 1u) * rgd + rg;
+                        ok = wait_reached<false>(rc, (unsigned)k * ((lg >> 1) + 1u), P.err, P.wait_limit, kErrBarrier) ? 1
+                                                                                                                    : 0;
+                    }
                     ok = __shfl_sync(0xffffffffu, ok, 0);
+                    __syncwarp();  // the other lanes' loads after lane 0's acquire
                     if (ok) {
                         const float* yr = ybuf(li);
                         const int* ord = sord + cur * kMaxPicks;
@@ -671,7 +693,7 @@ static int stack_grid() {
     return sms > 0 ? sms : 148;
 }
 
-size_t stack_block_words(int nl_max, int k, int ff) { return (size_t)nl_max * k * (ff >> 8); }
+size_t stack_block_words(int nl_max, int k, int ff) { return 1 + (size_t)nl_max * k * (ff >> 8); }
 
 bool stack_supported(int dim, int ff, int k, bool fast) {
     int dev = 0, optin = 0, coop = 0;

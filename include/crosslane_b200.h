@@ -228,10 +228,12 @@ int32_t clb_bank_set_wait_limit(clb_bank* bank, uint32_t polls, clb_error_v1* er
  * Each GPU's bank owns experts [expert_begin, expert_end) of every layer (contiguous
  * blocks, together covering all experts). In clb_stack_decode* every GPU routes the same
  * token, computes only the picks it owns, and stores their expert rows straight into every
- * peer's exchange slot over NVLink; a per-layer counter per peer (bounded waits) says when
- * a peer's rows are in place, and every GPU then runs the same combine, so all GPUs keep
- * bit-identical residual streams. All GPUs must make the same stack calls in the same
- * order. Replaces the per-layer gather that runtime.cpp:121-189 does across lanes. */
+ * peer's exchange slot over NVLink. Per layer, default (fast) order: every CTA makes its
+ * stores visible system-wide with one fence and counts itself, and the last CTA of the GPU
+ * writes the layer number into its flag on every peer (one writer per flag). Exact order: a
+ * per-layer counter per peer that every CTA increments. Every wait is bounded. Every GPU then runs the same combine, so all GPUs keep bit-identical
+ * residual streams. All GPUs must make the same stack calls in the same order. Replaces
+ * the per-layer gather that runtime.cpp:121-189 does across lanes. */
 #define CLB_EXCHANGE_HANDLE_BYTES 64
 /* The bank's exchange region as a CUDA IPC handle (64 bytes) for the other processes. */
 int32_t clb_bank_exchange_handle(clb_bank* bank, void* handle_out, clb_error_v1* err);
