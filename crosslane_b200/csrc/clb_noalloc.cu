@@ -1,9 +1,8 @@
 // One expert FFN for callers that cannot allocate device memory.
 //
-// Some callers of this lane cannot call cudaMalloc: a host that is capturing its decode
-// step into a CUDA graph (cudaMalloc is not allowed inside a global-mode capture), a
-// serving loop that must not risk the implicit device synchronisation an allocation can
-// cause, or a plugin whose process hands all device memory to another allocator. They
+// Some callers of this lane cannot call cudaMalloc: a serving loop that must not risk the
+// implicit device synchronisation an allocation can cause, or a plugin whose process hands
+// all device memory to another allocator (a pool it does not control). They
 // bring their own weights, input and output buffers; this entry point supplies the only
 // other memory it needs -- the quantised input, the hidden vector and its quantisation --
 // from one fixed array compiled into the library. Every GPU that loads the library holds

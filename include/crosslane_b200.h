@@ -448,10 +448,10 @@ int32_t clb_bank_synchronize(clb_bank* bank, clb_error_v1* err);
 /* y[dim] = down(swiglu(gate(x), up(x))) for one expert whose three matrices are given
  * in the packed layout (device pointers w_gate/w_up [ff, dim], w_down [dim, ff]); x and y
  * are device buffers; runs on `stream` and returns without synchronising.
- * No counterpart in crosslane. For callers that cannot call cudaMalloc (a decode step
- * being captured into a CUDA graph, a serving loop that must not risk an allocation's
- * implicit device synchronisation, a plugin whose device memory belongs to another
- * allocator): the quantised input, hidden vector and its quantisation live in one fixed
+ * No counterpart in crosslane. For callers that cannot call cudaMalloc (a serving loop
+ * that must not risk an allocation's implicit device synchronisation, a plugin whose
+ * device memory belongs to another allocator): the quantised input, hidden vector and
+ * its quantisation live in one fixed
  * 57,856-byte array inside the library, held by every GPU that loads it until exit.
  * Limits: dim <= 16384, ff <= 8192 (else CLB_E_UNSUPPORTED with a message). It calls no
  * cudaMalloc/cudaFree. The first call on a device resolves that array's address and

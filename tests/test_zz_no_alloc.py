@@ -1,8 +1,8 @@
 """The allocation-free expert entry point (clb_expert_forward_noalloc).
 
-Some callers of the lane cannot call cudaMalloc -- a decode step being captured into a
-CUDA graph, a serving loop that must not risk an allocation's device synchronisation, a
-plugin whose device memory is owned by another allocator. This entry point takes packed
+Some callers of the lane cannot call cudaMalloc -- a serving loop that must not risk an
+allocation's device synchronisation, a plugin whose device memory is owned by another
+allocator. This entry point takes packed
 weights, x and y from the caller and keeps its own intermediates in a fixed array inside
 the library. Here its output is checked against the bank's warm_compute on the same
 expert and against the CPU oracle's expert, twice in a row (the second call reuses the
