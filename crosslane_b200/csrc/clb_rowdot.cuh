@@ -19,6 +19,9 @@
 //               then byte*256 + lane*4, which one prmt builds from a data byte.
 //   [64K, 96K)  IQ2_XS grid selectors, 512 x 16 copies (address idx*64 + (lane&15)*4).
 //   [96K, 128K) IQ1_M grid selectors, 2048 x 4 copies (address idx*16 + (lane&3)*4).
+// fill_row_tables() also writes the 16 bytes of static shared memory clb_prmt_k (the byte
+// tables of the fast-order prmt decode); kernels that launch with the most dynamic shared
+// memory subtract them from the opt-in limit.
 #pragma once
 #include <cuda_fp16.h>
 #include <stdint.h>

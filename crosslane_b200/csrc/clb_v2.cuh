@@ -479,17 +479,6 @@ __device__ __forceinline__ float lane_row_roll_any(const PackedMat& m, int row, 
     return lane_row_roll<CLB_IQ1_M, AS>(m, row, b0, b1, aq, ad);
 }
 
-// L2 prefetch of the first block of a row segment (no registers held).
-__device__ __forceinline__ void prefetch_row_block(const PackedMat& m, int row, int b) {
-    const int np = m.type == CLB_IQ1_M ? 3 : 4;
-    const size_t n = (size_t)m.n;
-    const uint8_t* p = m.body + ((size_t)b * np * n + (size_t)row) * 16;
-    prefetch_l2(p);
-    prefetch_l2(p + n * 16);
-    prefetch_l2(p + n * 32);
-    if (np == 4) prefetch_l2(p + n * 48);
-}
-
 // S in {1, 2, 3, 4, 6, 8} (kSegChoices); anything else is treated as 1.
 template <bool PF>
 __device__ __forceinline__ float seg_row_dot_any(const PackedMat& m, int row, int S, const int8_t* aq,
