@@ -32,6 +32,10 @@ Other workloads (own JSON line each, same keys):
               with Zipf(1.1) routing (clb_stack_batch; at N GPUs expert-ID sharded with an
               NCCL all-reduce of the expert rows per layer; roofline "hbm" over the distinct
               experts' bytes).
+  --phase-trace : config 3 through the phase-trace build of the library (build it with
+              `python crosslane_b200/build.py --trace`): per-phase durations of the stack
+              kernel per token-layer from %globaltimer stamps, medians over CTAs and layers
+              (one JSON line per rank; a measurement aid, not a throughput line).
 """
 import argparse
 import json
@@ -732,6 +736,94 @@ def run_skewed(args, rank, world, local):
         dist.destroy_process_group()
 
 
+PHASES = ["h", "norm", "gateup", "gateup_end", "qh_wait", "down", "combine_barrier"]
+
+
+def run_phase_trace(args, rank, world, local):
+    """Config 3 through the phase-trace build: `steps` tokens after `warmup`, and for each
+    phase boundary of the stack kernel the duration per token-layer (median over CTAs and
+    over layers 1..L-1; layer 0 also stages the tables), plus the slowest CTA's (mean over
+    layers) and, sharded, a split by the number of picks this GPU owned in the layer."""
+    import ctypes as C
+    lib_path = os.path.join(ROOT, "crosslane_b200", "libcrosslane_b200_trace.so")
+    if not os.path.exists(lib_path):
+        raise SystemExit("phase trace: build it first with `python crosslane_b200/build.py --trace`")
+    os.environ["CROSSLANE_B200_LIB"] = lib_path
+    import torch
+    import torch.distributed as dist
+
+    import crosslane_b200 as cb
+    from crosslane_b200._capi import lib
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    L = args.layers
+    if world > 1:
+        from crosslane_b200.sharded import ShardedBank
+        bank = ShardedBank(n_layers=L, n_experts=args.experts, dim=DIM, ff=FF, max_picks=PICKS, device=local,
+                           rank=rank, world=world, exact_order=args.exact_order)
+    else:
+        bank = cb.ExpertBank(n_layers=L, n_experts=args.experts, dim=DIM, ff=FF, max_picks=PICKS, device=local,
+                             exact_order=args.exact_order)
+    bank.fill_synthetic(SEED, args.policy)
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.ExternalStream(bank.stream)
+    rng = np.random.default_rng(1000)  # the same tokens on every rank
+    n_layers, n_ctas, n_slots = 64, 160, 8  # the kernel's trace array
+    lib.clb_stack_trace_read.restype = C.c_int
+    lib.clb_stack_trace_read.argtypes = [C.c_void_p, C.c_size_t]
+    grid = torch.cuda.get_device_properties(local).multi_processor_count
+    per, kowns, ms_all = [], [], []
+    for i in range(args.warmup + args.steps):
+        x = torch.from_numpy(rng.standard_normal(DIM).astype(np.float32)).cuda()
+        lg = rng.standard_normal((L, args.experts)).astype(np.float32)
+        d_lg = torch.from_numpy(lg).cuda()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        bank.stack_decode_device(0, L, x, d_lg)
+        ev1.record(stream)
+        ev1.synchronize()
+        if i < args.warmup:
+            continue
+        buf = np.zeros(n_layers * n_ctas * n_slots, np.uint64)
+        if lib.clb_stack_trace_read(buf.ctypes.data, buf.nbytes) != 0:
+            raise SystemExit("phase trace: clb_stack_trace_read failed")
+        t = buf.reshape(n_layers, n_ctas, n_slots)[:L, :grid].astype(np.int64)
+        per.append(np.diff(t, axis=2)[1:] / 1e3)  # [layer][cta][phase] us
+        kowns.append([sum(1 for e in cb.route_host(0, lg[l], PICKS)[0] if bank.expert_begin <= int(e) < bank.expert_end)
+                      for l in range(1, L)])
+        ms_all.append(ev0.elapsed_time(ev1))
+    d = np.concatenate(per)  # [tokens * (L - 1)][cta][phase]
+    k_all = np.concatenate(kowns)
+    phases = {name: {"median_us": round(float(np.median(d[:, :, j])), 2),
+                     "slowest_cta_us": round(float(np.mean(d[:, :, j].max(axis=1))), 2)}
+              for j, name in enumerate(PHASES) if name != "gateup_end"}
+    span = [float(np.median(p.sum(axis=2))) for p in per]  # per token: median CTA's layer time
+    line = {"metric": "stack kernel phase trace", "rank": rank, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "us_per_token_layer": round(float(np.mean(ms_all)) * 1e3 / L, 2),
+            "token_ms": round(float(np.mean(ms_all)), 4), "phases": phases,
+            "layer_span_median_us": round(float(np.mean(span)), 2),
+            "config": config3(args, world, world > 1), "library": "libcrosslane_b200_trace.so (-DCLB_FLOW_TRACE)"}
+    if world > 1:
+        by = {}
+        for kk in sorted(set(int(v) for v in k_all)):
+            idx = k_all == kk
+            by[str(kk)] = {"layers": int(idx.sum()), **{name: round(float(np.median(d[idx][:, :, j])), 2)
+                                                       for j, name in enumerate(PHASES) if name != "gateup_end"}}
+        line["by_owned_picks"] = by
+    print(json.dumps(line), flush=True)
+    bank.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -753,6 +845,8 @@ def main():
                     help="BASELINE config 5: batch-64 decode through the stack with Zipf(1.1) routing")
     ap.add_argument("--prefill", action="store_true",
                     help="BASELINE config 4 instead: 2048 tokens through one IQ2_XXS layer per step (own JSON line)")
+    ap.add_argument("--phase-trace", action="store_true",
+                    help="per-phase durations of the stack kernel (the -DCLB_FLOW_TRACE build of the library)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -768,6 +862,10 @@ def main():
         if args.steps == 200:
             args.steps = 10
         return run_skewed(args, rank, world, local)
+    if args.phase_trace:
+        if args.steps == 200:
+            args.steps = 4
+        return run_phase_trace(args, rank, world, local)
 
     if args.impl == "reference":
         return run_reference(args, rank, world)

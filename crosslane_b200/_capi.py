@@ -7,7 +7,9 @@ import ctypes as C
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libcrosslane_b200.so")
+# CROSSLANE_B200_LIB selects another build of the library (e.g. the phase-trace build);
+# the default is the in-tree libcrosslane_b200.so.
+LIB_PATH = os.environ.get("CROSSLANE_B200_LIB") or os.path.join(_HERE, "libcrosslane_b200.so")
 
 CLB_OK = 0
 CLB_E_INVALID = 1

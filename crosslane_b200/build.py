@@ -2,6 +2,7 @@
 
     python crosslane_b200/build.py          # incremental
     python crosslane_b200/build.py --force  # rebuild everything
+    python crosslane_b200/build.py --trace  # the phase-trace build, libcrosslane_b200_trace.so
 
 (Run as a file, not `-m`: importing the package loads the library being rebuilt.)
 
@@ -18,6 +19,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libcrosslane_b200.so")
+# The phase-trace build (-DCLB_FLOW_TRACE: %globaltimer stamps at the stack kernel's phase
+# boundaries, read back with clb_stack_trace_read); load it with CROSSLANE_B200_LIB.
+BUILD_TRACE = os.path.join(HERE, "_build_trace")
+LIB_TRACE = os.path.join(HERE, "libcrosslane_b200_trace.so")
 SOURCES = ["clb_kernels.cu", "clb_bank.cu", "clb_noalloc.cu", "clb_stack.cu", "clb_prefill.cu",
            "clb_pack_io.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -32,40 +37,42 @@ def _deps():
     return max(os.path.getmtime(h) for h in headers)
 
 
-def _compile(src, force):
-    obj = os.path.join(BUILD, src.replace(".cu", ".o"))
+def _compile(src, force, build_dir=BUILD, extra=()):
+    obj = os.path.join(build_dir, src.replace(".cu", ".o"))
     path = os.path.join(CSRC, src)
     if not force and os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(path), _deps()):
         return obj, False
-    cmd = [NVCC] + FLAGS + ["-c", path, "-o", obj]
+    cmd = [NVCC] + FLAGS + list(extra) + ["-c", path, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
     return obj, True
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    os.makedirs(BUILD, exist_ok=True)
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> str:
+    build_dir, lib, extra = (BUILD_TRACE, LIB_TRACE, ["-DCLB_FLOW_TRACE"]) if trace else (BUILD, LIB, [])
+    os.makedirs(build_dir, exist_ok=True)
     with cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
-        results = list(ex.map(lambda s: _compile(s, force), SOURCES))
+        results = list(ex.map(lambda s: _compile(s, force, build_dir, extra), SOURCES))
     objs = [o for o, _ in results]
     rebuilt = any(r for _, r in results)
-    if rebuilt or force or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lpthread"]
+    if rebuilt or force or not os.path.exists(lib) or os.path.getmtime(lib) < max(os.path.getmtime(o) for o in objs):
+        cmd = [NVCC] + ARCH + ["-shared", "-o", lib] + objs + ["-lpthread"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
         if verbose:
-            print("built", LIB)
-    return LIB
+            print("built", lib)
+    return lib
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="the phase-trace build (libcrosslane_b200_trace.so)")
     a = ap.parse_args()
     try:
-        build(a.force, verbose=True)
+        build(a.force, verbose=True, trace=a.trace)
     except RuntimeError as e:
         print(e, file=sys.stderr)
         sys.exit(1)

@@ -37,9 +37,12 @@
 namespace clb {
 
 #ifdef CLB_FLOW_TRACE
-// Phase stamps of the lockstep kernel per (layer, CTA), a build-time option (%globaltimer
-// ns): 0 layer start, 1 combine done, 2 norm done, 3 gate/up rounds done, 4 first barrier
-// passed, 5 Q8_K(h) staged, 6 down rounds done, 7 second barrier passed.
+// Phase stamps of the stack kernel per (layer, CTA), a build-time option (%globaltimer ns;
+// python crosslane_b200/build.py --trace). Fast order: 0 layer start, 1 h and its sums of
+// squares loaded, 2 RMSNorm + Q8_K(x) done, 3 = 4 gate/up rounds done, 5 Q8_K(h) staged,
+// 6 down rounds done (sharded: and the CTA's signal), 7 combine + grid barrier passed.
+// Exact order: 1 combine done, 2 norm done, 3 gate/up done, 4 first barrier passed, 5
+// Q8_K(h) staged, 6 down rows done, 7 second barrier passed.
 constexpr int kStTraceLayers = 64, kStTraceCtas = 160, kStTraceSlots = 8;
 __device__ unsigned long long g_stack_trace[kStTraceLayers * kStTraceCtas * kStTraceSlots];
 __device__ __forceinline__ void stack_stamp(int li, int slot) {
