@@ -223,6 +223,14 @@ struct StackSmem {
 
 __device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
+// v[0..7] = p[0..7] from shared memory (p 16-byte aligned) as two 16-byte loads: a warp's
+// lanes at a stride of 8 floats then hit at most 2-way bank conflicts, where 8 scalar
+// loads would each be 8-way.
+__device__ __forceinline__ void load8(const float* p, float v[8]) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+
 // Sum of (double)h[i]^2 over i = lane, lane + 1024, ... in order (one of 1024 lanes).
 __device__ __forceinline__ double lane_sumsq(const float* hs, int dim, int lane) {
     double s = 0.0;
@@ -413,8 +421,9 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)dim), 1e-6f)));
             for (int b = warp; b < nbx; b += NW) {
                 float v[8];
+                load8(hs + b * 256 + lane * 8, v);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(hs[b * 256 + lane * 8 + i], sc);
+                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(v[i], sc);
                 warp_quant_regs(v, xq + (size_t)b * kActStride, xd + b);
             }
         } else {
@@ -437,8 +446,9 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             const float sc = (float)__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(mean, 1e-6)));
             for (int b = warp; b < nbx; b += NW) {
                 float v[8];
+                load8(hs + b * 256 + lane * 8, v);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(hs[b * 256 + lane * 8 + i], sc);
+                for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(v[i], sc);
                 warp_quant_regs(v, xq + (size_t)b * kActStride, xd + b);
             }
         }
@@ -648,8 +658,7 @@ __global__ void __launch_bounds__(NT, 1) k_stack(const StackParams P) {
             __syncthreads();
             for (int hb = warp; hb < nbh; hb += NW) {
                 float v[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = hf[hb * 256 + lane * 8 + i];
+                load8(hf + hb * 256 + lane * 8, v);
                 warp_quant_regs(v, hq + (size_t)hb * kActStride, hd + hb);
             }
             __syncthreads();
